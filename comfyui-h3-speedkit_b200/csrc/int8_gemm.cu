@@ -1,0 +1,692 @@
+// INT8 GEMM for B200 (sm_100a): D = epilogue(A[M,K] . B[N,K]^T) with int32
+// accumulation in tensor memory.
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: 128x128-byte A tiles and 256x128-byte B tiles,
+//               128-byte swizzle, into a 4-stage shared-memory ring guarded by
+//               full/empty mbarriers.  No multicast.
+//   warp 1      allocates 512 TMEM columns (two 128x256 int32 accumulators) and
+//               issues tcgen05.mma.kind::i8 (M=128, N=256, K=32; four per
+//               stage) from one thread; tcgen05.commit frees each smem stage and
+//               publishes each finished accumulator.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, dequantise, apply the
+//               fused epilogue (bias, GELU, gate-residual, raw int32) and store.
+//               The second accumulator lets the epilogue of tile t overlap the
+//               mainloop of tile t+1.
+// Tiles are visited in grouped raster order (16 M-tiles per group) so that a
+// wave of CTAs shares B tiles in L2.  Every mbarrier wait is bounded; a wait that
+// runs out stops the CTA cleanly and records a status code (see
+// h3sk_pipeline_status).
+//
+// Epilogue arithmetic (non-fast-math TU, explicit round-to-nearest intrinsics):
+//   y   = bf(__fadd_rn(__fmul_rn(__fmul_rn(float(acc), xs[m]), ws[n]), bias[n]))
+//         kernels/gemm/fc1.cu:83-90 (EVT multiplies, plus 0) and the explicit form
+//         of kernels/gemm/r84_kfourwarp.cu:240-241;
+//   gate: out = bf(__fmaf_rn(y, gate[rows[m]][n], residual[m][n]))
+//         kernels/gemm/gate.cu:172-180, 239-242 and indexed_gate.cuh:85-87;
+//   GELU: out = bf(gelu_tanh(y)), the formula of convrot64_exact.cuh:913-923.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "sm100.cuh"
+#include "../../include/h3sk_b200.h"
+
+namespace h3sk {
+
+cudaError_t convrot_quant_none(const void* x, int64_t xs, void* q, void* scale, int64_t rows, int k,
+                               cudaStream_t stream);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;            // tile rows (TMEM lanes)
+constexpr int kBN = 256;            // tile columns (TMEM columns per accumulator)
+constexpr int kBK = 128;            // K bytes per stage (one 128-byte swizzle row)
+constexpr int kStages = 4;
+constexpr int kUmmaK = 32;          // K of one kind::i8 MMA
+constexpr int kATileBytes = kBM * kBK;
+constexpr int kBTileBytes = kBN * kBK;
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kThreads = 192;
+constexpr int kEpilogueThreads = 128;
+constexpr int kTmemCols = 512;
+constexpr int kGroupM = 16;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
+constexpr uint32_t kIdesc = idesc_i8(kBM, kBN);
+
+enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
+
+struct SmemLayout {
+  // offsets from the 1024-aligned base
+  static constexpr int a = 0;
+  static constexpr int b = kStages * kATileBytes;
+  static constexpr int bars = b + kStages * kBTileBytes;        // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int nbars = 2 * kStages + 5;
+  static constexpr int misc = bars + nbars * 8;                  // tmem slot, abort flag
+  static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float
+  static constexpr int total = colv + 2 * kBN * 4;
+  static constexpr int dynamic_bytes = total + 1024;             // slack for 1024 alignment
+};
+
+struct GemmParams {
+  const float* xs;
+  const float* ws;
+  const __nv_bfloat16* bias;      // may be null
+  void* d;                        // BF16 (or int32 for kEpiAcc)
+  int64_t ldd;
+  const __nv_bfloat16* gate;      // [G, gate_ld]
+  const int32_t* rows;            // [M]
+  const __nv_bfloat16* residual;  // [M, ldr]
+  int64_t gate_ld;
+  int64_t ldr;
+  int m, n, k;
+  int m_tiles, n_tiles, k_blocks, tiles;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+__device__ int g_pipeline_status = 0;
+
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int per_group = kGroupM * n_tiles;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, m_tiles - first_m);
+  const int local = tile - group * per_group;
+  mt = first_m + local % gm;
+  nt = local / gm;
+}
+
+__device__ __forceinline__ float gelu_tanh_precise(float v) {
+  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+// Named barrier among the four epilogue warps only.
+__device__ __forceinline__ void epilogue_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+}
+
+// Epilogue of 32 consecutive accumulators of one row: columns [col0, col0+32),
+// tile-local chunk c.  Columns are stored in groups of 8 (N % 8 == 0).
+template <int kEpi>
+__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row, int col0, int c,
+                                            float xs_row, const __nv_bfloat16* gate_row, const float* col_ws,
+                                            const float* col_bias) {
+  if constexpr (kEpi == kEpiAcc) {
+    int32_t* out = reinterpret_cast<int32_t*>(p.d) + int64_t(row) * p.ldd + col0;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      if (col0 + 4 * v < p.n)
+        reinterpret_cast<int4*>(out)[v] =
+            make_int4(int(r[4 * v]), int(r[4 * v + 1]), int(r[4 * v + 2]), int(r[4 * v + 3]));
+  } else {
+    uint32_t packed[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float y2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int cc = c * 32 + i + h;
+        const float a = __int2float_rn(int(r[i + h]));
+        const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, xs_row), col_ws[cc]), col_bias[cc]);
+        y2[h] = __bfloat162float(__float2bfloat16_rn(y));
+        if constexpr (kEpi == kEpiGelu) y2[h] = gelu_tanh_precise(y2[h]);
+      }
+      packed[i / 2] = pack_bf2(y2[0], y2[1]);
+    }
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.d) + int64_t(row) * p.ldd + col0;
+    if constexpr (kEpi == kEpiGate) {
+      // D may alias the residual: each element is read before it is written, by this thread.
+      const __nv_bfloat16* res = p.residual + int64_t(row) * p.ldr + col0;
+      const __nv_bfloat16* gat = gate_row + col0;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        if (col0 + 8 * v >= p.n) break;
+        const uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * v);
+        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gat + 8 * v));
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t yw = packed[4 * v + w];
+          const float lo = __fmaf_rn(bf_lo(yw), bf_lo(gw[w]), bf_lo(rw[w]));
+          const float hi = __fmaf_rn(bf_hi(yw), bf_hi(gw[w]), bf_hi(rw[w]));
+          o[w] = pack_bf2(lo, hi);
+        }
+        reinterpret_cast<uint4*>(out)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        if (col0 + 8 * v < p.n)
+          reinterpret_cast<uint4*>(out)[v] =
+              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+    }
+  }
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem + SmemLayout::a;
+  uint8_t* smem_b = smem + SmemLayout::b;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + SmemLayout::misc + 4);
+  volatile int* ready = reinterpret_cast<volatile int*>(smem + SmemLayout::misc + 8);
+  float* col_ws = reinterpret_cast<float*>(smem + SmemLayout::colv);
+  float* col_bias = col_ws + kBN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* status = p.status;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpilogueThreads);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_mbar_init();
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Control flow is warp-uniform in every role: lane 0 waits and issues, and
+  // __shfl_sync hands its verdict to the other lanes, so every .sync.aligned
+  // tcgen05 instruction and every barrier below is reached by converged warps.
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    uint64_t policy_a = 0, policy_b = 0;
+    if (lane == 0) {
+      policy_a = l2_policy_evict_normal();
+      policy_b = l2_policy_evict_last();
+    }
+    uint32_t issued_mask = 0, issued_phase_bits = 0;   // per stage: issued at least once / parity of last issue
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+      int mt, nt;
+      tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        int got = 0;
+        if (lane == 0) {
+          got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, status, 11, p.timeout_ns) ? 1 : 0;
+          if (got) {
+            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], kb * kBK, mt * kBM, policy_a);
+            tma_load_2d(smem_b + stage * kBTileBytes, &map_b, &full[stage], kb * kBK, nt * kBN, policy_b);
+          }
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        issued_mask |= 1u << stage;
+        issued_phase_bits = (issued_phase_bits & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // Drain: every copy this warp issued lands before the CTA exits.
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait_bounded(&full[s], (issued_phase_bits >> s) & 1u, nullptr, status, 12, p.timeout_ns);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0, acc = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+      int got = 0;
+      if (lane == 0) {
+        got = mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort, status, 21, p.timeout_ns) ? 1 : 0;
+        if (got) tc_fence_after();
+      }
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
+      const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        got = 0;
+        if (lane == 0) {
+          got = mbar_wait_bounded(&full[stage], phase, abort, status, 22, p.timeout_ns) ? 1 : 0;
+          if (got) {
+            tc_fence_after();
+            const uint64_t a_desc = smem_desc_k_sw128(smem_a + stage * kATileBytes);
+            const uint64_t b_desc = smem_desc_k_sw128(smem_b + stage * kBTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+              // +32 bytes along K inside the swizzle atom = +2 in the 16-byte address field
+              mma_i8(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), kIdesc,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&empty[stage]);
+          }
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) mma_commit(&tfull[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    // Drain: every MMA issued by this warp completes before TMEM is released.
+    if (lane == 0) {
+      mma_commit(drain);
+      mbar_wait_bounded(drain, 0, nullptr, status, 23, p.timeout_ns);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int ep_tid = threadIdx.x - 64;     // 0..127
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+      int mt, nt;
+      tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      const int n0 = nt * kBN;
+      // Stage this tile's per-column scales (and bias) in shared memory.
+      epilogue_sync();   // the previous tile's readers are done
+      if (kEpi != kEpiAcc) {
+        for (int c = ep_tid; c < kBN; c += kEpilogueThreads) {
+          const int n = n0 + c;
+          col_ws[c] = n < p.n ? p.ws[n] : 0.0f;
+          col_bias[c] = (p.bias != nullptr && n < p.n) ? __bfloat162float(p.bias[n]) : 0.0f;
+        }
+      }
+      // One thread waits for the accumulator; the named barrier hands the
+      // outcome to the other 127 so all of them leave or continue together.
+      if (ep_tid == 0) *ready = mbar_wait_bounded(&tfull[acc], acc_phase, abort, status, 31, p.timeout_ns) ? 1 : 0;
+      epilogue_sync();
+      if (*ready == 0) break;
+      tc_fence_after();
+      const int row = mt * kBM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      const float xs_row = (kEpi != kEpiAcc && row_ok) ? p.xs[row] : 0.0f;
+      const __nv_bfloat16* gate_row = nullptr;
+      if (kEpi == kEpiGate && row_ok) gate_row = p.gate + int64_t(p.rows[row]) * p.gate_ld;
+      const uint32_t t_row = tmem_base + uint32_t(acc * kBN) + (uint32_t(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_load_32cols(t_row + uint32_t(c * 32), r);
+        tmem_load_wait();
+        if (c == kBN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.n) store_chunk<kEpi>(p, r, row, col0, c, xs_row, gate_row, col_ws, col_bias);
+      }
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---- bounded-wait self-test and MMA issue-rate probe --------------------------
+
+__global__ void wait_selftest_kernel(int* status, uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on `bar`: the wait must run out and report.
+    mbar_wait_bounded(&bar, 0, reinterpret_cast<volatile int*>(&abort_flag), status, H3SK_STATUS_WAIT_TIMEOUT,
+                      timeout_ns);
+  }
+}
+
+__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t done;
+  __shared__ uint32_t slot;
+  for (int i = threadIdx.x; i < kStageBytes / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+  if (threadIdx.x == 0) {
+    mbar_init(&done, 1);
+    fence_mbar_init();
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  const int warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    tmem_alloc(&slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = slot;
+  if (warp == 0) {
+    if (threadIdx.x == 0) {
+      const uint64_t a_desc = smem_desc_k_sw128(smem);
+      const uint64_t b_desc = smem_desc_k_sw128(smem + kATileBytes);
+      for (int i = 0; i < iters; ++i) {
+        const int kk = i & 3;
+        mma_i8(tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), kIdesc, i > 0 ? 1u : 0u);
+      }
+      mma_commit(&done);
+      mbar_wait_bounded(&done, 0, nullptr, status, 41, kWaitTimeoutNs);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---- host side -------------------------------------------------------------------
+
+thread_local int t_last_error = 0;
+thread_local char t_last_message[256] = "ok";
+
+int fail(int code, const char* what) {
+  t_last_error = code;
+  std::snprintf(t_last_message, sizeof(t_last_message), "%s (%s)", what,
+                cudaGetErrorString(static_cast<cudaError_t>(code)));
+  return 0;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// K-major INT8 operand [rows, k] with row stride k bytes, box of box_rows x 128 bytes.
+bool make_operand_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(k)};
+  const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                        elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool attrs_set[4] = {false, false, false, false};
+};
+
+DeviceInfo& device_info(int device) {
+  static std::mutex mu;
+  static DeviceInfo infos[64];
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceInfo& d = infos[device & 63];
+  if (d.sms == 0) cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
+  return d;
+}
+
+int* status_ptr() {
+  int* ptr = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_pipeline_status) != cudaSuccess) return nullptr;
+  return ptr;
+}
+
+template <int kEpi>
+cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cudaStream_t stream) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  DeviceInfo& info = device_info(device);
+  auto kernel = int8_gemm_persistent<kEpi>;
+  if (!info.attrs_set[kEpi]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::dynamic_bytes);
+    if (e != cudaSuccess) return e;
+    info.attrs_set[kEpi] = true;
+  }
+  p.status = status_ptr();
+  if (!p.status) return cudaErrorInvalidSymbol;
+  const int grid = p.tiles < info.sms ? p.tiles : info.sms;
+  kernel<<<grid, kThreads, SmemLayout::dynamic_bytes, stream>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
+             void* D, int64_t ldd, const void* gate, const int32_t* rows, const void* residual, int M, int N,
+             int K, cudaStream_t stream) {
+  if (!A || !B || !D || M < 1 || N < 1 || K < 16 || K % 16 || N % 8 || ldd < N || ldd % 8)
+    return fail(cudaErrorInvalidValue, "h3_int8: invalid shape or null operand");
+  if ((uintptr_t(A) & 15u) || (uintptr_t(B) & 15u) || (uintptr_t(D) & 15u))
+    return fail(cudaErrorInvalidValue, "h3_int8: A, B and D must be 16-byte aligned");
+  if (epi != kEpiAcc && (!xs || !ws || (uintptr_t(xs) & 3u) || (uintptr_t(ws) & 3u)))
+    return fail(cudaErrorInvalidValue, "h3_int8: scales must be non-null FP32");
+  if (bias && (uintptr_t(bias) & 1u)) return fail(cudaErrorInvalidValue, "h3_int8: misaligned bias");
+  if (epi == kEpiGate) {
+    if (!gate || !rows || !residual || (uintptr_t(gate) & 15u) || (uintptr_t(residual) & 15u) ||
+        (uintptr_t(rows) & 3u))
+      return fail(cudaErrorInvalidValue, "h3_int8_gate: gate/rows/residual null or misaligned");
+  }
+  CUtensorMap ma, mb;
+  if (!make_operand_map(&ma, A, M, K, kBM) || !make_operand_map(&mb, B, N, K, kBN))
+    return fail(cudaErrorInvalidValue, "h3_int8: tensor map encoding failed");
+  GemmParams p{};
+  p.xs = xs;
+  p.ws = ws;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.d = D;
+  p.ldd = ldd;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.rows = rows;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.gate_ld = N;
+  p.ldr = N;
+  p.m = M;
+  p.n = N;
+  p.k = K;
+  p.m_tiles = (M + kBM - 1) / kBM;
+  p.n_tiles = (N + kBN - 1) / kBN;
+  p.k_blocks = (K + kBK - 1) / kBK;
+  p.tiles = p.m_tiles * p.n_tiles;
+  p.timeout_ns = kWaitTimeoutNs;
+  cudaError_t e;
+  switch (epi) {
+    case kEpiDequant: e = launch_gemm<kEpiDequant>(ma, mb, p, stream); break;
+    case kEpiGelu: e = launch_gemm<kEpiGelu>(ma, mb, p, stream); break;
+    case kEpiGate: e = launch_gemm<kEpiGate>(ma, mb, p, stream); break;
+    default: e = launch_gemm<kEpiAcc>(ma, mb, p, stream); break;
+  }
+  if (e != cudaSuccess) return fail(e, "h3_int8: launch failed");
+  t_last_error = 0;
+  std::snprintf(t_last_message, sizeof(t_last_message), "ok");
+  return 1;
+}
+
+}  // namespace
+}  // namespace h3sk
+
+#define H3SK_EXPORT extern "C" __attribute__((visibility("default")))
+
+H3SK_EXPORT int h3_int8(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M,
+                        int N, int K, int config, uintptr_t stream) {
+  if (config < 0 || config > 15) return h3sk::fail(cudaErrorInvalidValue, "h3_int8: config out of range");
+  return h3sk::run_gemm(h3sk::kEpiDequant, A, B, xs, ws, nullptr, D, N, nullptr, nullptr, nullptr, M, N, K,
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+H3SK_EXPORT int h3_int8_gate(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                             const void* gate, const int32_t* rows, const void* residual, int M, int N, int K,
+                             int config, uintptr_t stream) {
+  if (config < 0 || config > 15) return h3sk::fail(cudaErrorInvalidValue, "h3_int8_gate: config out of range");
+  return h3sk::run_gemm(h3sk::kEpiGate, A, B, xs, ws, nullptr, D, N, gate, rows, residual, M, N, K,
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+H3SK_EXPORT int h3_int8_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
+                           void* D, int M, int N, int K, int64_t ldd, int epilogue, uintptr_t stream) {
+  if (epilogue != H3_EPI_DEQUANT && epilogue != H3_EPI_DEQUANT_GELU && epilogue != H3_EPI_ACC_INT32)
+    return h3sk::fail(cudaErrorInvalidValue, "h3_int8_ex: unknown epilogue");
+  if (epilogue == H3_EPI_ACC_INT32 && (ldd % 4)) return h3sk::fail(cudaErrorInvalidValue, "h3_int8_ex: ldd");
+  return h3sk::run_gemm(epilogue, A, B, xs, ws, bias, D, ldd, nullptr, nullptr, nullptr, M, N, K,
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+H3SK_EXPORT int h3_int8_gate_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws,
+                                const void* bias, void* D, const void* gate, const int32_t* rows,
+                                const void* residual, void* q, void* qscale, int M, int N, int K,
+                                uintptr_t stream) {
+  if ((q == nullptr) != (qscale == nullptr))
+    return h3sk::fail(cudaErrorInvalidValue, "h3_int8_gate_ex: q and qscale go together");
+  if (q && (N % 256 || N > 16384 || (uintptr_t(q) & 7u) || (uintptr_t(qscale) & 3u)))
+    return h3sk::fail(cudaErrorInvalidValue, "h3_int8_gate_ex: requant needs N % 256 == 0, N <= 16384");
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!h3sk::run_gemm(h3sk::kEpiGate, A, B, xs, ws, bias, D, N, gate, rows, residual, M, N, K, s)) return 0;
+  if (q) {
+    const cudaError_t e = h3sk::convrot_quant_none(D, N, q, qscale, M, N, s);
+    if (e != cudaSuccess) return h3sk::fail(e, "h3_int8_gate_ex: requant launch failed");
+  }
+  return 1;
+}
+
+H3SK_EXPORT int h3_int8_last_error(void) { return h3sk::t_last_error; }
+H3SK_EXPORT const char* h3_int8_error(void) { return h3sk::t_last_message; }
+
+H3SK_EXPORT int h3sk_pipeline_status(int* status, int clear, uintptr_t stream) {
+  if (!status) return cudaErrorInvalidValue;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int value = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&value, h3sk::g_pipeline_status, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return e;
+  *status = value;
+  if (clear && value) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(h3sk::g_pipeline_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  return e;
+}
+
+H3SK_EXPORT int h3sk_wait_selftest(int timeout_us, int* status, uintptr_t stream) {
+  if (!status || timeout_us < 1 || timeout_us > 1000000) return cudaErrorInvalidValue;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* dev = h3sk::status_ptr();
+  if (!dev) return cudaErrorInvalidSymbol;
+  cudaError_t e = cudaMemsetAsync(dev, 0, sizeof(int), s);
+  if (e != cudaSuccess) return e;
+  h3sk::wait_selftest_kernel<<<1, 32, 0, s>>>(dev, uint64_t(timeout_us) * 1000ull);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return h3sk_pipeline_status(status, 1, stream);
+}
+
+H3SK_EXPORT int h3sk_int8_mma_peak(int iters, double* tops, uintptr_t stream) {
+  if (!tops || iters < 64 || iters > (1 << 24)) return cudaErrorInvalidValue;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int device = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  int* dev = h3sk::status_ptr();
+  if (!dev) return cudaErrorInvalidSymbol;
+  // 120 KB of dynamic shared memory keeps the probe at one CTA per SM (only the
+  // first 48 KB are read).
+  const int smem = 120 * 1024;
+  e = cudaFuncSetAttribute(h3sk::mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaEvent_t t0, t1;
+  cudaEventCreate(&t0);
+  cudaEventCreate(&t1);
+  h3sk::mma_peak_kernel<<<sms, 128, smem, s>>>(64, dev);   // warm-up
+  cudaEventRecord(t0, s);
+  h3sk::mma_peak_kernel<<<sms, 128, smem, s>>>(iters, dev);
+  cudaEventRecord(t1, s);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventSynchronize(t1);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t0, t1);
+  cudaEventDestroy(t0);
+  cudaEventDestroy(t1);
+  if (e != cudaSuccess) return e;
+  const double ops = 2.0 * h3sk::kBM * h3sk::kBN * h3sk::kUmmaK * double(iters) * double(sms);
+  *tops = ops / (double(ms) * 1e-3) / 1e12;
+  return cudaSuccess;
+}
+
+H3SK_EXPORT const char* h3sk_version(void) { return "h3sk_b200 0.1.0 (sm_100a)"; }

@@ -1,0 +1,224 @@
+"""The quantized DiT-block linear chain and its token-sharded block stack.
+
+One block (the linear path of ``Backend.block``, runtime.py:126-164 of H3
+SpeedKit, with attention replaced by an identity passthrough of V):
+
+    q, qs   = prologue(x; norm1, shift_msa, scale_msa)        fused RMSNorm/adaLN/ConvRot/INT8
+    qkv     = bf(dequant(q . Wqkv^T))                           INT8 GEMM, N = 3D
+    aq, as  = convrot_quant(qkv[:, 2D:3D])                      identity attention: V
+    x       = bf(fmaf(bf(dequant(aq . Wout^T)), gate_msa, x))   outproj gate-residual, in place
+    q, qs   = prologue(x; norm2, shift_mlp, scale_mlp)
+    h       = bf(gelu_tanh(bf(dequant(q . Wfc1^T))))            FC1 + GELU epilogue
+    hq, hs  = convrot_quant(h)                                  ACT none (GELU already applied)
+    x       = bf(fmaf(bf(dequant(hq . Wfc2^T)), gate_mlp, x))   FC2 gate-residual, in place
+
+Every op is row-local, so a contiguous token shard gives bit-identical rows on
+any number of GPUs.  ``ShardedStack`` splits the tokens across the ranks of a
+torch.distributed process group (weights replicated), runs the blocks with no
+collective, and gathers the final BF16 rows with one all_gather_into_tensor.
+
+``BlockPlan`` binds one block's launches to preallocated buffers once and then
+replays them through the C-ABI with fixed pointers, so a step is a short list of
+ctypes calls on the current stream (and can be captured in a CUDA graph).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .synthetic import BlockWeights
+
+ACT_NONE = 0
+EPI_DEQUANT, EPI_GELU = 0, 1
+LAUNCHES_PER_BLOCK = 8   # 2 prologues, 2 quantisers, 4 GEMMs
+GEMM_NAMES = ("qkv", "outproj", "fc1", "fc2")
+
+
+def shard_bounds(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous token block of `rank`: rows [start, stop).  Ranks get
+    ceil(total/world) rows except the tail, which may be shorter or empty."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("invalid rank/world")
+    per = -(-total // world)
+    start = min(total, rank * per)
+    return start, min(total, start + per)
+
+
+@dataclass
+class Workspace:
+    """Per-shard activation buffers, sized once for m rows."""
+    q: torch.Tensor
+    qs: torch.Tensor
+    qkv: torch.Tensor
+    aq: torch.Tensor
+    as_: torch.Tensor
+    h: torch.Tensor
+    hq: torch.Tensor
+    hs: torch.Tensor
+
+    @classmethod
+    def allocate(cls, m: int, d: int, ffn: int, device) -> "Workspace":
+        e = dict(device=device)
+        return cls(q=torch.empty((m, d), dtype=torch.int8, **e), qs=torch.empty((m, 1), dtype=torch.float32, **e),
+                   qkv=torch.empty((m, 3 * d), dtype=torch.bfloat16, **e),
+                   aq=torch.empty((m, d), dtype=torch.int8, **e), as_=torch.empty((m, 1), dtype=torch.float32, **e),
+                   h=torch.empty((m, ffn), dtype=torch.bfloat16, **e),
+                   hq=torch.empty((m, ffn), dtype=torch.int8, **e), hs=torch.empty((m, 1), dtype=torch.float32, **e))
+
+
+class BlockPlan:
+    """One block's eight launches, bound to fixed buffers.
+
+    ``x`` is updated in place.  ``rows`` maps each token to a row of the adaLN /
+    gate tables.  Nothing is allocated when the plan runs.
+    """
+
+    def __init__(self, weights: BlockWeights, x: torch.Tensor, rows: torch.Tensor, ws: Workspace,
+                 eps: float = 1e-6):
+        self.lib = _lib.load()
+        m, d = x.shape
+        ffn = weights.fc1.shape[0]
+        if weights.qkv.shape != (3 * d, d) or weights.fc2.shape != (d, ffn) or weights.out.shape != (d, d):
+            raise ValueError("block weights do not match the activation width")
+        if m < 1:
+            raise ValueError("empty shard")
+        self.keep = (weights, x, rows, ws)   # owners of every pointer below
+        lib, P = self.lib, lambda t: t.data_ptr()
+        w = weights
+        tdt = int(w.shift_msa.dtype == torch.bfloat16)
+        self.calls = [
+            ("prologue", lib.h3_norm_quant_run_k,
+             (P(x), P(w.norm1), P(w.shift_msa), P(w.scale_msa), P(rows), P(ws.q), P(ws.qs), None, None, None,
+              m, d, x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps), tdt, 0)),
+            ("qkv", lib.h3_int8_ex,
+             (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * d, d, 3 * d, EPI_DEQUANT)),
+            ("quant_v", lib.h3_convrot_quant_act,
+             (P(ws.qkv) + 2 * d * 2, 3 * d, P(ws.aq), P(ws.as_), m, d, ACT_NONE)),
+            ("outproj", lib.h3_int8_gate,
+             (P(ws.aq), P(w.out), P(ws.as_), P(w.out_s), P(x), P(w.gate_msa), P(rows), P(x), m, d, d, 13)),
+            ("prologue", lib.h3_norm_quant_run_k,
+             (P(x), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows), P(ws.q), P(ws.qs), None, None, None,
+              m, d, x.stride(0), w.shift_mlp.stride(0), w.scale_mlp.stride(0), float(eps), tdt, 0)),
+            ("fc1", lib.h3_int8_ex,
+             (P(ws.q), P(w.fc1), P(ws.qs), P(w.fc1_s), None, P(ws.h), m, ffn, d, ffn, EPI_GELU)),
+            ("quant_h", lib.h3_convrot_quant_act,
+             (P(ws.h), ffn, P(ws.hq), P(ws.hs), m, ffn, ACT_NONE)),
+            ("fc2", lib.h3_int8_gate,
+             (P(ws.hq), P(w.fc2), P(ws.hs), P(w.fc2_s), P(x), P(w.gate_mlp), P(rows), P(x), m, d, ffn, 13)),
+        ]
+
+    def launch(self, stream: int, events=None) -> None:
+        """Enqueue the eight launches on `stream`.  With `events` (a dict of
+        name -> list of (start, end) CUDA event pairs) each launch is bracketed."""
+        for name, fn, args in self.calls:
+            if events is not None:
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+            rc = fn(*args, stream)
+            if name in GEMM_NAMES:
+                _lib.check_int8(rc)          # GEMM entry points return 1 on success
+            elif rc != 0:                    # the others return a cudaError_t
+                raise RuntimeError(f"{name} launch failed with CUDA error {rc}")
+            if events is not None:
+                end.record()
+                events.setdefault(name, []).append((start, end))
+
+    @staticmethod
+    def gemm_ops(m: int, d: int, ffn: int) -> dict:
+        return {"qkv": 2 * m * 3 * d * d, "outproj": 2 * m * d * d, "fc1": 2 * m * ffn * d, "fc2": 2 * m * d * ffn}
+
+
+def block_ops_per_token(d: int = 4096, ffn: int = 16384) -> int:
+    """INT8 ops per token per block: 2*D*(3D + D + FFN) + 2*FFN*D."""
+    return 2 * d * (3 * d + d + ffn) + 2 * ffn * d
+
+
+class LocalStack:
+    """All blocks over one contiguous shard of tokens, on the current device."""
+
+    def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6):
+        m, d = x.shape
+        ffn = blocks[0].fc1.shape[0]
+        self.x, self.rows = x, rows
+        self.ws = Workspace.allocate(m, d, ffn, x.device)
+        self.plans = [BlockPlan(b, x, rows, self.ws, eps) for b in blocks]
+        self.graph = None
+
+    @property
+    def launches_per_step(self) -> int:
+        return LAUNCHES_PER_BLOCK * len(self.plans)
+
+    def run(self, events=None) -> torch.Tensor:
+        if self.graph is not None and events is None:
+            self.graph.replay()
+            return self.x
+        stream = torch.cuda.current_stream(self.x.device).cuda_stream
+        for plan in self.plans:
+            plan.launch(stream, events)
+        return self.x
+
+    def capture(self) -> None:
+        """Capture the whole stack as one CUDA graph (fixed buffers, no host work per step)."""
+        torch.cuda.synchronize(self.x.device)
+        stream = torch.cuda.Stream(self.x.device)
+        stream.wait_stream(torch.cuda.current_stream(self.x.device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                self.run()
+        torch.cuda.current_stream(self.x.device).wait_stream(stream)
+        self.graph = graph
+
+
+class ShardedStack:
+    """Token-sharded block stack: rank r owns rows shard_bounds(M, world, r),
+    weights are replicated, one all_gather_into_tensor assembles the output.
+
+    The shard lives in ``self.send`` (padded to ceil(M/world) rows); the blocks
+    update it in place and the same buffer feeds the all-gather, so no copy
+    sits between the last block and the collective.
+    """
+
+    def __init__(self, blocks, rows_shard: torch.Tensor, total_rows: int, d: int, device, group=None,
+                 eps: float = 1e-6, dtype=torch.bfloat16):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.start, self.stop = shard_bounds(total_rows, self.world, self.rank)
+        self.rows_local = self.stop - self.start
+        if rows_shard.shape[0] != self.rows_local:
+            raise ValueError(f"rank {self.rank} expects {self.rows_local} table rows, got {rows_shard.shape[0]}")
+        self.total = total_rows
+        self.per = -(-total_rows // self.world)
+        self.send = torch.zeros((self.per, d), dtype=dtype, device=device)
+        self.out = torch.empty((self.per * self.world, d), dtype=dtype, device=device)
+        self.x = self.send[: self.rows_local]
+        self.local = LocalStack(blocks, self.x, rows_shard, eps) if self.rows_local else None
+
+    @property
+    def launches_per_step(self) -> int:
+        return self.local.launches_per_step if self.local is not None else 0
+
+    def load(self, x_shard: torch.Tensor, non_blocking: bool = True) -> None:
+        """Copy this rank's input rows (device or pinned host) into the shard buffer."""
+        if x_shard.shape != self.x.shape:
+            raise ValueError(f"expected input shard {tuple(self.x.shape)}, got {tuple(x_shard.shape)}")
+        self.x.copy_(x_shard, non_blocking=non_blocking)
+
+    def forward_local(self, events=None) -> None:
+        if self.local is not None:
+            self.local.run(events)
+
+    def gather(self) -> torch.Tensor:
+        if self.world == 1:
+            return self.send[: self.total]
+        self.dist.all_gather_into_tensor(self.out, self.send, group=self.group)
+        return self.out[: self.total]
+
+    def forward(self, events=None) -> torch.Tensor:
+        self.forward_local(events)
+        return self.gather()

@@ -1,0 +1,205 @@
+/*
+ * h3sk_b200.h -- C-ABI of the B200 (sm_100a) quantized DiT-block linear path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle
+ * (cast to uintptr_t) and enqueues its work on that stream without a device
+ * synchronisation.  No entry point allocates device memory: the caller owns
+ * every input and output buffer.  All pointers are device pointers.
+ *
+ * Two return conventions are kept from the interface each symbol replaces:
+ *   - h3_norm_quant_* and h3_convrot_* return a cudaError_t value (0 = success);
+ *   - h3_int8* return 1 on success and 0 on failure (the reason is available
+ *     through h3_int8_last_error / h3_int8_error).
+ * Validation runs on the host before anything is enqueued; a failed check
+ * launches nothing.
+ *
+ * Reference interfaces are cited as path:line inside the H3 SpeedKit sources.
+ */
+#ifndef H3SK_B200_H
+#define H3SK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Fused prologue: RMSNorm -> adaLN x*(1+scale)+shift -> ConvRot256 -> INT8  */
+/* ------------------------------------------------------------------------ */
+
+/* Resource report; field order of kernels/norm_quant/norm_quant.cu:215-218. */
+typedef struct H3NormQuantResources {
+  int64_t abi, bytes, k, threads, warps, num_regs, static_shared_bytes, local_bytes;
+  int64_t active_blocks_per_sm, sm_count, max_threads_per_sm, binary_version, ptx_version;
+} H3NormQuantResources;
+
+/* Replaces h3_norm_quant_abi (norm_quant.cu:234). Returns 1: the K=5376 ABI. */
+int h3_norm_quant_abi(void);
+/* Returns 2 when the K-generic extensions (*_k) below are present. */
+int h3_norm_quant_abi_ex(void);
+/* Replaces h3_norm_quant_resources_size (norm_quant.cu:235). */
+size_t h3_norm_quant_resources_size(void);
+/* Replaces h3_norm_quant_error (norm_quant.cu:236): cudaGetErrorString. */
+const char* h3_norm_quant_error(int code);
+/* Replaces h3_norm_quant_query (norm_quant.cu:237-241) for K=5376. */
+int h3_norm_quant_query(int table_dtype, int debug, H3NormQuantResources* out, size_t bytes);
+/* K-generic query (no reference counterpart; K % 256 == 0, 256 <= K <= 16384). */
+int h3_norm_quant_query_k(int64_t k, int table_dtype, int debug, H3NormQuantResources* out,
+                          size_t bytes);
+/*
+ * Replaces h3_norm_quant_run (norm_quant.cu:242-266), K fixed at 5376.
+ *   x      BF16 [m, K], row stride xs elements (xs >= K, xs % 4 == 0, 8-byte aligned)
+ *   w      BF16 [K] RMSNorm weight
+ *   shift  table [T, K] (row stride ss), scale table [T, K] (row stride cs);
+ *          table_dtype 0 = FP32, 1 = BF16
+ *   rows   int32 [m] table row per token
+ *   q      INT8 [m, K] dense, qscale FP32 [m]
+ *   debug  1 => also write debug_norm BF16 [m, K], debug_rotated FP32 [m, K],
+ *          debug_rstd FP32 [m]; 0 => those must be NULL
+ *   eps    finite, >= FLT_MIN
+ */
+int h3_norm_quant_run(const void* x, const void* w, const void* shift, const void* scale,
+                      const void* rows, void* q, void* qscale, void* debug_norm,
+                      void* debug_rotated, void* debug_rstd, int64_t m, int64_t xs, int64_t ss,
+                      int64_t cs, float eps, int table_dtype, int debug, uintptr_t stream);
+/* Same contract with K explicit (K % 256 == 0, 256 <= K <= 16384). The
+ * reference fixes K at compile time (norm_quant.cu:16); this is its K-generic form. */
+int h3_norm_quant_run_k(const void* x, const void* w, const void* shift, const void* scale,
+                        const void* rows, void* q, void* qscale, void* debug_norm,
+                        void* debug_rotated, void* debug_rstd, int64_t m, int64_t k, int64_t xs,
+                        int64_t ss, int64_t cs, float eps, int table_dtype, int debug,
+                        uintptr_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* ConvRot256 + per-token INT8 quantiser                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Field order of kernels/convrot/convrot_register_v2.cu:140-144. */
+typedef struct H3ConvRotResources {
+  int64_t abi, bytes, k, threads, warps, num_regs, static_shared_bytes;
+  int64_t local_bytes, max_threads_per_block, active_blocks_per_sm;
+  int64_t sm_count, max_threads_per_sm, binary_version, ptx_version;
+} H3ConvRotResources;
+
+/* Replaces h3_convrot_register_abi (convrot_register_v2.cu:189). Returns 1. */
+int h3_convrot_register_abi(void);
+/* Replaces h3_convrot_register_resources_size (convrot_register_v2.cu:190). */
+size_t h3_convrot_register_resources_size(void);
+/* Replaces h3_convrot_register_error (convrot_register_v2.cu:191-193). */
+const char* h3_convrot_register_error(int code);
+/* Replaces h3_convrot_register_query (convrot_register_v2.cu:194-199); any K % 256 == 0. */
+int h3_convrot_register_query(int k, H3ConvRotResources* out, size_t bytes);
+/*
+ * Replaces h3_convrot_register_run (convrot_register_v2.cu:200-209).
+ *   x BF16 [rows, k] dense (16-byte aligned); q INT8 [rows, k] (8-byte aligned);
+ *   scale FP32 [rows]; rotated FP32 [rows, k].
+ *   mode 0 = production (q, scale), 1 = diagnostic (q, scale and rotated),
+ *   2 = rotation only (rotated; q and scale unused).
+ *   Any k % 256 == 0 with 256 <= k <= 16384 is accepted (reference: 5376, 7168).
+ */
+int h3_convrot_register_run(const void* x, void* q, void* scale, void* rotated, int64_t rows,
+                            int k, int mode, uintptr_t stream);
+/*
+ * Replaces Kitchen's quantize_int8_rowwise_convrot64(x, 256, input_act=...) as
+ * called at h3_speedkit/runtime.py:159; arithmetic of
+ * kernels/convrot/vendor/convrot64_exact.cuh:913-1027.
+ *   act 0 = none, 1 = GELU-tanh, 2 = SwiGLU (x row is [gate | up], 2k wide)
+ *   x BF16 with row stride xs elements (xs >= k, or >= 2k for SwiGLU;
+ *     x and xs*2 bytes 16-byte aligned); q INT8 [rows, k] dense; scale FP32 [rows].
+ */
+int h3_convrot_quant_act(const void* x, int64_t xs, void* q, void* scale, int64_t rows, int k,
+                         int act, uintptr_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* INT8 GEMM (tcgen05 kind::i8, int32 accumulators in TMEM) + fused epilogues */
+/* ------------------------------------------------------------------------ */
+
+/* Epilogue selectors of h3_int8_ex. */
+enum {
+  H3_EPI_DEQUANT = 0,      /* D = bf(((acc*xs)*ws)+bias) */
+  H3_EPI_DEQUANT_GELU = 1, /* D = bf(gelu_tanh(bf(((acc*xs)*ws)+bias))) */
+  H3_EPI_ACC_INT32 = 3     /* D = acc as int32 (debug: bit-exact accumulators) */
+};
+
+/*
+ * Replaces h3_int8 (kernels/gemm/fc1.cu:119-138):
+ *   D[m, n] = bf16( ((float(sum_k A[m,k]*B[n,k]) * xs[m]) * ws[n]) + 0 )
+ *   A INT8 [M, K] row-major, B INT8 [N, K] row-major (K-major), xs FP32 [M],
+ *   ws FP32 [N], D BF16 [M, N] dense.  K % 16 == 0, N % 8 == 0, A/B/D 16-byte
+ *   aligned.  `config` is accepted for ABI compatibility (any value 0..15).
+ *   Returns 1 on success, 0 on failure.
+ */
+int h3_int8(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M,
+            int N, int K, int config, uintptr_t stream);
+/*
+ * Replaces h3_int8_gate (kernels/gemm/gate.cu:275-282):
+ *   D[m, n] = bf16( fmaf( bf16(((acc*xs[m])*ws[n])+0), gate[rows[m]*N + n], residual[m, n] ) )
+ *   gate BF16 table [G, N], rows int32 [M], residual BF16 [M, N].  D may equal
+ *   residual (in-place update, h3_speedkit/runtime.py:120).  Returns 1 / 0.
+ */
+int h3_int8_gate(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                 const void* gate, const int32_t* rows, const void* residual, int M, int N, int K,
+                 int config, uintptr_t stream);
+/*
+ * Extended GEMM (no single reference counterpart): optional BF16 bias [N]
+ * (NULL = 0), epilogue selector (H3_EPI_*), output row stride ldd in elements
+ * (ldd >= N; ldd % 8 == 0).  The bias formula is the explicit
+ * __fadd_rn(__fmul_rn(__fmul_rn(acc, xs), ws), bias) of
+ * kernels/gemm/r84_kfourwarp.cu:240-241.  Returns 1 / 0.
+ */
+int h3_int8_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws,
+               const void* bias, void* D, int M, int N, int K, int64_t ldd, int epilogue,
+               uintptr_t stream);
+/*
+ * Extended gate GEMM: optional BF16 bias [N], and an optional requantised copy
+ * of the updated rows for the next layer (q INT8 [M, N] + qscale FP32 [M],
+ * ConvRot256 + per-token INT8 of D, the arithmetic of
+ * kernels/convrot/convrot_register_v2.cu:67-138).  q and qscale both NULL =>
+ * no requant.  Returns 1 / 0.
+ */
+int h3_int8_gate_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws,
+                    const void* bias, void* D, const void* gate, const int32_t* rows,
+                    const void* residual, void* q, void* qscale, int M, int N, int K,
+                    uintptr_t stream);
+/* cudaError_t-style code of the last failed h3_int8* call on this host thread
+ * (0 if the last call succeeded; cudaErrorInvalidValue for a rejected argument). */
+int h3_int8_last_error(void);
+/* Text for the last failure on this host thread. */
+const char* h3_int8_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Pipeline health and diagnostics                                           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Every mbarrier wait inside the GEMM pipeline is bounded.  A wait that runs
+ * out records a nonzero code in a per-device status word, stops the kernel
+ * (draining its own copies and releasing TMEM) and leaves the context usable.
+ * h3sk_pipeline_status copies that word to *status after synchronising
+ * `stream` and, when clear != 0, resets it.  Returns a cudaError_t value.
+ */
+int h3sk_pipeline_status(int* status, int clear, uintptr_t stream);
+/*
+ * Self-test of the bounded wait: launches one CTA that waits on an mbarrier no
+ * one arrives at, for at most timeout_us microseconds.  The kernel must come
+ * back with status H3SK_STATUS_WAIT_TIMEOUT in *status.  Returns cudaError_t.
+ */
+int h3sk_wait_selftest(int timeout_us, int* status, uintptr_t stream);
+/*
+ * tcgen05 kind::i8 issue-rate probe: every SM issues `iters` back-to-back
+ * 128x256x32 MMAs from shared memory into TMEM; *tops receives the achieved
+ * dense INT8 tera-ops per second.  Returns cudaError_t.
+ */
+int h3sk_int8_mma_peak(int iters, double* tops, uintptr_t stream);
+/* Library version string. */
+const char* h3sk_version(void);
+
+enum { H3SK_STATUS_OK = 0, H3SK_STATUS_WAIT_TIMEOUT = 1 };
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3SK_B200_H */

@@ -1,0 +1,124 @@
+"""Build the oracles.  TEST INFRASTRUCTURE ONLY.
+
+1. ``oracle/libh3_oracle.so`` -- the C restatement (h3_oracle.c), built with gcc,
+   -ffp-contract=off, no fast-math, OpenMP, baseline x86-64 code (it travels to
+   the GPU box, whose CPU may differ from the build host).
+2. ``oracle/_ref/*.so`` -- the reference's own CUDA kernels, compiled from the
+   sources where they lie under the reference checkout (never copied into this
+   repository) with the reference's flags (tools/build_kernels.py:26-40) and the
+   architecture switched to sm_100a:
+     * ``ref_norm_k{K}.so``  kernels/norm_quant/norm_quant.cu.  The reference fixes
+       ``K = 5376`` in a constexpr (norm_quant.cu:16); for other widths this
+       recipe writes a derived copy with only that constant changed into
+       ``oracle/_ref/gen/``, compiles it and deletes it again (only the .so stays);
+     * ``ref_convrot.so``    kernels/convrot/convrot_register_v2.cu, unmodified
+       (K in {5376, 7168});
+     * ``ref_kitchen.so``    oracle/ref_kitchen_launch.cu, which instantiates the
+       vendored Kitchen quantiser of kernels/convrot/vendor/convrot64_exact.cuh.
+   The reference's INT8 GEMMs (kernels/gemm/fc1.cu, gate.cu) need the external
+   CUTLASS library and are therefore not built; the GEMM oracle is the exact C
+   restatement (int32 accumulation + IEEE epilogue, reproducible bit for bit).
+   Step 2 runs only where the reference checkout exists (the build host); the
+   GPU box uses the prebuilt files.
+"""
+from __future__ import annotations
+
+import os
+import re
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REF_OUT = HERE / "_ref"
+REFERENCE = Path(os.environ.get("H3SK_REFERENCE", "/root/reference"))
+C_LIB = HERE / "libh3_oracle.so"
+NORM_WIDTHS = (2048, 4096, 5376)
+REF_FLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "--expt-relaxed-constexpr", "--expt-extended-lambda",
+             "--shared", "-Xcompiler=-fPIC", "-gencode=arch=compute_100a,code=sm_100a"]
+
+
+def _newer(target: Path, *sources: Path) -> bool:
+    return target.exists() and all(target.stat().st_mtime >= s.stat().st_mtime for s in sources if s.exists())
+
+
+def build_c(force: bool = False) -> Path:
+    src = HERE / "h3_oracle.c"
+    if not force and _newer(C_LIB, src, Path(__file__)):
+        return C_LIB
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("gcc is required to build the CPU oracle")
+    tmp = C_LIB.with_suffix(".so.tmp")
+    cmd = [cc, "-O2", "-std=c11", "-fno-fast-math", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared",
+           "-fvisibility=hidden", str(src), "-o", str(tmp), "-lm"]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    os.replace(tmp, C_LIB)
+    return C_LIB
+
+
+def _nvcc() -> str:
+    for c in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if c and Path(c).exists():
+            return c
+    raise RuntimeError("nvcc is required to build the reference GPU oracle")
+
+
+def _compile(nvcc: str, source: Path, target: Path, includes: list[Path], extra: list[str]) -> None:
+    cmd = [nvcc, *REF_FLAGS, *extra, *(f"-I{p}" for p in includes), str(source), "-o", str(target)]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode:
+        raise RuntimeError(f"reference oracle build failed for {source.name}:\n{result.stderr[-4000:]}")
+
+
+def build_ref(force: bool = False) -> list[Path]:
+    """Compile the reference kernels into oracle/_ref (needs the reference checkout)."""
+    kernels = REFERENCE / "kernels"
+    if not (kernels / "norm_quant" / "norm_quant.cu").exists():
+        return sorted(REF_OUT.glob("*.so"))
+    nvcc = _nvcc()
+    REF_OUT.mkdir(exist_ok=True)
+    gen = REF_OUT / "gen"
+    gen.mkdir(exist_ok=True)
+    built = []
+    norm_src = kernels / "norm_quant" / "norm_quant.cu"
+    text = norm_src.read_text()
+    pattern = re.compile(r"constexpr int K = 5376,")
+    if len(pattern.findall(text)) != 1:
+        raise RuntimeError("norm_quant.cu no longer has the single K constant this recipe rewrites")
+    for k in NORM_WIDTHS:
+        target = REF_OUT / f"ref_norm_k{k}.so"
+        if force or not _newer(target, norm_src, Path(__file__)):
+            source = norm_src if k == 5376 else gen / f"norm_quant_k{k}.cu"
+            if k != 5376:
+                source.write_text(pattern.sub(f"constexpr int K = {k},", text))
+            try:
+                _compile(nvcc, source, target, [norm_src.parent, norm_src.parent / "vendor"],
+                         ["--use_fast_math"])
+            finally:
+                if k != 5376:
+                    source.unlink(missing_ok=True)
+        built.append(target)
+    conv_src = kernels / "convrot" / "convrot_register_v2.cu"
+    target = REF_OUT / "ref_convrot.so"
+    if force or not _newer(target, conv_src):
+        _compile(nvcc, conv_src, target, [conv_src.parent, conv_src.parent / "vendor"], ["--use_fast_math"])
+    built.append(target)
+    launcher = HERE / "ref_kitchen_launch.cu"
+    target = REF_OUT / "ref_kitchen.so"
+    vendor = kernels / "convrot" / "vendor"
+    if force or not _newer(target, launcher, vendor / "convrot64_exact.cuh"):
+        _compile(nvcc, launcher, target, [vendor], ["--use_fast_math"])
+    built.append(target)
+    return built
+
+
+def build(force: bool = False) -> None:
+    build_c(force)
+    build_ref(force)
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv)
+    print("oracle built:", C_LIB, *sorted(p.name for p in REF_OUT.glob("*.so")))

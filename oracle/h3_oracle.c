@@ -1,0 +1,314 @@
+/*
+ * h3_oracle.c -- CPU restatement of the H3 SpeedKit quantized DiT-block linear
+ * path.  TEST INFRASTRUCTURE ONLY: tests/, the smoke check and bench.py's
+ * cpu_baseline / reference arm use it as the checker and CPU baseline; the
+ * product path never calls it.
+ *
+ * Every function states the reference lines it restates.  Built with
+ * -ffp-contract=off and without fast-math, so each C float operation is one
+ * IEEE round-to-nearest FP32 operation and fmaf is the correctly rounded fused
+ * multiply-add.  Known, documented departures from the GPU reference:
+ *   - rrms: the reference uses the hardware rsqrt.approx.f32; here it is
+ *     1/sqrt evaluated in double and rounded (callers may inject the GPU's rrms);
+ *   - the quantiser quotient: the reference divides with the compiler's fast
+ *     division (its quantiser TUs use --use_fast_math); here IEEE division;
+ *   - tanhf/expf in the activations are libm's.
+ * Flush-to-zero of the fast-math quantiser TUs is reproduced on the operations
+ * of the rotation and the code computation (ftz_* helpers).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define H3O_EXPORT __attribute__((visibility("default")))
+
+/* ---- BF16 / FP32 bit helpers ------------------------------------------------ */
+static inline float f_from_u(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t u_from_f(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bf_to_f(uint16_t b) { return f_from_u((uint32_t)b << 16); }
+/* Round-to-nearest-even FP32 -> BF16 (cvt.rn.bf16.f32); NaN stays NaN. */
+static inline uint16_t f_to_bf(float f) {
+  uint32_t u = u_from_f(f);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return (uint16_t)((u >> 16) | 0x0040u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+static inline float bf_round(float f) { return bf_to_f(f_to_bf(f)); }
+/* Flush a subnormal to a zero of the same sign. */
+static inline float ftz(float f) {
+  uint32_t u = u_from_f(f);
+  return ((u & 0x7f800000u) == 0 && (u & 0x007fffffu)) ? f_from_u(u & 0x80000000u) : f;
+}
+static inline float ftz_add(float a, float b) { return ftz(ftz(a) + ftz(b)); }
+static inline float ftz_sub(float a, float b) { return ftz(ftz(a) - ftz(b)); }
+static inline float ftz_mul(float a, float b) { return ftz(ftz(a) * ftz(b)); }
+
+static int set_threads(int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+  return omp_get_max_threads();
+#else
+  (void)threads;
+  return 1;
+#endif
+}
+
+/* ---- ConvRot256 ---------------------------------------------------------------
+ * Four radix-4 stages with strides 1, 4, 16, 64 over one 256-value group; output
+ * i of a stage is 0.5f * h4_d(x0..x3) with d = (i / s) & 3, base = i - d*s,
+ * x_j = v[base + j*s], and the additions taken left to right
+ * (kernels/convrot/vendor/convrot64_exact.cuh:202-234, 664-677).            */
+static inline float h4_half(int d, float x0, float x1, float x2, float x3) {
+  float s;
+  switch (d) {
+    case 0: s = ftz_sub(ftz_add(ftz_add(x0, x1), x2), x3); break;
+    case 1: s = ftz_add(ftz_sub(ftz_add(x0, x1), x2), x3); break;
+    case 2: s = ftz_add(ftz_add(ftz_sub(x0, x1), x2), x3); break;
+    default: s = ftz_add(ftz_add(ftz_add(-x0, x1), x2), x3); break;
+  }
+  return ftz_mul(0.5f, s);
+}
+
+static void convrot256(float* g) {
+  float tmp[256];
+  static const int strides[4] = {1, 4, 16, 64};
+  for (int st = 0; st < 4; ++st) {
+    const int s = strides[st];
+    for (int i = 0; i < 256; ++i) {
+      const int d = (i / s) & 3, base = i - d * s;
+      tmp[i] = h4_half(d, g[base], g[base + s], g[base + 2 * s], g[base + 3 * s]);
+    }
+    memcpy(g, tmp, sizeof(tmp));
+  }
+}
+
+/* ---- Row scale and INT8 codes ---------------------------------------------------
+ * scale = max(min(absmax, BF16_MAX) * (1/127), 1e-30), stored unrounded
+ * (kernels/norm_quant/norm_quant.cu:183-192); code = clamp(nearbyint(
+ * bf(bf(v) / bf(scale))), -128, 127) (convrot64_exact.cuh:53-57,
+ * convrot_register_v2.cu:126-129).                                          */
+static float row_scale(const float* v, int64_t k) {
+  float amax = 0.0f;
+  for (int64_t i = 0; i < k; ++i) amax = fmaxf(amax, fabsf(ftz(v[i])));
+  return fmaxf(ftz_mul(fminf(amax, 3.38953139e38f), 1.0f / 127.0f), 1.0e-30f);
+}
+
+static inline int8_t int8_code(float v, float scale) {
+  const float sb = bf_round(ftz(scale));
+  const float vb = bf_round(ftz(v));
+  const float q = bf_round(ftz(ftz(vb) / ftz(sb)));
+  float c = nearbyintf(q);
+  c = fminf(127.0f, fmaxf(-128.0f, c));
+  return (int8_t)c;
+}
+
+/* Public: quantise already-rotated rows (used by tests that inject values). */
+H3O_EXPORT void h3o_quant_rows(const float* rot, int64_t m, int64_t k, int8_t* q, float* scale, int threads) {
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const float* v = rot + r * k;
+    const float s = row_scale(v, k);
+    scale[r] = s;
+    for (int64_t i = 0; i < k; ++i) q[r * k + i] = int8_code(v[i], s);
+  }
+}
+
+/* Public: ConvRot256 of each group of each row, FP32 in/out. */
+H3O_EXPORT void h3o_convrot_rows(float* v, int64_t m, int64_t k, int threads) {
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t g = 0; g < k / 256; ++g) convrot256(v + r * k + g * 256);
+}
+
+/* ---- Fused prologue (kernels/norm_quant/norm_quant.cu:51-213) -------------------
+ * sum of squares: logical thread t in 0..127 fma-accumulates the 4-element
+ * chunks t, t+128, ... of the row in element order (:56-65); each 32-thread
+ * warp folds with shfl_down offsets 16, 8, 4, 2, 1 (:66-67); the warp sums fold
+ * as (w0+w2)+(w1+w3) (:69-74); variance = sum / K (:75).
+ * rrms = rsqrt(var + eps) (:134).
+ * n = bf(w * (rrms * x)); s = bf(shift); c = bf(scale); one_c = bf(1 + c);
+ * out = bf(bf(n * one_c) + s) (:164-172), table row = rows[token] (:138-140). */
+static float rms_variance(const uint16_t* x, int64_t k) {
+  float lane_sum[128];
+  const int64_t chunks = k / 4;
+  for (int t = 0; t < 128; ++t) {
+    float s = 0.0f;
+    for (int64_t i = t; i < chunks; i += 128)
+      for (int e = 0; e < 4; ++e) {
+        const float v = bf_to_f(x[4 * i + e]);
+        s = fmaf(v, v, s);
+      }
+    lane_sum[t] = s;
+  }
+  float warp_sum[4];
+  for (int w = 0; w < 4; ++w) {
+    float s[32];
+    for (int l = 0; l < 32; ++l) s[l] = lane_sum[32 * w + l];
+    for (int off = 16; off > 0; off >>= 1) {
+      float nxt[32];
+      for (int l = 0; l < 32; ++l) nxt[l] = (l + off < 32) ? s[l] + s[l + off] : s[l] + s[l];
+      /* lanes whose source is out of range add their own value, as shfl_down
+       * returns the caller's own register; only lane 0's result is used. */
+      memcpy(s, nxt, sizeof(s));
+    }
+    warp_sum[w] = s[0];
+  }
+  const float total = (warp_sum[0] + warp_sum[2]) + (warp_sum[1] + warp_sum[3]);
+  return total / (float)k;
+}
+
+H3O_EXPORT float h3o_rms_variance(const uint16_t* x, int64_t k) { return rms_variance(x, k); }
+
+H3O_EXPORT int h3o_norm_quant(const uint16_t* x, int64_t xs, const uint16_t* w, const void* shift,
+                              const void* scale, int table_dtype, int64_t ss, int64_t cs,
+                              const int32_t* rows, int64_t m, int64_t k, float eps,
+                              const float* rrms_in, int8_t* q, float* qscale, uint16_t* dbg_norm,
+                              float* dbg_rot, float* dbg_rstd, int threads) {
+  if (k % 256 || k < 256 || xs < k) return 1;
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const uint16_t* xr = x + r * xs;
+    float rrms;
+    if (rrms_in) {
+      rrms = rrms_in[r];
+    } else {
+      const float var = rms_variance(xr, k);
+      rrms = (float)(1.0 / sqrt((double)(var + eps)));
+    }
+    const int64_t tr = rows[r];
+    float* v = (float*)malloc(sizeof(float) * (size_t)k);
+    for (int64_t i = 0; i < k; ++i) {
+      const float xv = bf_to_f(xr[i]);
+      const float wv = bf_to_f(w[i]);
+      float sh, sc;
+      if (table_dtype == 0) {
+        sh = ((const float*)shift)[tr * ss + i];
+        sc = ((const float*)scale)[tr * cs + i];
+      } else {
+        sh = bf_to_f(((const uint16_t*)shift)[tr * ss + i]);
+        sc = bf_to_f(((const uint16_t*)scale)[tr * cs + i]);
+      }
+      float n = bf_round(wv * (rrms * xv));
+      const float sb = bf_round(sh), cb = bf_round(sc);
+      const float one_c = bf_round(1.0f + cb);
+      const float p = bf_round(n * one_c);
+      n = bf_round(p + sb);
+      v[i] = n;
+      if (dbg_norm) dbg_norm[r * k + i] = f_to_bf(n);
+    }
+    for (int64_t g = 0; g < k / 256; ++g) convrot256(v + g * 256);
+    const float s = row_scale(v, k);
+    qscale[r] = s;
+    if (dbg_rstd) dbg_rstd[r] = rrms;
+    for (int64_t i = 0; i < k; ++i) {
+      if (dbg_rot) dbg_rot[r * k + i] = v[i];
+      q[r * k + i] = int8_code(v[i], s);
+    }
+    free(v);
+  }
+  return 0;
+}
+
+/* ---- ConvRot quantiser with input activation --------------------------------------
+ * convrot64_exact.cuh:913-1027 (act none / GELU-tanh / SwiGLU) and
+ * convrot_register_v2.cu:67-138 (act none).  x rows have stride xs elements;
+ * for SwiGLU the row is [gate | up], 2k wide.                               */
+static inline float act_value(const uint16_t* xr, int64_t i, int64_t k, int act) {
+  if (act == 2) {
+    const float g = bf_to_f(xr[i]), u = bf_to_f(xr[k + i]);
+    return (g / (1.0f + expf(-g))) * u;
+  }
+  const float v = bf_to_f(xr[i]);
+  if (act == 1) {
+    const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(inner));
+  }
+  return v;
+}
+
+H3O_EXPORT int h3o_convrot_quant(const uint16_t* x, int64_t xs, int64_t m, int64_t k, int act, int8_t* q,
+                                 float* scale, float* rotated, int threads) {
+  if (k % 256 || k < 256 || act < 0 || act > 2) return 1;
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const uint16_t* xr = x + r * xs;
+    float* v = (float*)malloc(sizeof(float) * (size_t)k);
+    for (int64_t i = 0; i < k; ++i) v[i] = act_value(xr, i, k, act);
+    for (int64_t g = 0; g < k / 256; ++g) convrot256(v + g * 256);
+    if (rotated) memcpy(rotated + r * k, v, sizeof(float) * (size_t)k);
+    if (q) {
+      const float s = row_scale(v, k);
+      scale[r] = s;
+      for (int64_t i = 0; i < k; ++i) q[r * k + i] = int8_code(v[i], s);
+    }
+    free(v);
+  }
+  return 0;
+}
+
+/* ---- INT8 GEMM, exact int32 (kernels/gemm/fc1.cu:60-101: A row-major [M,K],
+ * B [N,K] "ColumnMajor" = K-major, int32 accumulator).                         */
+H3O_EXPORT void h3o_gemm_s32(const int8_t* a, const int8_t* b, int64_t m, int64_t n, int64_t k, int32_t* c,
+                             int threads) {
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i) {
+    const int8_t* ar = a + i * k;
+    for (int64_t j = 0; j < n; ++j) {
+      const int8_t* br = b + j * k;
+      int32_t s = 0;
+      for (int64_t t = 0; t < k; ++t) s += (int32_t)ar[t] * (int32_t)br[t];
+      c[i * n + j] = s;
+    }
+  }
+}
+
+/* ---- Epilogues --------------------------------------------------------------------
+ * dequant: y = bf(((float(acc) * xs[m]) * ws[n]) + bias[n])   fc1.cu:83-90 and
+ *          the explicit __fadd_rn(__fmul_rn(__fmul_rn(..))) of r84_kfourwarp.cu:240-241
+ * gelu:    out = bf(gelu_tanh(y))                               convrot64_exact.cuh:913-923
+ * gate:    out = bf(fmaf(y, gate[rows[m]*gate_ld + n], residual[m, n]))
+ *                                                              gate.cu:172-180, 239-242     */
+static inline float dequant_value(int32_t acc, float xs, float ws, float bias) {
+  const float a = (float)acc;
+  return bf_round(((a * xs) * ws) + bias);
+}
+
+H3O_EXPORT void h3o_dequant(const int32_t* acc, const float* xs, const float* ws, const uint16_t* bias,
+                            int64_t m, int64_t n, int gelu, uint16_t* out, int64_t ldo, int threads) {
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j) {
+      float y = dequant_value(acc[i * n + j], xs[i], ws[j], bias ? bf_to_f(bias[j]) : 0.0f);
+      if (gelu) {
+        const float inner = 0.7978845608028654f * (y + 0.044715f * y * y * y);
+        y = 0.5f * y * (1.0f + tanhf(inner));
+      }
+      out[i * ldo + j] = f_to_bf(y);
+    }
+}
+
+H3O_EXPORT void h3o_gate(const int32_t* acc, const float* xs, const float* ws, const uint16_t* bias,
+                         const uint16_t* gate, int64_t gate_ld, const int32_t* rows, const uint16_t* residual,
+                         int64_t m, int64_t n, uint16_t* out, int threads) {
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < m; ++i) {
+    const uint16_t* g = gate + (int64_t)rows[i] * gate_ld;
+    for (int64_t j = 0; j < n; ++j) {
+      const float y = dequant_value(acc[i * n + j], xs[i], ws[j], bias ? bf_to_f(bias[j]) : 0.0f);
+      out[i * n + j] = f_to_bf(fmaf(y, bf_to_f(g[j]), bf_to_f(residual[i * n + j])));
+    }
+  }
+}
+
+H3O_EXPORT int h3o_max_threads(void) { return set_threads(0); }

@@ -1,0 +1,94 @@
+"""The reference's own CUDA kernels as the GPU oracle.  TEST INFRASTRUCTURE ONLY.
+
+Loads the libraries ``oracle/build.py`` compiled into ``oracle/_ref`` from the
+reference sources (norm_quant.cu, convrot_register_v2.cu and the vendored
+Kitchen quantiser) and runs them on torch CUDA tensors.  Output buffers are
+allocated by the caller-side helpers here with torch; nothing in the product
+path uses this module.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+from pathlib import Path
+
+REF = Path(__file__).resolve().parent / "_ref"
+_CACHE: dict[str, ct.CDLL] = {}
+
+
+def available(name: str) -> bool:
+    return (REF / name).exists()
+
+
+def _load(name: str) -> ct.CDLL:
+    if name not in _CACHE:
+        path = REF / name
+        if not path.exists():
+            raise FileNotFoundError(f"reference GPU oracle {path} is not built (run oracle/build.py)")
+        _CACHE[name] = ct.CDLL(str(path), mode=ct.RTLD_LOCAL)
+    return _CACHE[name]
+
+
+def _stream(t):
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def norm_widths() -> list[int]:
+    return sorted(int(p.stem.split("_k")[1]) for p in REF.glob("ref_norm_k*.so"))
+
+
+def norm_quant(x, w, shift, scale, rows, eps, *, debug=False):
+    """Reference norm_quant_kernel (norm_quant.cu:122-213) at K = x.shape[1]."""
+    import torch
+    m, k = x.shape
+    so = _load(f"ref_norm_k{k}.so")
+    fn = so.h3_norm_quant_run
+    fn.argtypes = [ct.c_void_p] * 10 + [ct.c_int64] * 4 + [ct.c_float, ct.c_int, ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    dev = x.device
+    q = torch.empty((m, k), dtype=torch.int8, device=dev)
+    qs = torch.empty((m, 1), dtype=torch.float32, device=dev)
+    dn = torch.empty((m, k), dtype=torch.bfloat16, device=dev) if debug else None
+    dr = torch.empty((m, k), dtype=torch.float32, device=dev) if debug else None
+    drs = torch.empty((m,), dtype=torch.float32, device=dev) if debug else None
+    ptrs = [t.data_ptr() if t is not None else None for t in (x, w, shift, scale, rows, q, qs, dn, dr, drs)]
+    rc = fn(*ptrs, m, x.stride(0), shift.stride(0), scale.stride(0), float(eps),
+            int(shift.dtype == torch.bfloat16), int(debug), _stream(x))
+    if rc:
+        raise RuntimeError(f"reference norm_quant failed with CUDA error {rc}")
+    return (q, qs, dn, dr, drs) if debug else (q, qs)
+
+
+def convrot_register(x, mode=0):
+    """Reference register_rotate_quant (convrot_register_v2.cu:67-138), K in {5376, 7168}."""
+    import torch
+    m, k = x.shape
+    so = _load("ref_convrot.so")
+    fn = so.h3_convrot_register_run
+    fn.argtypes = [ct.c_void_p] * 4 + [ct.c_int64, ct.c_int, ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device) if mode != 2 else None
+    sc = torch.empty((m, 1), dtype=torch.float32, device=x.device) if mode != 2 else None
+    rot = torch.empty((m, k), dtype=torch.float32, device=x.device) if mode != 0 else None
+    rc = fn(x.data_ptr(), q.data_ptr() if q is not None else None, sc.data_ptr() if sc is not None else None,
+            rot.data_ptr() if rot is not None else None, m, k, mode, _stream(x))
+    if rc:
+        raise RuntimeError(f"reference convrot_register failed with CUDA error {rc}")
+    return q, sc, rot
+
+
+def kitchen_quant(x, act=0):
+    """Reference Kitchen quantize_int8_rowwise_convrot64_kernel (convrot64_exact.cuh:942-1027)."""
+    import torch
+    m, width = x.shape
+    k = width // 2 if act == 2 else width
+    so = _load("ref_kitchen.so")
+    fn = so.ref_kitchen_convrot64_quant
+    fn.argtypes = [ct.c_void_p] * 3 + [ct.c_int64, ct.c_int, ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    sc = torch.empty((m,), dtype=torch.float32, device=x.device)
+    rc = fn(x.data_ptr(), q.data_ptr(), sc.data_ptr(), m, k, act, _stream(x))
+    if rc:
+        raise RuntimeError(f"reference Kitchen quantiser failed with CUDA error {rc}")
+    return q, sc

@@ -27,27 +27,27 @@ import torch
 FULL_ROWS = {1: 1024, 2: 6144, 3: 24576, 4: 24576, 5: 98304}
 
 
-def generator(cfg: int, salt: int = 0) -> torch.Generator:
-    return torch.Generator().manual_seed(1000 + cfg + 7919 * salt)
+def generator(cfg: int, salt: int = 0, device="cpu") -> torch.Generator:
+    return torch.Generator(device=device).manual_seed(1000 + cfg + 7919 * salt)
 
 
 def outlier_normal(rows: int, cols: int, n_outliers: int, factor: float, g: torch.Generator) -> torch.Tensor:
-    x = torch.randn((rows, cols), generator=g, dtype=torch.float32)
-    channels = torch.randperm(cols, generator=g)[:n_outliers]
+    x = torch.randn((rows, cols), generator=g, dtype=torch.float32, device=g.device)
+    channels = torch.randperm(cols, generator=g, device=g.device)[:n_outliers]
     x[:, channels] *= factor
     return x.to(torch.bfloat16)
 
 
 def int8_uniform(rows: int, cols: int, g: torch.Generator) -> torch.Tensor:
-    return torch.randint(-127, 128, (rows, cols), generator=g, dtype=torch.int8)
+    return torch.randint(-127, 128, (rows, cols), generator=g, dtype=torch.int8, device=g.device)
 
 
 def uniform(n: int, lo: float, hi: float, g: torch.Generator) -> torch.Tensor:
-    return torch.rand((n,), generator=g, dtype=torch.float32) * (hi - lo) + lo
+    return torch.rand((n,), generator=g, dtype=torch.float32, device=g.device) * (hi - lo) + lo
 
 
 def normal_bf16(shape, std: float, g: torch.Generator) -> torch.Tensor:
-    return (torch.randn(shape, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
+    return (torch.randn(shape, generator=g, dtype=torch.float32, device=g.device) * std).to(torch.bfloat16)
 
 
 def cfg1(rows: int = FULL_ROWS[1], k: int = 2048, n: int = 2048):
@@ -117,11 +117,13 @@ class BlockWeights:
         return BlockWeights(**{k: v.to(device) for k, v in self.__dict__.items()})
 
 
-def cfg5_block(index: int, d: int = 4096, ffn: int = 16384, tables: int = 1) -> BlockWeights:
-    g = generator(5, salt=1 + index)
+def cfg5_block(index: int, d: int = 4096, ffn: int = 16384, tables: int = 1, device="cpu") -> BlockWeights:
+    """Block `index` of the cfg-5 stack, drawn on `device` (a CPU draw and a CUDA
+    draw of the same block differ: each device has its own generator stream)."""
+    g = generator(5, salt=1 + index, device=device)
     return BlockWeights(
-        norm1=(torch.rand((d,), generator=g) + 0.5).to(torch.bfloat16),
-        norm2=(torch.rand((d,), generator=g) + 0.5).to(torch.bfloat16),
+        norm1=(torch.rand((d,), generator=g, device=g.device) + 0.5).to(torch.bfloat16),
+        norm2=(torch.rand((d,), generator=g, device=g.device) + 0.5).to(torch.bfloat16),
         qkv=int8_uniform(3 * d, d, g), qkv_s=uniform(3 * d, 0.0005, 0.005, g),
         out=int8_uniform(d, d, g), out_s=uniform(d, 0.0005, 0.005, g),
         fc1=int8_uniform(ffn, d, g), fc1_s=uniform(ffn, 0.0005, 0.005, g),
@@ -132,6 +134,6 @@ def cfg5_block(index: int, d: int = 4096, ffn: int = 16384, tables: int = 1) -> 
     )
 
 
-def cfg5_tokens(rows: int = FULL_ROWS[5], d: int = 4096) -> torch.Tensor:
-    g = generator(5)
-    return torch.randn((rows, d), generator=g).to(torch.bfloat16)
+def cfg5_tokens(rows: int = FULL_ROWS[5], d: int = 4096, device="cpu") -> torch.Tensor:
+    g = generator(5, device=device)
+    return torch.randn((rows, d), generator=g, device=g.device).to(torch.bfloat16)

@@ -1,11 +1,11 @@
 // ConvRot256 + per-token INT8 quantiser for B200, with an optional input
 // activation (none / GELU-tanh / SwiGLU).
 //
-// One CTA per row, ceil(K/1024) warps; every lane owns 32 values of one 256-wide
-// group in the register layout of rowquant.cuh and loads them with 16-byte
-// vector loads straight from HBM (each 32-byte sector of the row is consumed by
-// one warp instruction, so the row is read exactly once).  The rotation runs in
-// registers and warp shuffles; codes leave as 8-byte stores.
+// One CTA per row, 4 threads per 256-value group, 64 values per thread (see
+// rq_core.cuh): 16-byte vector loads of 64 consecutive BF16 values per thread,
+// FHT stages 1-3 in registers, one swizzled shared-memory exchange, stage 4 in
+// registers, row absmax (one block barrier), packed codes as 16-byte stores.
+// HBM traffic per row: 2K bytes in (4K for SwiGLU), K + 4 bytes out.
 //
 // Replaces kernels/convrot/convrot_register_v2.cu:67-138 (ACT none, K in
 // {5376, 7168}) and Kitchen's quantize_int8_rowwise_convrot64_kernel
@@ -13,7 +13,7 @@
 // / SwiGLU) for any K % 256 == 0 up to 16384.  The per-value results do not
 // depend on the thread layout: each FHT output is the same expression of the
 // same four inputs, and the absmax is an order-free fmaxf.
-#include "rowquant.cuh"
+#include "rq_core.cuh"
 #include "../../include/h3sk_b200.h"
 
 namespace h3sk {
@@ -21,88 +21,86 @@ namespace {
 
 constexpr int kMaxK = 16384;
 
-__host__ __device__ constexpr int convrot_threads(int k) { return ((k + 1023) / 1024) * 32; }
+__host__ __device__ constexpr int convrot_threads(int k) { return ((k / 64 + 31) / 32) * 32; }
+__host__ __device__ constexpr int convrot_smem(int k) { return (convrot_threads(k) / rq::kTeam) * rq::kGroupBytes; }
 
 enum : int { kModeQuant = 0, kModeDiag = 1, kModeRotate = 2 };
 
-__device__ __forceinline__ void unpack8(const uint4 raw, float* out) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+template <int kAct>
+__device__ __forceinline__ void load_act_a(const __nv_bfloat16* xr, int col0, int K, uint64_t (&v)[32]) {
 #pragma unroll
-  for (int e = 0; e < 8; ++e) out[e] = bf_bits_to_float((w[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
+  for (int i = 0; i < 8; ++i) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + col0 + 8 * i));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    if constexpr (kAct == kActNone) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) v[4 * i + h] = rq::bf2_to_f2(w[h]);
+    } else if constexpr (kAct == kActGeluTanh) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t x = rq::bf2_to_f2(w[h]);
+        v[4 * i + h] = rq::f2_pack(gelu_tanh(rq::f2_lo(x)), gelu_tanh(rq::f2_hi(x)));
+      }
+    } else {
+      const uint4 up = __ldg(reinterpret_cast<const uint4*>(xr + K + col0 + 8 * i));
+      const uint32_t u[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t g = rq::bf2_to_f2(w[h]), x = rq::bf2_to_f2(u[h]);
+        v[4 * i + h] = rq::f2_pack(swiglu(rq::f2_lo(g), rq::f2_lo(x)), swiglu(rq::f2_hi(g), rq::f2_hi(x)));
+      }
+    }
+  }
 }
 
 template <int kAct, int kMode>
-__global__ void __launch_bounds__(512) convrot_quant_rows(
+__global__ void __launch_bounds__(256) convrot_quant_rows(
     const __nv_bfloat16* __restrict__ X, int64_t xs, int8_t* __restrict__ Q,
-    float* __restrict__ Scales, float* __restrict__ Rotated, int K) {
-  __shared__ float warp_max[16];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int group = warp * 4 + (lane >> 3), octet = lane & 7;
+    float* __restrict__ Scales, float* __restrict__ Rotated, int K, int q_vec16) {
+  extern __shared__ __align__(16) float exch[];
+  __shared__ float warp_max[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int group = tid >> 2, q = tid & 3;
   const bool active = group < K / 256;
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = X + row * xs;
+
+  uint64_t v[32];
+  if (active) {
+    load_act_a<kAct>(xr, group * 256 + 64 * q, K, v);
+  } else {
+#pragma unroll
+    for (int p = 0; p < 32; ++p) v[p] = 0;
+  }
+  rq::fht_layout_a(v);
+  rq::exchange_a_to_b(v, exch + group * 256, q, group & 1);
+  rq::fht_layout_b(v);
+
   const int64_t out_row = row * K;
-
-  float v[32];
-  uint4 raw[4], up_raw[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = group * 256 + octet_run_col(octet, j);
-    raw[j] = make_uint4(0, 0, 0, 0);
-    up_raw[j] = make_uint4(0, 0, 0, 0);
-    if (active) {
-      raw[j] = __ldg(reinterpret_cast<const uint4*>(xr + col));
-      if constexpr (kAct == kActSwiGLU) up_raw[j] = __ldg(reinterpret_cast<const uint4*>(xr + K + col));
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float a[8];
-    unpack8(raw[j], a);
-    if constexpr (kAct == kActSwiGLU) {
-      float u[8];
-      unpack8(up_raw[j], u);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[j * 8 + e] = active ? swiglu(a[e], u[e]) : 0.0f;
-    } else if constexpr (kAct == kActGeluTanh) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[j * 8 + e] = active ? gelu_tanh(a[e]) : 0.0f;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[j * 8 + e] = a[e];
-    }
-  }
-
-  convrot256_registers(v, lane);
-
   if constexpr (kMode != kModeQuant) {
     if (active) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int col = group * 256 + octet_run_col(octet, j);
-        float4* dst = reinterpret_cast<float4*>(Rotated + out_row + col);
-        dst[0] = make_float4(v[j * 8 + 0], v[j * 8 + 1], v[j * 8 + 2], v[j * 8 + 3]);
-        dst[1] = make_float4(v[j * 8 + 4], v[j * 8 + 5], v[j * 8 + 6], v[j * 8 + 7]);
+        float4* dst = reinterpret_cast<float4*>(Rotated + out_row + group * 256 + rq::run_col_b(q, j));
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint64_t a = v[8 * j + 2 * h], b = v[8 * j + 2 * h + 1];
+          dst[h] = make_float4(rq::f2_lo(a), rq::f2_hi(a), rq::f2_lo(b), rq::f2_hi(b));
+        }
       }
     }
   }
   if constexpr (kMode == kModeRotate) return;
 
-  float local = 0.0f;
-#pragma unroll
-  for (int r = 0; r < 32; ++r) local = fmaxf(local, fabsf(v[r]));
-  local = warp_allmax(local);
+  const float local = warp_allmax(rq::absmax64(v));
   if (lane == 0) warp_max[warp] = local;
   __syncthreads();
   const int nwarps = blockDim.x >> 5;
   const float scale = int8_row_scale(warp_allmax(lane < nwarps ? warp_max[lane] : 0.0f));
-  if (threadIdx.x == 0) Scales[row] = scale;
+  if (tid == 0) Scales[row] = scale;
   if (active) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = group * 256 + octet_run_col(octet, j);
-      *reinterpret_cast<uint2*>(Q + out_row + col) = pack_codes8(&v[j * 8], scale);
-    }
+    const float scale_bf = __bfloat162float(__float2bfloat16_rn(scale));
+    rq::store_codes(Q + out_row + group * 256, q, v, scale_bf, q_vec16);
   }
 }
 
@@ -111,9 +109,15 @@ bool valid_k(int64_t k) { return k >= 256 && k <= kMaxK && k % 256 == 0; }
 template <int kAct, int kMode>
 cudaError_t launch(const void* x, int64_t xs, void* q, void* scale, void* rotated, int64_t rows, int k,
                    cudaStream_t stream) {
-  convrot_quant_rows<kAct, kMode><<<dim3(unsigned(rows)), convrot_threads(k), 0, stream>>>(
+  auto kernel = convrot_quant_rows<kAct, kMode>;
+  const int smem = convrot_smem(k);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
+  kernel<<<dim3(unsigned(rows)), convrot_threads(k), smem, stream>>>(
       static_cast<const __nv_bfloat16*>(x), xs, static_cast<int8_t*>(q), static_cast<float*>(scale),
-      static_cast<float*>(rotated), k);
+      static_cast<float*>(rotated), k, (uintptr_t(q) & 15u) == 0 ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -144,7 +148,8 @@ H3SK_EXPORT int h3_convrot_register_query(int k, H3ConvRotResources* out, size_t
   int active = 0, device = 0, sms = 0, max_threads = 0;
   cudaError_t e = cudaFuncGetAttributes(&attr, kernel);
   if (e != cudaSuccess) return e;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, 0)) != cudaSuccess) return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, convrot_smem(k))) != cudaSuccess)
+    return e;
   if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&max_threads, cudaDevAttrMaxThreadsPerMultiProcessor, device)) != cudaSuccess)

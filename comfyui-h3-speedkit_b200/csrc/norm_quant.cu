@@ -1,23 +1,26 @@
 // Fused prologue for B200: RMSNorm -> adaLN modulation -> ConvRot256 -> per-token INT8.
 //
-// One CTA per token row.  The row (K BF16 values) is staged once into shared
-// memory with 16-byte (or, for 8-byte-aligned strided rows, 8-byte) coalesced
-// loads; the RMS statistics are read from shared memory in the reference's
-// accumulation order, and the modulated values are then read in the ConvRot
-// register layout, rotated with warp shuffles and quantised in registers.  HBM
-// traffic per row: K*2 bytes in, K bytes + 4 bytes out.
+// One CTA per token row; the ConvRot/quantisation core is rq_core.cuh (4 threads
+// per 256-value group, 64 consecutive values per thread, one swizzled
+// shared-memory exchange).  HBM traffic per row: K*2 bytes in, K bytes + 4 out.
 //
 // Arithmetic follows kernels/norm_quant/norm_quant.cu:51-213:
 //  * sum of squares: logical thread t (0..127) fma-accumulates the 4-element
-//    chunks t, t+128, ... in element order; a shfl_down tree per warp; the four
-//    warp sums fold as (w0+w2)+(w1+w3); variance = div.rn(sum, K)  (:51-78);
+//    chunks t, t+128, ... in element order; a shfl_down tree per 32-thread
+//    logical warp; the four warp sums fold as (w0+w2)+(w1+w3);
+//    variance = div.rn(sum, K)  (:51-78).  Here physical thread p < 64 runs the
+//    logical threads p and p+64 as the two halves of packed f32x2 FMAs (IEEE, no
+//    flush), so physical warp 0 carries logical warps 0 and 2, warp 1 carries 1 and 3;
 //  * rrms = rsqrt.approx(add.rn(var, eps))  (:133-134);
-//  * n = bf(w*(rrms*x)); out = bf(bf(n*bf(1+bf(scale))) + bf(shift))  (:164-172);
-//  * ConvRot256 + row scale + codes as in rowquant.cuh  (:179-211).
-// The reference fixes K = 5376 with 192 threads; this kernel takes K as a
-// runtime value (K % 256 == 0, 256 <= K <= 16384) with
-// max(128, ceil(K/1024)*32) threads.
-#include "rowquant.cuh"
+//  * n = bf(w*(rrms*x)) with IEEE f32x2 multiplies; out = bf(bf(n*bf(1+bf(scale))) +
+//    bf(shift))  (:164-172) with BF16x2 add/multiply: for BF16 operands the FP32
+//    result rounded to BF16 equals the directly rounded BF16 result (the FP32
+//    product of two BF16 values is exact, and FP32 has more than 2*8+2 bits, so
+//    rounding the FP32 sum again to BF16 is the correctly rounded BF16 sum);
+//  * ConvRot256 + row scale + codes as in rq_core.cuh  (:179-211).
+// The reference fixes K = 5376 with 192 threads; this kernel takes any
+// K % 256 == 0 up to 16384 with max(64, K/64 rounded up to a warp) threads.
+#include "rq_core.cuh"
 #include "../../include/h3sk_b200.h"
 
 #include <cfloat>
@@ -26,64 +29,94 @@
 namespace h3sk {
 namespace {
 
-constexpr int kStatThreads = 128;   // logical reduction width of the reference
 constexpr int kMaxK = 16384;
 constexpr int kNormK = 5376;        // K of the unsuffixed (reference) entry point
 
 __host__ __device__ constexpr int norm_threads(int k) {
-  return ((k + 1023) / 1024) * 32 < kStatThreads ? kStatThreads : ((k + 1023) / 1024) * 32;
+  return ((k / 64 + 31) / 32) * 32 < 64 ? 64 : ((k / 64 + 31) / 32) * 32;
+}
+__host__ __device__ constexpr int norm_smem(int k) { return (norm_threads(k) / rq::kTeam) * rq::kGroupBytes; }
+
+// Eight consecutive BF16 values of a row as four words (16-byte or 2x8-byte loads).
+__device__ __forceinline__ uint4 load8(const __nv_bfloat16* p, int vec16) {
+  if (vec16) return __ldg(reinterpret_cast<const uint4*>(p));
+  const uint2 a = __ldg(reinterpret_cast<const uint2*>(p)), b = __ldg(reinterpret_cast<const uint2*>(p + 4));
+  return make_uint4(a.x, a.y, b.x, b.y);
 }
 
-template <class T> __device__ __forceinline__ float table_value(const T* p);
-template <> __device__ __forceinline__ float table_value<float>(const float* p) { return *p; }
-template <> __device__ __forceinline__ float table_value<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return bf_bits_to_float(*reinterpret_cast<const unsigned short*>(p));
+// Eight modulation-table values (BF16 or FP32) as four BF16 pair words, each
+// value rounded to BF16 (an identity for BF16 tables).  vec: the eight values
+// start on a 16-byte boundary.
+template <class T> __device__ __forceinline__ uint4 table8(const T* p, int vec);
+template <> __device__ __forceinline__ uint4 table8<__nv_bfloat16>(const __nv_bfloat16* p, int vec) {
+  if (vec) return __ldg(reinterpret_cast<const uint4*>(p));
+  const unsigned short* h = reinterpret_cast<const unsigned short*>(p);
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = uint32_t(__ldg(h + 2 * i)) | (uint32_t(__ldg(h + 2 * i + 1)) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <> __device__ __forceinline__ uint4 table8<float>(const float* p, int vec) {
+  float f[8];
+  if (vec) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p + 4));
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __ldg(p + i);
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = rq::f2_to_bf2(rq::f2_pack(f[2 * i], f[2 * i + 1]));
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <class ModT, bool kDebug>
-__global__ void __launch_bounds__(512) norm_quant_rows(
+__global__ void __launch_bounds__(256) norm_quant_rows(
     const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ W,
     const ModT* __restrict__ Shift, const ModT* __restrict__ Scale,
     const int32_t* __restrict__ Rows, int8_t* __restrict__ Q, float* __restrict__ QScale,
     __nv_bfloat16* __restrict__ DebugNorm, float* __restrict__ DebugRotated,
     float* __restrict__ DebugRstd, int64_t xs, int64_t ss, int64_t cs, float eps, int K,
-    int vec16) {
-  extern __shared__ __align__(16) unsigned char smem_row[];
-  __shared__ float fold[16];
+    int x_vec16, int w_vec16, int t_vec16, int q_vec16) {
+  extern __shared__ __align__(16) float exch[];
+  __shared__ float fold[8];
   __shared__ float row_stat;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nthreads = blockDim.x;
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = X + row * xs;
 
-  // 1. Stage the row in shared memory (coalesced vector loads).
-  if (vec16) {
-    const uint4* src = reinterpret_cast<const uint4*>(xr);
-    uint4* dst = reinterpret_cast<uint4*>(smem_row);
-    for (int i = tid; i < K / 8; i += nthreads) dst[i] = __ldg(src + i);
-  } else {
-    const uint2* src = reinterpret_cast<const uint2*>(xr);
-    uint2* dst = reinterpret_cast<uint2*>(smem_row);
-    for (int i = tid; i < K / 4; i += nthreads) dst[i] = __ldg(src + i);
-  }
-  __syncthreads();
-
-  // 2. Sum of squares in the reference's order.
-  float sum = 0.0f;
-  if (tid < kStatThreads) {
-    const uint2* chunks = reinterpret_cast<const uint2*>(smem_row);
-    for (int i = tid; i < K / 4; i += kStatThreads) {
-      const uint2 raw = chunks[i];
-      const float a = bf_bits_to_float(raw.x & 0xffffu), b = bf_bits_to_float(raw.x >> 16);
-      const float c = bf_bits_to_float(raw.y & 0xffffu), d = bf_bits_to_float(raw.y >> 16);
-      sum = ieee_fma(a, a, sum);
-      sum = ieee_fma(b, b, sum);
-      sum = ieee_fma(c, c, sum);
-      sum = ieee_fma(d, d, sum);
+  // 1. Sum of squares in the reference's order: logical threads tid and tid+64.
+  if (tid < 64) {
+    const uint2* chunks = reinterpret_cast<const uint2*>(xr);
+    const int nchunks = K / 4;
+    uint64_t acc = 0;   // (+0.0f, +0.0f)
+#pragma unroll 4
+    for (int base = 0; base < nchunks; base += 128) {
+      const int c0 = base + tid, c1 = base + tid + 64;
+      const uint2 r0 = c0 < nchunks ? __ldg(chunks + c0) : make_uint2(0, 0);
+      const uint2 r1 = c1 < nchunks ? __ldg(chunks + c1) : make_uint2(0, 0);
+      // element order inside a chunk: r.x low, r.x high, r.y low, r.y high
+      uint64_t e;
+      e = rq::f2_pack(__uint_as_float(r0.x << 16), __uint_as_float(r1.x << 16));
+      acc = rq::f2_fma_ieee(e, e, acc);
+      e = rq::f2_pack(__uint_as_float(r0.x & 0xffff0000u), __uint_as_float(r1.x & 0xffff0000u));
+      acc = rq::f2_fma_ieee(e, e, acc);
+      e = rq::f2_pack(__uint_as_float(r0.y << 16), __uint_as_float(r1.y << 16));
+      acc = rq::f2_fma_ieee(e, e, acc);
+      e = rq::f2_pack(__uint_as_float(r0.y & 0xffff0000u), __uint_as_float(r1.y & 0xffff0000u));
+      acc = rq::f2_fma_ieee(e, e, acc);
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sum = ieee_add(sum, __shfl_down_sync(kFullMask, sum, off));
-    if (lane == 0) fold[warp] = sum;
+    for (int off = 16; off > 0; off >>= 1) {
+      const float lo = __shfl_down_sync(kFullMask, rq::f2_lo(acc), off);
+      const float hi = __shfl_down_sync(kFullMask, rq::f2_hi(acc), off);
+      acc = rq::f2_add_ieee(acc, rq::f2_pack(lo, hi));
+    }
+    if (lane == 0) {
+      fold[warp] = rq::f2_lo(acc);        // logical warp `warp`
+      fold[warp + 2] = rq::f2_hi(acc);    // logical warp `warp + 2`
+    }
   }
   __syncthreads();
   if (tid == 0) {
@@ -93,72 +126,76 @@ __global__ void __launch_bounds__(512) norm_quant_rows(
   __syncthreads();
   const float rrms = hw_rsqrt(ieee_add(row_stat, eps));
 
-  // 3. Normalise and modulate in the ConvRot register layout.
-  const int group = warp * 4 + (lane >> 3), octet = lane & 7;
+  // 2. Normalise and modulate in layout A (64 consecutive values per thread).
+  const int group = tid >> 2, q = tid & 3;
   const bool active = group < K / 256;
-  const int table_row = Rows[row];
-  const ModT* shift_row = Shift + static_cast<int64_t>(table_row) * ss;
-  const ModT* scale_row = Scale + static_cast<int64_t>(table_row) * cs;
+  const int col0 = group * 256 + 64 * q;
   const int64_t out_row = row * K;
-  float v[32];
+  uint64_t v[32];
+  if (active) {
+    const int table_row = Rows[row];
+    const ModT* shift_row = Shift + static_cast<int64_t>(table_row) * ss + col0;
+    const ModT* scale_row = Scale + static_cast<int64_t>(table_row) * cs + col0;
+    const uint64_t rr = rq::f2_pack(rrms, rrms);
+    const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = group * 256 + octet_run_col(octet, j);
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    uint2 wa = make_uint2(0, 0), wb = make_uint2(0, 0);
-    if (active) {
-      xv = *reinterpret_cast<const uint4*>(smem_row + 2 * col);
-      wa = __ldg(reinterpret_cast<const uint2*>(W + col));
-      wb = __ldg(reinterpret_cast<const uint2*>(W + col + 4));
-    }
-    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-    const uint32_t ww[4] = {wa.x, wa.y, wb.x, wb.y};
+    for (int i = 0; i < 8; ++i) {
+      const uint4 xv = load8(xr + col0 + 8 * i, x_vec16);
+      const uint4 wv = load8(W + col0 + 8 * i, w_vec16);
+      const uint4 sv = table8<ModT>(shift_row + 8 * i, t_vec16);
+      const uint4 cv = table8<ModT>(scale_row + 8 * i, t_vec16);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, cw[4] = {cv.x, cv.y, cv.z, cv.w};
+      uint32_t nw[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float n = 0.0f;
-      if (active) {
-        const float x = bf_bits_to_float((xw[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
-        const float w = bf_bits_to_float((ww[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
-        n = bf_round(ieee_mul(w, ieee_mul(rrms, x)));
-        const float sh = bf_round(table_value(shift_row + col + e));
-        const float sc = bf_round(table_value(scale_row + col + e));
-        const float one_plus = bf_round(ieee_add(1.0f, sc));
-        const float prod = bf_round(ieee_mul(n, one_plus));
-        n = bf_round(ieee_add(prod, sh));
-        if constexpr (kDebug) {
-          reinterpret_cast<unsigned short*>(DebugNorm)[out_row + col + e] =
-              static_cast<unsigned short>(float_to_bf_bits(n));
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
+        const uint32_t n = rq::f2_to_bf2(t);
+        const uint32_t one_c = rq::bf2_add(one2, cw[h]);
+        nw[h] = rq::bf2_add(rq::bf2_mul(n, one_c), sw[h]);
+        v[4 * i + h] = rq::bf2_to_f2(nw[h]);
+      }
+      if constexpr (kDebug) {
+        unsigned short* dst = reinterpret_cast<unsigned short*>(DebugNorm) + out_row + col0 + 8 * i;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          dst[2 * h] = static_cast<unsigned short>(nw[h] & 0xffffu);
+          dst[2 * h + 1] = static_cast<unsigned short>(nw[h] >> 16);
         }
       }
-      v[j * 8 + e] = n;
     }
+  } else {
+#pragma unroll
+    for (int p = 0; p < 32; ++p) v[p] = 0;
   }
 
-  // 4. ConvRot256 in registers, row absmax, scale, codes.
-  convrot256_registers(v, lane);
-  float local = 0.0f;
-#pragma unroll
-  for (int r = 0; r < 32; ++r) local = fmaxf(local, fabsf(v[r]));
-  local = warp_allmax(local);
+  // 3. ConvRot256, row absmax, scale, codes.
+  rq::fht_layout_a(v);
+  rq::exchange_a_to_b(v, exch + group * 256, q, group & 1);
+  rq::fht_layout_b(v);
+  const float local = warp_allmax(rq::absmax64(v));
   if (lane == 0) fold[warp] = local;
   __syncthreads();
-  const int nwarps = nthreads >> 5;
-  const float abs_max = warp_allmax(lane < nwarps ? fold[lane] : 0.0f);
-  const float scale = int8_row_scale(abs_max);
+  const int nwarps = blockDim.x >> 5;
+  const float scale = int8_row_scale(warp_allmax(lane < nwarps ? fold[lane] : 0.0f));
   if (tid == 0) {
     QScale[row] = scale;
     if constexpr (kDebug) DebugRstd[row] = rrms;
   }
   if (active) {
+    if constexpr (kDebug) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = group * 256 + octet_run_col(octet, j);
-      if constexpr (kDebug) {
+      for (int j = 0; j < 4; ++j) {
+        float* dst = DebugRotated + out_row + group * 256 + rq::run_col_b(q, j);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) DebugRotated[out_row + col + e] = v[j * 8 + e];
+        for (int h = 0; h < 8; ++h) {
+          dst[2 * h] = rq::f2_lo(v[8 * j + h]);
+          dst[2 * h + 1] = rq::f2_hi(v[8 * j + h]);
+        }
       }
-      *reinterpret_cast<uint2*>(Q + out_row + col) = pack_codes8(&v[j * 8], scale);
     }
+    const float scale_bf = __bfloat162float(__float2bfloat16_rn(scale));
+    rq::store_codes(Q + out_row + group * 256, q, v, scale_bf, q_vec16);
   }
 }
 
@@ -170,7 +207,7 @@ int query_kernel(int k, H3NormQuantResources* out) {
   int active = 0, device = 0, sms = 0, max_threads = 0;
   cudaError_t e = cudaFuncGetAttributes(&a, kernel);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, size_t(k) * 2);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, norm_smem(k));
   if (e != cudaSuccess) return e;
   if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return e;
@@ -201,16 +238,29 @@ int run_checked(const void* x, const void* w, const void* shift, const void* sca
   if (debug && (!dn || !dr || !drs || (uintptr_t(dn) & 1u) || (uintptr_t(dr) & 3u) || (uintptr_t(drs) & 3u)))
     return cudaErrorInvalidValue;
   if (!debug && (dn || dr || drs)) return cudaErrorInvalidValue;
-  const int vec16 = ((uintptr_t(x) & 15u) == 0 && (xs % 8) == 0) ? 1 : 0;
+  const int x_vec16 = ((uintptr_t(x) & 15u) == 0 && (xs % 8) == 0) ? 1 : 0;
+  const int w_vec16 = (uintptr_t(w) & 15u) == 0 ? 1 : 0;
+  const int q_vec16 = (uintptr_t(q) & 15u) == 0 ? 1 : 0;
+  const int64_t tsz = table_dtype ? 2 : 4;
+  const int t_vec16 = ((uintptr_t(shift) & 15u) == 0 && (uintptr_t(scale) & 15u) == 0 && (ss * tsz) % 16 == 0 &&
+                       (cs * tsz) % 16 == 0) ? 1 : 0;
   const int threads = norm_threads(int(k));
-  const size_t smem = size_t(k) * 2;
+  const int smem = norm_smem(int(k));
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
-#define H3SK_NQ_LAUNCH(T, D)                                                                      \
-  norm_quant_rows<T, D><<<dim3(unsigned(m)), threads, smem, stream>>>(                            \
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),               \
-      static_cast<const T*>(shift), static_cast<const T*>(scale), static_cast<const int32_t*>(rows), \
-      static_cast<int8_t*>(q), static_cast<float*>(qscale), static_cast<__nv_bfloat16*>(dn),     \
-      static_cast<float*>(dr), static_cast<float*>(drs), xs, ss, cs, eps, int(k), vec16)
+#define H3SK_NQ_LAUNCH(T, D)                                                                       \
+  do {                                                                                             \
+    auto kernel = norm_quant_rows<T, D>;                                                           \
+    if (smem > 48 * 1024) {                                                                        \
+      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+      if (e != cudaSuccess) return e;                                                              \
+    }                                                                                              \
+    kernel<<<dim3(unsigned(m)), threads, smem, stream>>>(                                          \
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),               \
+        static_cast<const T*>(shift), static_cast<const T*>(scale), static_cast<const int32_t*>(rows), \
+        static_cast<int8_t*>(q), static_cast<float*>(qscale), static_cast<__nv_bfloat16*>(dn),     \
+        static_cast<float*>(dr), static_cast<float*>(drs), xs, ss, cs, eps, int(k), x_vec16, w_vec16, \
+        t_vec16, q_vec16);                                                                                  \
+  } while (0)
   if (table_dtype == 0) {
     if (debug) H3SK_NQ_LAUNCH(float, true); else H3SK_NQ_LAUNCH(float, false);
   } else {

@@ -52,7 +52,7 @@ def up_to_date() -> bool:
     lib = NATIVE / LIB_NAME
     if not lib.exists() or not (NATIVE / "build.json").exists():
         return False
-    newest = max(p.stat().st_mtime for p in list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh"))
+    newest = max(p.stat().st_mtime for p in list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
                  + [PKG.parent / "include" / "h3sk_b200.h", Path(__file__)])
     return lib.stat().st_mtime >= newest
 

@@ -1,0 +1,50 @@
+// Host-side launch helpers shared by the row-quantiser translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+namespace h3sk {
+
+// Device address of the library's pipeline status word on the current device
+// (defined with the GEMM); bounded waits that run out record their code there.
+int* status_device_ptr();
+
+// Grid of a persistent kernel: as many CTAs as fit on the device at once
+// (occupancy x SM count, computed once per kernel, device, block and smem size),
+// but no more than `work_ctas`.  Also opts the kernel into `smem` bytes of
+// dynamic shared memory when that exceeds the 48 KB default.
+inline cudaError_t rq_persistent_grid(const void* kernel, int threads, int smem, int64_t work_ctas, int* grid) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int, int>, int> resident;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_tuple(kernel, device, threads, smem);
+  int capacity = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = resident.find(key);
+    if (it == resident.end()) {
+      if (smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+      }
+      int per_sm = 0, sms = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+      if (e != cudaSuccess) return e;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      if (e != cudaSuccess) return e;
+      if (per_sm < 1) return cudaErrorInvalidConfiguration;
+      it = resident.emplace(key, per_sm * sms).first;
+    }
+    capacity = it->second;
+  }
+  *grid = int(work_ctas < capacity ? work_ctas : capacity);
+  return cudaSuccess;
+}
+
+}  // namespace h3sk

@@ -9,7 +9,8 @@
 //               issues tcgen05.mma.kind::i8 (M=128, N=256, K=32; four per
 //               stage) from one thread; tcgen05.commit frees each smem stage and
 //               publishes each finished accumulator.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, dequantise, apply the
+//   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column half
+//               (w - 2) / 4, 32 columns per tcgen05.ld; dequantise, apply the
 //               fused epilogue (bias, GELU, gate-residual, raw int32) and store.
 //               The second accumulator lets the epilogue of tile t overlap the
 //               mainloop of tile t+1.
@@ -55,8 +56,9 @@ constexpr int kUmmaK = 32;          // K of one kind::i8 MMA
 constexpr int kATileBytes = kBM * kBK;
 constexpr int kBTileBytes = kBN * kBK;
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
-constexpr int kThreads = 192;
-constexpr int kEpilogueThreads = 128;
+constexpr int kEpilogueWarps = 8;    // two per TMEM lane quarter, one per column half
+constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
+constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
 constexpr int kGroupM = 16;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
@@ -72,7 +74,9 @@ struct SmemLayout {
   static constexpr int nbars = 2 * kStages + 5;
   static constexpr int misc = bars + nbars * 8;                  // tmem slot, abort flag
   static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float
-  static constexpr int total = colv + 2 * kBN * 4;
+  static constexpr int stage = ((colv + 2 * kBN * 4) + 1023) / 1024 * 1024;   // per-warp output staging
+  static constexpr int stage_warp_bytes = 32 * 32 * 2;           // 32 rows x 32 BF16 columns
+  static constexpr int total = stage + kEpilogueWarps * stage_warp_bytes;
   static constexpr int dynamic_bytes = total + 1024;             // slack for 1024 alignment
 };
 
@@ -112,10 +116,11 @@ __device__ __forceinline__ float gelu_tanh_precise(float v) {
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// Two FP32 values -> one word of two BF16 (round to nearest even), low half = lo.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-  return a | (b << 16);
+  uint32_t w;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
+  return w;
 }
 
 // Named barrier among the four epilogue warps only.
@@ -123,62 +128,53 @@ __device__ __forceinline__ void epilogue_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
 }
 
-// Epilogue of 32 consecutive accumulators of one row: columns [col0, col0+32),
-// tile-local chunk c.  Columns are stored in groups of 8 (N % 8 == 0).
+// Raw int32 accumulators of one row, columns [col0, col0+32) (debug epilogue).
+__device__ __forceinline__ void store_chunk_acc(const GemmParams& p, const uint32_t (&r)[32], int row, int col0) {
+  int32_t* out = reinterpret_cast<int32_t*>(p.d) + int64_t(row) * p.ldd + col0;
+#pragma unroll
+  for (int v = 0; v < 8; ++v)
+    if (col0 + 4 * v < p.n)
+      reinterpret_cast<int4*>(out)[v] = make_int4(int(r[4 * v]), int(r[4 * v + 1]), int(r[4 * v + 2]), int(r[4 * v + 3]));
+}
+
+// BF16 epilogue values of 32 consecutive accumulators of one row (columns
+// [col0, col0+32), tile-local chunk c) as 16 packed words.  Rows >= M and
+// columns >= N produce unused values and read no memory.
 template <int kEpi>
-__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row, int col0, int c,
-                                            float xs_row, const __nv_bfloat16* gate_row, const float* col_ws,
-                                            const float* col_bias) {
-  if constexpr (kEpi == kEpiAcc) {
-    int32_t* out = reinterpret_cast<int32_t*>(p.d) + int64_t(row) * p.ldd + col0;
+__device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t (&r)[32], bool row_ok, int row,
+                                             int col0, int c, float xs_row, const __nv_bfloat16* gate_row,
+                                             const float* col_ws, const float* col_bias, uint32_t (&packed)[16]) {
 #pragma unroll
-    for (int v = 0; v < 8; ++v)
-      if (col0 + 4 * v < p.n)
-        reinterpret_cast<int4*>(out)[v] =
-            make_int4(int(r[4 * v]), int(r[4 * v + 1]), int(r[4 * v + 2]), int(r[4 * v + 3]));
-  } else {
-    uint32_t packed[16];
+  for (int i = 0; i < 32; i += 2) {
+    float y2[2];
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      float y2[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int cc = c * 32 + i + h;
-        const float a = __int2float_rn(int(r[i + h]));
-        const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, xs_row), col_ws[cc]), col_bias[cc]);
-        y2[h] = __bfloat162float(__float2bfloat16_rn(y));
-        if constexpr (kEpi == kEpiGelu) y2[h] = gelu_tanh_precise(y2[h]);
-      }
-      packed[i / 2] = pack_bf2(y2[0], y2[1]);
+    for (int h = 0; h < 2; ++h) {
+      const int cc = c * 32 + i + h;
+      const float a = __int2float_rn(int(r[i + h]));
+      y2[h] = __fadd_rn(__fmul_rn(__fmul_rn(a, xs_row), col_ws[cc]), col_bias[cc]);
     }
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.d) + int64_t(row) * p.ldd + col0;
-    if constexpr (kEpi == kEpiGate) {
-      // D may alias the residual: each element is read before it is written, by this thread.
-      const __nv_bfloat16* res = p.residual + int64_t(row) * p.ldr + col0;
-      const __nv_bfloat16* gat = gate_row + col0;
+    packed[i / 2] = pack_bf2(y2[0], y2[1]);
+    if constexpr (kEpi == kEpiGelu)
+      packed[i / 2] = pack_bf2(gelu_tanh_precise(bf_lo(packed[i / 2])), gelu_tanh_precise(bf_hi(packed[i / 2])));
+  }
+  if constexpr (kEpi == kEpiGate) {
+    // D may alias the residual: every element is read here, before its store is issued.
+    const __nv_bfloat16* res = p.residual + int64_t(row) * p.ldr + col0;
+    const __nv_bfloat16* gat = gate_row + col0;
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        if (col0 + 8 * v >= p.n) break;
-        const uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * v);
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gat + 8 * v));
-        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-        uint32_t o[4];
+    for (int v = 0; v < 4; ++v) {
+      if (!row_ok || col0 + 8 * v >= p.n) continue;
+      const uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * v);
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gat + 8 * v));
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t yw = packed[4 * v + w];
-          const float lo = __fmaf_rn(bf_lo(yw), bf_lo(gw[w]), bf_lo(rw[w]));
-          const float hi = __fmaf_rn(bf_hi(yw), bf_hi(gw[w]), bf_hi(rw[w]));
-          o[w] = pack_bf2(lo, hi);
-        }
-        reinterpret_cast<uint4*>(out)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t yw = packed[4 * v + w];
+        const float lo = __fmaf_rn(bf_lo(yw), bf_lo(gw[w]), bf_lo(rw[w]));
+        const float hi = __fmaf_rn(bf_hi(yw), bf_hi(gw[w]), bf_hi(rw[w]));
+        packed[4 * v + w] = pack_bf2(lo, hi);
       }
-    } else {
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        if (col0 + 8 * v < p.n)
-          reinterpret_cast<uint4*>(out)[v] =
-              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
     }
   }
 }
@@ -186,7 +182,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
 template <int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                         const GemmParams p) {
+                         const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem + SmemLayout::a;
@@ -219,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    if (kEpi != kEpiAcc) tma_prefetch_map(&map_d);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -333,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue ----------------
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int ep_tid = threadIdx.x - 64;     // 0..127
+    const int half = (warp - 2) >> 2;        // column half of the tile
+    const int ep_tid = threadIdx.x - 64;     // 0..255
+    uint8_t* stage = smem + SmemLayout::stage + (warp - 2) * SmemLayout::stage_warp_bytes;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
@@ -355,24 +354,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       epilogue_sync();
       if (*ready == 0) break;
       tc_fence_after();
-      const int row = mt * kBM + quarter * 32 + lane;
+      const int row_base = mt * kBM + quarter * 32;
+      const int row = row_base + lane;
       const bool row_ok = row < p.m;
       const float xs_row = (kEpi != kEpiAcc && row_ok) ? p.xs[row] : 0.0f;
       const __nv_bfloat16* gate_row = nullptr;
       if (kEpi == kEpiGate && row_ok) gate_row = p.gate + int64_t(p.rows[row]) * p.gate_ld;
       const uint32_t t_row = tmem_base + uint32_t(acc * kBN) + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
         uint32_t r[32];
         __syncwarp();
         tmem_load_32cols(t_row + uint32_t(c * 32), r);
         tmem_load_wait();
-        if (c == kBN / 32 - 1) {
+        if (c == (half + 1) * (kBN / 64) - 1) {
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
         const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.n) store_chunk<kEpi>(p, r, row, col0, c, xs_row, gate_row, col_ws, col_bias);
+        if constexpr (kEpi == kEpiAcc) {
+          if (row_ok && col0 < p.n) store_chunk_acc(p, r, row, col0);
+        } else if (col0 < p.n && row_base < p.m) {
+          // BF16 chunk: 32 rows x 32 columns through this warp's staging buffer and
+          // one TMA tensor store (rows >= M and columns >= N are clipped by TMA).
+          uint32_t packed[16];
+          chunk_values<kEpi>(p, r, row_ok, row, col0, c, xs_row, gate_row, col_ws, col_bias, packed);
+          if (lane == 0) bulk_wait_read_all();    // the previous store has read the buffer
+          __syncwarp();
+          // 64-byte swizzle: 16-byte chunk v of row i sits at chunk v ^ ((i >> 1) & 3)
+          uint8_t* srow = stage + lane * 64;
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(srow + ((v ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_d, stage, col0, row_base);
+            bulk_commit();
+          }
+        }
       }
       __syncwarp();
       if (++acc == 2) {
@@ -380,6 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_all();   // every output store has completed
+    __syncwarp();
   }
 
   __syncthreads();
@@ -489,6 +512,21 @@ bool make_operand_map(CUtensorMap* map, const void* base, int rows, int k, int b
   return r == CUDA_SUCCESS;
 }
 
+// BF16 output [rows, cols] with row stride ld elements, stored in 32 x 32 boxes
+// from a 64-byte-swizzled staging buffer.
+bool make_output_map(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   int sms = 0;
   bool attrs_set[4] = {false, false, false, false};
@@ -510,7 +548,8 @@ int* status_ptr() {
 }
 
 template <int kEpi>
-cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, GemmParams p,
+                        cudaStream_t stream) {
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
@@ -524,7 +563,7 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams
   p.status = status_ptr();
   if (!p.status) return cudaErrorInvalidSymbol;
   const int grid = p.tiles < info.sms ? p.tiles : info.sms;
-  kernel<<<grid, kThreads, SmemLayout::dynamic_bytes, stream>>>(ma, mb, p);
+  kernel<<<grid, kThreads, SmemLayout::dynamic_bytes, stream>>>(ma, mb, md, p);
   return cudaGetLastError();
 }
 
@@ -543,9 +582,12 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
         (uintptr_t(rows) & 3u))
       return fail(cudaErrorInvalidValue, "h3_int8_gate: gate/rows/residual null or misaligned");
   }
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, md;
   if (!make_operand_map(&ma, A, M, K, kBM) || !make_operand_map(&mb, B, N, K, kBN))
     return fail(cudaErrorInvalidValue, "h3_int8: tensor map encoding failed");
+  std::memset(&md, 0, sizeof(md));
+  if (epi != kEpiAcc && !make_output_map(&md, D, M, N, ldd))
+    return fail(cudaErrorInvalidValue, "h3_int8: output tensor map encoding failed");
   GemmParams p{};
   p.xs = xs;
   p.ws = ws;
@@ -567,10 +609,10 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
   switch (epi) {
-    case kEpiDequant: e = launch_gemm<kEpiDequant>(ma, mb, p, stream); break;
-    case kEpiGelu: e = launch_gemm<kEpiGelu>(ma, mb, p, stream); break;
-    case kEpiGate: e = launch_gemm<kEpiGate>(ma, mb, p, stream); break;
-    default: e = launch_gemm<kEpiAcc>(ma, mb, p, stream); break;
+    case kEpiDequant: e = launch_gemm<kEpiDequant>(ma, mb, md, p, stream); break;
+    case kEpiGelu: e = launch_gemm<kEpiGelu>(ma, mb, md, p, stream); break;
+    case kEpiGate: e = launch_gemm<kEpiGate>(ma, mb, md, p, stream); break;
+    default: e = launch_gemm<kEpiAcc>(ma, mb, md, p, stream); break;
   }
   if (e != cudaSuccess) return fail(e, "h3_int8: launch failed");
   t_last_error = 0;
@@ -579,6 +621,9 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
 }
 
 }  // namespace
+
+int* status_device_ptr() { return status_ptr(); }
+
 }  // namespace h3sk
 
 #define H3SK_EXPORT extern "C" __attribute__((visibility("default")))

@@ -1,0 +1,261 @@
+"""Model-scoped B200 backend of the quantized DiT-block linear path.
+
+Mirror of h3_speedkit/runtime.py of H3 SpeedKit for this path: the same class
+and function names (``Unsupported``, ``Backend``, ``ModelPatch``,
+``patch_model``), the same install flow (clone, explicit block replacements, a
+request wrapper, first-use exact verification, fallback to the original block
+on ``Unsupported``) and the same error behaviour (checks raise before any
+mutation; a launch failure aborts the request, never retried).  Differences:
+
+* the kernels are the sm_100a library (capability 10.0 instead of 12.0), one
+  ``libh3sk_b200.so`` published under the reference's library names and checked
+  against ``_native/build.json`` (same manifest schema);
+* the hidden width K is generic (the reference fixes 5376);
+* attention is not part of this path: ``Backend.block`` takes an ``attention``
+  callable on the BF16 Q/K/V slices of the QKV output (identity on V in the
+  benchmark configuration).  ``patch_model`` installs replacements only with an
+  attention provider; without one it raises ``Unsupported`` and the model stays
+  unpatched.
+
+ComfyUI and comfy-kitchen are imported lazily, only on the model-patching path.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import hashlib
+import json
+import logging
+import threading
+from collections import Counter
+from contextvars import ContextVar
+from pathlib import Path
+
+import torch
+
+from . import _lib
+from .ops.convrot import ConvRotRegister, quantize_int8_rowwise_convrot64
+from .ops.gemm import int8_linear
+from .ops.norm_quant import DEVICE_CAPABILITY, NormQuant
+
+LOG = logging.getLogger(__name__)
+KEY = "h3_speedkit_b200"
+LIBRARY_NAMES = ("norm", "convrot", "fc1", "gate")
+BLOCKS = 50
+
+
+class Unsupported(ValueError):
+    """A contract failed before any in-place model output was changed."""
+
+
+def verify_manifest(directory: Path) -> dict:
+    """Every library name must match its build.json SHA-256 (runtime.py:49-53)."""
+    build = json.loads((directory / "build.json").read_text())
+    for name in LIBRARY_NAMES:
+        path = directory / (name + ".so")
+        if not path.exists():
+            raise Unsupported("Missing kernel library: " + name)
+        if hashlib.sha256(path.read_bytes()).hexdigest() != build["kernels"][name]["sha256"]:
+            raise Unsupported("Kernel differs from its build manifest: " + name)
+    return build
+
+
+def segment_rows(segments, tokens: int, table_rows: int, device) -> torch.Tensor:
+    """Int32 per-token modulation row map from contiguous (start, stop, row)
+    segments (runtime.py:278-291); validated before any GPU work."""
+    cursor = 0
+    for start, stop, row in segments:
+        if (type(start) is not int or type(stop) is not int or type(row) is not int or start != cursor
+                or stop < start or not 0 <= row < table_rows):
+            raise Unsupported("Only contiguous integer modulation segments are qualified")
+        cursor = stop
+    if cursor != tokens:
+        raise Unsupported("Incomplete modulation row map")
+    rows = torch.empty((tokens,), dtype=torch.int32, device=device)
+    for start, stop, row in segments:
+        rows[start:stop].fill_(row)
+    return rows
+
+
+class Backend:
+    def __init__(self, directory=None, *, require_device=True):
+        self.directory = Path(directory) if directory else _lib.NATIVE
+        if require_device and (not torch.cuda.is_available()
+                               or torch.cuda.get_device_capability() != DEVICE_CAPABILITY):
+            raise Unsupported("This build requires a B200 (sm_100) GPU")
+        self.build = verify_manifest(self.directory)
+        self.lib = _lib.load(self.directory / _lib.LIB_NAME)
+        self.norm = NormQuant(self.directory / _lib.LIB_NAME)
+        self.convrot = ConvRotRegister(self.directory / _lib.LIB_NAME)
+        self.fc1 = self.lib.h3_int8          # reference names: runtime.py:62-66
+        self.gate = self.lib.h3_int8_gate
+
+    @staticmethod
+    def check(code):
+        if code != 1:
+            raise RuntimeError("SpeedKit GEMM failed; the request is aborted, never retried after mutation")
+
+    @staticmethod
+    def touch(*operands):
+        stream = torch.cuda.current_stream(operands[0].device)
+        for tensor in operands:
+            tensor.record_stream(stream)
+        return stream.cuda_stream
+
+    @staticmethod
+    def plain_weight(module, x):
+        """INT8 weight [N, K] and FP32 per-channel scale [N] of a linear module:
+        comfy-kitchen QuantizedTensor weights (runtime.py:97-107) or a module that
+        carries ``weight_int8`` / ``weight_scale`` tensors."""
+        weight = module.weight
+        if hasattr(module, "weight_int8"):
+            w, scale = module.weight_int8, module.weight_scale
+        else:
+            from comfy_kitchen.tensor.int8 import TensorWiseINT8Layout
+            w, scale = TensorWiseINT8Layout.get_plain_tensors(weight)
+        w = w.to(device=x.device).contiguous()
+        scale = scale.to(device=x.device, dtype=torch.float32).contiguous().view(-1)
+        if w.dtype != torch.int8 or scale.numel() != w.shape[0]:
+            raise RuntimeError("Unexpected cast weight layout")
+        return w, scale
+
+    def normalize(self, module, x, shift, scale, rows):
+        weight = module.weight.to(device=x.device).detach()
+        q = torch.empty(x.shape, device=x.device, dtype=torch.int8)
+        qs = torch.empty((len(x), 1), device=x.device, dtype=torch.float32)
+        self.norm.bind(x, weight, shift, scale, rows, q, qs, eps=module.eps, check_values=False)()
+        return q, qs
+
+    def gate_projection(self, linear, q, qs, x, gate, rows, skip=0):
+        w, ws = self.plain_weight(linear, x)
+        g = gate.to(dtype=torch.bfloat16).contiguous()
+        operands = (q[skip:], w, qs[skip:], ws, x[skip:], g, rows[skip:], x[skip:])
+        st = self.touch(*operands)
+        self.check(self.gate(*(t.data_ptr() for t in operands), len(x) - skip, x.shape[1], w.shape[1], 13, st))
+        torch.autograd.graph.increment_version(x)
+
+    def block(self, block, x, t_emb, segments, rope=None, *, rows, skip=0, counts=None, attention=None,
+              mlp_act="gelu_tanh"):
+        """One block of the linear path on BF16 tokens x [M, D], updated in place
+        (runtime.py:126-164).  attention(q, k, v) -> [M, D_attn] BF16; None is the
+        identity on V.  mlp_act: 'gelu_tanh' (FC1 epilogue, the benchmark
+        configuration) or 'swiglu' (the H3 geometry: FC1 rows are [gate | up])."""
+        counts = Counter() if counts is None else counts
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = block.adaln_proj(t_emb)
+        qi, qs = self.normalize(block.norm1, x, shift_msa, scale_msa, rows)
+        w, ws = self.plain_weight(block.attn.qkv_proj, x)
+        qkv = int8_linear(qi, w, qs, ws)
+        width = qkv.shape[1] // 3
+        q_, k_, v_ = qkv[:, :width], qkv[:, width:2 * width], qkv[:, 2 * width:]
+        attn = v_ if attention is None else attention(q_, k_, v_)
+        aq, asc = quantize_int8_rowwise_convrot64(attn)
+        self.gate_projection(block.attn.out_proj, aq, asc, x, gate_msa, rows, skip)
+        qi, qs = self.normalize(block.norm2, x, shift_mlp, scale_mlp, rows)
+        w1, ws1 = self.plain_weight(block.mlp.fc1, x)
+        if mlp_act == "swiglu":
+            hidden = int8_linear(qi, w1, qs, ws1)
+            fq, fs = quantize_int8_rowwise_convrot64(hidden, 256, input_act="swiglu")
+        else:
+            hidden = int8_linear(qi, w1, qs, ws1, gelu=True)
+            fq, fs = quantize_int8_rowwise_convrot64(hidden)
+        self.gate_projection(block.mlp.fc2, fq, fs, x, gate_mlp, rows, skip)
+        counts.update(qkv=1, attention=1, norm_quant=2, fc1=1, gate=2)
+        return x
+
+
+class ModelPatch:
+    """Request wrapper + block replacements (runtime.py:167-308)."""
+
+    def __init__(self, model, backend, verify_new_shapes=True, attention=None, blocks=BLOCKS):
+        self.model = model
+        self.backend = backend
+        self.attention = attention
+        self.blocks = blocks
+        self.context = ContextVar("speedkit_b200_request", default=None)
+        self.lock = threading.RLock()
+        self.last_report = {}
+        self.warned = set()
+        self.verify_new_shapes = verify_new_shapes
+        self.verified_shapes = Counter()
+        self.rejected_shapes = set()
+
+    def preflight(self, args, kwargs):
+        if torch.is_grad_enabled():
+            raise Unsupported("Eager inference only")
+        x = args[0][0] if args and isinstance(args[0], (list, tuple)) else (args[0] if args else None)
+        if x is None or not x.is_cuda or torch.cuda.get_device_capability(x.device) != DEVICE_CAPABILITY:
+            raise Unsupported("B200 GPU required")
+        if self.attention is None:
+            raise Unsupported("No attention provider for the B200 linear path")
+        tokens = int(x.shape[-2]) if x.ndim >= 2 else 0
+        return {"skip": 0, "rows": None, "row_key": None, "counts": Counter(), "tokens": tokens,
+                "shape_key": (tokens, 0), "verify": self.verified_shapes[(tokens, 0)] < 8 and self.verify_new_shapes}
+
+    def wrapper(self, executor, *args, **kwargs):
+        with self.lock:
+            try:
+                frame = self.preflight(args, kwargs)
+            except Unsupported as error:
+                reason = str(error)
+                if reason not in self.warned:
+                    LOG.warning("H3 SpeedKit fallback: %s", reason)
+                    self.warned.add(reason)
+                frame = {"fallback": reason}
+            token = self.context.set(frame)
+            try:
+                result = executor(*args, **kwargs)
+                if "fallback" not in frame and frame["counts"]["attention"] != self.blocks:
+                    raise RuntimeError("Incomplete SpeedKit block coverage")
+                if frame.get("verify") and "verification_failed" not in frame:
+                    self.verified_shapes[frame["shape_key"]] += 1
+                self.last_report = {k: dict(v) if isinstance(v, Counter) else v for k, v in frame.items()
+                                    if k not in ("rows", "row_key")}
+                return result
+            finally:
+                self.context.reset(token)
+
+    def replacement(self, index):
+        def run(inputs, extra):
+            frame = self.context.get()
+            if frame is None or "fallback" in frame or "verification_failed" in frame:
+                return extra["original_block"](inputs)
+            x, segments = inputs["img"], inputs["mod_segments"]
+            if x.dtype != torch.bfloat16 or not x.is_contiguous():
+                raise RuntimeError("Hidden activation changed after preflight")
+            key = tuple(segments)
+            if frame["row_key"] != key:
+                frame["rows"] = segment_rows(segments, len(x), inputs["t_emb"].shape[0] * 3, x.device)
+                frame["row_key"] = key
+            work = x.clone() if frame["verify"] else x
+            reference = extra["original_block"](inputs)["img"] if frame["verify"] else None
+            output = self.backend.block(self.model.blocks[index], work, inputs["t_emb"], segments,
+                                        inputs.get("rope_freqs"), rows=frame["rows"], skip=0,
+                                        counts=frame["counts"], attention=self.attention)
+            if reference is not None and not torch.equal(output, reference):
+                self.rejected_shapes.add(frame["shape_key"])
+                frame["verification_failed"] = index
+                frame["fallback"] = "Exact layout verification failed at block " + str(index)
+                LOG.warning("H3 SpeedKit: %s; using reference", frame["fallback"])
+                return {"img": reference}
+            return {"img": output}
+        return run
+
+
+def patch_model(model, directory=None, *, release_embeddings=True, verify_new_shapes=True, attention=None,
+                backend=None):
+    """Return a Comfy clone with explicit block replacements and a request
+    wrapper (runtime.py:311-338).  The original model is not modified."""
+    import comfy.patcher_extension as pe
+    if attention is None:
+        raise Unsupported("The B200 linear path needs an attention provider (attention is outside this path)")
+    clone = model.clone()
+    options = clone.model_options.setdefault("transformer_options", {})
+    existing = options.get("patches_replace", {}).get("dit", {})
+    if any(("double_block", i) in existing for i in range(BLOCKS)):
+        raise Unsupported("A DiT block replacement is already installed; start from the unpatched MODEL output")
+    patch = ModelPatch(model.model.diffusion_model, backend or Backend(directory), verify_new_shapes, attention)
+    for index in range(BLOCKS):
+        clone.set_model_patch_replace(patch.replacement(index), "dit", "double_block", index)
+    pe.add_wrapper_with_key(pe.WrappersMP.DIFFUSION_MODEL, KEY, patch.wrapper,
+                            clone.model_options["transformer_options"])
+    clone._h3_speedkit = patch
+    return clone

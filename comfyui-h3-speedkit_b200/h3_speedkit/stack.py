@@ -46,6 +46,18 @@ def shard_bounds(total: int, world: int, rank: int) -> tuple[int, int]:
     return start, min(total, start + per)
 
 
+def gather_shards(send: torch.Tensor, out: torch.Tensor, total: int, group=None) -> torch.Tensor:
+    """Assemble the token-sharded output: every rank contributes its padded shard
+    ``send`` [ceil(total/world), D]; ``out`` [world * ceil(total/world), D]
+    receives all of them in rank order (one all_gather_into_tensor); the first
+    ``total`` rows are returned."""
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return send[:total]
+    dist.all_gather_into_tensor(out, send, group=group)
+    return out[:total]
+
+
 @dataclass
 class Workspace:
     """Per-shard activation buffers, sized once for m rows."""
@@ -214,10 +226,7 @@ class ShardedStack:
             self.local.run(events)
 
     def gather(self) -> torch.Tensor:
-        if self.world == 1:
-            return self.send[: self.total]
-        self.dist.all_gather_into_tensor(self.out, self.send, group=self.group)
-        return self.out[: self.total]
+        return gather_shards(self.send, self.out, self.total, self.group)
 
     def forward(self, events=None) -> torch.Tensor:
         self.forward_local(events)

@@ -19,6 +19,16 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 device (sm_100a)")
 
 
+def pytest_sessionstart(session):
+    """Build the kernel library and the oracles if they are missing or stale
+    (no-op when up to date; nvcc and gcc are present on both hosts)."""
+    sys.path.insert(0, str(PKG_DIR / "csrc"))
+    import build as kernel_build
+    kernel_build.build(force=False)
+    from oracle import build as oracle_build
+    oracle_build.build()
+
+
 @pytest.fixture(scope="session")
 def device():
     import torch

@@ -1,0 +1,83 @@
+"""Generate the golden fixtures from the reference's own CUDA kernels.
+
+Run on a B200 box from the repository root after ``oracle/build.py`` has built
+``oracle/_ref`` (the reference's norm_quant.cu, convrot_register_v2.cu and the
+vendored Kitchen quantiser, compiled from the reference sources):
+
+    python tests/golden/make_golden.py
+
+Inputs are seeded CPU draws; every fixture stores the inputs (BF16 as uint16
+bits) and the reference kernel's outputs.  The CPU oracle is pinned against
+these files by tests/test_golden.py; the CUDA kernels by tests/test_gpu_golden.py.
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path[:0] = [str(ROOT)]
+
+from oracle import ref_gpu  # noqa: E402
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def norm_case(name, k, m, tables, table_dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((m, k), generator=g)
+    x[:, torch.randperm(k, generator=g)[:16]] *= 20.0
+    x = x.to(torch.bfloat16)
+    w = (torch.rand((k,), generator=g) + 0.5).to(torch.bfloat16)
+    shift = (torch.randn((tables, k), generator=g) * 0.1).to(table_dtype)
+    scale = (torch.randn((tables, k), generator=g) * 0.1).to(table_dtype)
+    rows = torch.randint(0, tables, (m,), generator=g, dtype=torch.int32)
+    dev = torch.device("cuda")
+    q, qs, dn, _, drs = ref_gpu.norm_quant(x.to(dev), w.to(dev), shift.to(dev), scale.to(dev), rows.to(dev), 1e-6,
+                                           debug=True)
+    torch.cuda.synchronize()
+    tab = (lambda t: bits(t)) if table_dtype == torch.bfloat16 else (lambda t: t.numpy())
+    np.savez_compressed(HERE / f"{name}.npz", kind="norm_quant", k=k, eps=np.float32(1e-6), x=bits(x), w=bits(w),
+                        shift=tab(shift), scale=tab(scale), rows=rows.numpy(), q=q.cpu().numpy(),
+                        qscale=qs.cpu().numpy().reshape(-1), norm=bits(dn), rstd=drs.cpu().numpy())
+
+
+def convrot_case(name, k, m, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn((m, k), generator=g) * 3).to(torch.bfloat16)
+    q, sc, _ = ref_gpu.convrot_register(x.cuda(), mode=0)
+    torch.cuda.synchronize()
+    np.savez_compressed(HERE / f"{name}.npz", kind="convrot_register", k=k, act=0, x=bits(x), q=q.cpu().numpy(),
+                        scale=sc.cpu().numpy().reshape(-1))
+
+
+def kitchen_case(name, k, m, act, seed):
+    g = torch.Generator().manual_seed(seed)
+    width = 2 * k if act == 2 else k
+    x = (torch.randn((m, width), generator=g) * 2).to(torch.bfloat16)
+    q, sc = ref_gpu.kitchen_quant(x.cuda(), act)
+    torch.cuda.synchronize()
+    np.savez_compressed(HERE / f"{name}.npz", kind="kitchen_quant", k=k, act=act, x=bits(x), q=q.cpu().numpy(),
+                        scale=sc.cpu().numpy().reshape(-1))
+
+
+def main():
+    norm_case("norm_k4096_bf16", 4096, 8, 2, torch.bfloat16, 101)
+    norm_case("norm_k5376_f32", 5376, 6, 3, torch.float32, 102)
+    norm_case("norm_k2048_bf16", 2048, 8, 1, torch.bfloat16, 103)
+    convrot_case("convrot_k5376", 5376, 6, 104)
+    convrot_case("convrot_k7168", 7168, 4, 105)
+    kitchen_case("kitchen_k4096_none", 4096, 8, 0, 106)
+    kitchen_case("kitchen_k4096_gelu", 4096, 8, 1, 107)
+    kitchen_case("kitchen_k2048_swiglu", 2048, 8, 2, 108)
+    print("golden fixtures:", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,55 @@
+"""Pin the CPU oracle to golden vectors produced by the reference's own CUDA
+kernels (tests/golden/make_golden.py; norm_quant.cu, convrot_register_v2.cu and
+the vendored Kitchen quantiser compiled from the reference sources).
+
+Exact: the normalised/modulated BF16 values (with the reference's rrms, which
+comes from the hardware rsqrt.approx), the ConvRot row scales, and codes except
+where the reference's fast division lands a quotient on the other side of a
+BF16 rounding tie (at most 1 code, at a rate below 1e-3).  GELU-tanh/SwiGLU
+inputs go through the device tanhf/expf, so their scales are compared to 1e-6
+relative and their codes by the same +-1 rule.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import assert_codes_close
+from oracle import cpu as ocpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz"))
+
+
+def load(name):
+    return dict(np.load(GOLDEN / f"{name}.npz"))
+
+
+def test_fixtures_present():
+    assert len(CASES) >= 8
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c.startswith("norm_")])
+def test_oracle_prologue_matches_reference_kernel(name):
+    g = load(name)
+    q, qs, norm, _, _ = ocpu.norm_quant(g["x"], g["w"], g["shift"], g["scale"], g["rows"], float(g["eps"]),
+                                        rrms=g["rstd"], debug=True)
+    assert np.array_equal(norm, g["norm"]), "normalised/modulated BF16 values"
+    assert np.array_equal(qs, g["qscale"]), "row scales"
+    assert_codes_close(q, g["q"], 1e-3, name)
+    # without the injected rrms: 1/sqrt in double stands in for rsqrt.approx
+    _, _, _, _, rstd = ocpu.norm_quant(g["x"], g["w"], g["shift"], g["scale"], g["rows"], float(g["eps"]),
+                                       debug=True)
+    ulps = np.abs(rstd.view(np.int32).astype(np.int64) - g["rstd"].view(np.int32).astype(np.int64))
+    assert ulps.max() <= 2
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c.startswith(("convrot_", "kitchen_"))])
+def test_oracle_quantiser_matches_reference_kernel(name):
+    g = load(name)
+    q, s = ocpu.convrot_quant(g["x"], int(g["k"]), int(g["act"]))
+    if int(g["act"]) == 0:
+        assert np.array_equal(s, g["scale"])
+    else:
+        assert np.allclose(s, g["scale"], rtol=1e-6, atol=0)
+    assert_codes_close(q, g["q"], 1e-3, name)

@@ -1,0 +1,49 @@
+"""The CUDA kernels reproduce the reference kernels' golden vectors bit for bit
+(no reference code is needed at test time: the fixtures are committed)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import bits_to_bf16
+from h3_speedkit.ops.convrot import quantize_int8_rowwise_convrot64
+from h3_speedkit.ops.norm_quant import NormQuant
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _tensor(a, device):
+    if a.dtype == np.uint16:
+        return bits_to_bf16(a).to(device)
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in GOLDEN.glob("norm_*.npz")))
+def test_prologue_reproduces_golden(device, name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    x, w = _tensor(g["x"], device), _tensor(g["w"], device)
+    shift, scale, rows = _tensor(g["shift"], device), _tensor(g["scale"], device), _tensor(g["rows"], device)
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=device)
+    qs = torch.empty((m, 1), dtype=torch.float32, device=device)
+    rstd = torch.empty((m,), dtype=torch.float32, device=device)
+    NormQuant().bind(x, w, shift, scale, rows, q, qs, eps=float(g["eps"]),
+                     debug_norm=torch.empty((m, k), dtype=torch.bfloat16, device=device),
+                     debug_rotated=torch.empty((m, k), dtype=torch.float32, device=device), debug_rstd=rstd)()
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), g["q"])
+    assert np.array_equal(qs.cpu().numpy().reshape(-1), g["qscale"])
+    assert np.array_equal(rstd.cpu().numpy(), g["rstd"])
+
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in GOLDEN.glob("*.npz") if p.stem.startswith(("convrot_", "kitchen_"))))
+def test_quantiser_reproduces_golden(device, name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    act = int(g["act"])
+    q, s = quantize_int8_rowwise_convrot64(_tensor(g["x"], device), 256,
+                                           input_act=[None, "gelu_tanh", "swiglu"][act])
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), g["q"])
+    assert np.array_equal(s.cpu().numpy().reshape(-1), g["scale"])

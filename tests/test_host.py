@@ -1,0 +1,220 @@
+"""Host-side contracts on CPU: binding validation, row maps, manifest checks,
+model patching and the request wrapper (with fake ComfyUI modules, in the style
+of the reference's tests/test_indexed_gate.py)."""
+import copy
+import json
+import shutil
+import sys
+from types import ModuleType, SimpleNamespace
+from unittest.mock import patch
+
+import pytest
+import torch
+
+from h3_speedkit import runtime
+from h3_speedkit.ops import norm_quant as nq
+from h3_speedkit.runtime import Unsupported
+
+
+def _operands(m=4, k=512, tables=2, dtype=torch.bfloat16):
+    x = torch.randn((m, k)).to(torch.bfloat16)
+    w = torch.ones((k,), dtype=torch.bfloat16)
+    shift = torch.zeros((tables, k), dtype=dtype)
+    scale = torch.zeros((tables, k), dtype=dtype)
+    rows = torch.zeros((m,), dtype=torch.int32)
+    q = torch.empty((m, k), dtype=torch.int8)
+    qs = torch.empty((m, 1), dtype=torch.float32)
+    return x, w, shift, scale, rows, q, qs
+
+
+def test_validate_accepts_the_contract_on_cpu():
+    ins, outs = nq.validate(*_operands(), eps=1e-6, require_cuda=False)
+    assert [n for n, _ in ins] == ["x", "weight", "shift", "scale", "rows"]
+    ins, outs = nq.validate(*_operands(dtype=torch.float32), eps=1e-6, require_cuda=False)
+
+
+@pytest.mark.parametrize("mutate, message", [
+    (lambda o: o.__setitem__(0, o[0].float()), "X requires"),
+    (lambda o: o.__setitem__(0, torch.randn((4, 500)).to(torch.bfloat16)), "X requires"),
+    (lambda o: o.__setitem__(1, torch.ones((256,), dtype=torch.bfloat16)), "weight requires"),
+    (lambda o: o.__setitem__(3, torch.zeros((2, 512), dtype=torch.float32)), "Tables require"),
+    (lambda o: o.__setitem__(4, torch.zeros((4,), dtype=torch.int64)), "rows requires"),
+    (lambda o: o.__setitem__(5, torch.empty((4, 512), dtype=torch.uint8)), "q requires"),
+    (lambda o: o.__setitem__(6, torch.empty((4,), dtype=torch.float32)), "q_scale requires"),
+])
+def test_validate_rejects(mutate, message):
+    ops = list(_operands())
+    mutate(ops)
+    with pytest.raises(ValueError, match=message):
+        nq.validate(*ops, eps=1e-6, require_cuda=False)
+
+
+def test_validate_rejects_bad_eps_overlap_nonfinite_and_rows():
+    x, w, shift, scale, rows, q, qs = _operands()
+    for eps in (0.0, float("nan"), float("inf"), 1e-45):
+        with pytest.raises(ValueError, match="Epsilon"):
+            nq.validate(x, w, shift, scale, rows, q, qs, eps=eps, require_cuda=False)
+    alias = x.view(torch.int8)[:, :512]
+    with pytest.raises(ValueError):
+        nq.validate(x, w, shift, scale, rows, alias, qs, eps=1e-6, require_cuda=False)
+    bad = x.clone()
+    bad[2, 7] = float("nan")
+    with pytest.raises(ValueError, match="Nonfinite"):
+        nq.validate(bad, w, shift, scale, rows, q, qs, eps=1e-6, require_cuda=False)
+    rows_bad = torch.full((4,), 2, dtype=torch.int32)
+    with pytest.raises(ValueError, match="Rows outside"):
+        nq.validate(x, w, shift, scale, rows_bad, q, qs, eps=1e-6, require_cuda=False)
+
+
+def test_debug_outputs_come_together():
+    x, w, shift, scale, rows, q, qs = _operands()
+    with pytest.raises(ValueError, match="Debug requires"):
+        nq.validate(x, w, shift, scale, rows, q, qs, eps=1e-6, require_cuda=False,
+                    debug_norm=torch.empty((4, 512), dtype=torch.bfloat16))
+
+
+def test_check_disjoint_and_span_include_strided_padding():
+    base = torch.zeros((4, 16))
+    a = base[:, :8]
+    assert nq.span(a) == (a.data_ptr(), a.data_ptr() + (3 * 16 + 8) * 4)
+    with pytest.raises(ValueError, match="overlap"):
+        nq.check_disjoint([("a", a)], [("b", base[3:, 4:])])
+    nq.check_disjoint([("a", base[:2])], [("b", base[2:])])
+
+
+def test_segment_rows_reject_before_gpu_work():
+    assert runtime.segment_rows([(0, 3, 0), (3, 3, 1), (3, 8, 2)], 8, 3, "cpu").tolist() == [0, 0, 0, 2, 2, 2, 2, 2]
+    for segments in ([(0, 4, 0), (5, 8, 1)], [(0, 5, 0), (4, 8, 1)], [(0, 8, -1)], [(0, 8, 3)], [(0, 9, 0)],
+                     [(0, 7, 0)], [(0, 8, [0])], [(0, 8, True)]):
+        with pytest.raises(Unsupported):
+            runtime.segment_rows(segments, 8, 3, "cpu")
+
+
+def test_manifest_sha_mismatch_is_unsupported(tmp_path):
+    from h3_speedkit import _lib
+    for name in ("build.json", _lib.LIB_NAME):
+        shutil.copy(_lib.NATIVE / name, tmp_path / name)
+    for alias in runtime.LIBRARY_NAMES:
+        (tmp_path / (alias + ".so")).symlink_to(_lib.LIB_NAME)
+    runtime.verify_manifest(tmp_path)
+    build = json.loads((tmp_path / "build.json").read_text())
+    build["kernels"]["gate"]["sha256"] = "0" * 64
+    (tmp_path / "build.json").write_text(json.dumps(build))
+    with pytest.raises(Unsupported, match="gate"):
+        runtime.verify_manifest(tmp_path)
+    (tmp_path / "fc1.so").unlink()
+    with pytest.raises(Unsupported, match="fc1"):
+        runtime.verify_manifest(tmp_path)
+
+
+def test_backend_requires_a_b200():
+    if torch.cuda.is_available() and torch.cuda.get_device_capability() == (10, 0):
+        pytest.skip("a B200 is present")
+    with pytest.raises(Unsupported, match="B200"):
+        runtime.Backend()
+
+
+def _copy_options(obj):
+    if isinstance(obj, dict):
+        return {key: _copy_options(value) for key, value in obj.items()}
+    if isinstance(obj, list):
+        return [_copy_options(value) for value in obj]
+    return obj
+
+
+class FakeModel:
+    def __init__(self):
+        self.model_options = {"transformer_options": {"keep": "original"}}
+        self.model = SimpleNamespace(diffusion_model=SimpleNamespace(blocks=[]))
+
+    def clone(self):
+        cloned = copy.copy(self)
+        cloned.model_options = _copy_options(self.model_options)
+        return cloned
+
+    def set_model_patch_replace(self, replacement, name, block, index):
+        # ComfyUI replaces this options dictionary on every call
+        options = _copy_options(self.model_options["transformer_options"])
+        options.setdefault("patches_replace", {}).setdefault(name, {})[(block, index)] = replacement
+        self.model_options["transformer_options"] = options
+
+
+def _fake_comfy():
+    modules = {name: ModuleType(name) for name in ("comfy", "comfy.patcher_extension")}
+    modules["comfy"].patcher_extension = modules["comfy.patcher_extension"]
+    pe = modules["comfy.patcher_extension"]
+    pe.WrappersMP = SimpleNamespace(DIFFUSION_MODEL="diffusion")
+    pe.add_wrapper_with_key = lambda kind, key, wrapper, options: options.setdefault("wrappers", {}).update(
+        {key: wrapper})
+    return modules
+
+
+def test_patch_model_installs_on_a_clone_and_rejects_double_install():
+    model = FakeModel()
+    with patch.dict(sys.modules, _fake_comfy()):
+        with pytest.raises(Unsupported, match="attention provider"):
+            runtime.patch_model(model)
+        fast = runtime.patch_model(model, attention=lambda q, k, v: v, backend=object())
+        assert model.model_options == {"transformer_options": {"keep": "original"}}
+        options = fast.model_options["transformer_options"]
+        assert len(options["patches_replace"]["dit"]) == runtime.BLOCKS
+        assert options["wrappers"][runtime.KEY].__self__ is fast._h3_speedkit
+        with pytest.raises(Unsupported, match="already installed"):
+            runtime.patch_model(fast, attention=lambda q, k, v: v, backend=object())
+
+
+def test_wrapper_falls_back_and_cleans_context():
+    consumer = runtime.ModelPatch(object(), backend=object())
+
+    def executor(*args, **kwargs):
+        assert "fallback" in consumer.context.get()
+        return "original result"
+    with patch.object(runtime.LOG, "warning") as warn:
+        assert consumer.wrapper(executor, [torch.zeros((1, 4))]) == "original result"
+        assert warn.called
+    assert consumer.context.get() is None
+    assert "fallback" in consumer.last_report
+
+    def failed(*args, **kwargs):
+        raise OSError("executor failure")
+    with pytest.raises(OSError):
+        consumer.wrapper(failed, [torch.zeros((1, 4))])
+    assert consumer.context.get() is None
+
+    # a replacement outside a request, or in a fallback request, runs the original block
+    run = consumer.replacement(0)
+    assert run({"img": 1}, {"original_block": lambda inputs: "orig"}) == "orig"
+
+
+def test_node_schema_matches_the_reference():
+    io = ModuleType("comfy_api.latest.io")
+
+    class Spec(SimpleNamespace):
+        pass
+
+    class Kind:
+        def __init__(self, name):
+            self.name = name
+
+        def Input(self, *a, **k):
+            return Spec(kind=self.name, args=a, kw=k)
+
+        def Output(self, *a, **k):
+            return Spec(kind=self.name, args=a, kw=k)
+
+    io.ComfyNode = object
+    io.Schema = lambda **kw: Spec(**kw)
+    io.Model, io.Boolean, io.String = Kind("model"), Kind("bool"), Kind("string")
+    io.NodeOutput = lambda *a: a
+    latest = ModuleType("comfy_api.latest")
+    latest.io = io
+    modules = {"comfy_api": ModuleType("comfy_api"), "comfy_api.latest": latest}
+    with patch.dict(sys.modules, modules):
+        from h3_speedkit import nodes
+        (node,) = nodes.make_nodes()
+        schema = node.define_schema()
+        assert schema.node_id == "H3SpeedKitOptimize"
+        assert [i.kind for i in schema.inputs] == ["model", "bool"]
+        assert [o.kind for o in schema.outputs] == ["model", "string"]
+        out = node.execute(FakeModel(), enabled=False)
+        assert out[1] == "H3 SpeedKit disabled"

@@ -40,9 +40,9 @@ def test_block_matches_cpu_restatement(device):
     same = float((got == ref).mean())
     a = torch.from_numpy(got.view(np.int16)).view(torch.bfloat16).float()
     b = torch.from_numpy(ref.view(np.int16)).view(torch.bfloat16).float()
-    rel = ((a - b).abs() / b.abs().clamp_min(1e-3)).max().item()
+    err = ((a - b).abs().max() / b.abs().max()).item()
     assert same > 0.99, f"only {same:.4f} of the outputs are bit-identical"
-    assert rel < 0.05
+    assert err < 1e-2, f"largest deviation {err:.2e} of the output magnitude"
 
 
 def test_row_shards_are_bit_identical_to_the_whole(device):

@@ -13,7 +13,7 @@
 // / SwiGLU) for any K % 256 == 0 up to 16384.  The per-value results do not
 // depend on the thread layout: each FHT output is the same expression of the
 // same four inputs, and the absmax is an order-free fmaxf.
-#include "rq_core.cuh"
+#include "row_stream.cuh"
 #include "../../include/h3sk_b200.h"
 
 namespace h3sk {
@@ -104,11 +104,149 @@ __global__ void __launch_bounds__(256) convrot_quant_rows(
   }
 }
 
+// Layout-A values of one thread from its 8 raw input words (and, for SwiGLU,
+// the 8 words of the up half), through the input activation.
+template <int kAct>
+__device__ __forceinline__ void activate_raw(const uint4 (&raw)[8], const uint4 (&up)[8], uint64_t (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    if constexpr (kAct == kActNone) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) v[4 * i + h] = rq::bf2_to_f2(w[h]);
+    } else if constexpr (kAct == kActGeluTanh) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t x = rq::bf2_to_f2(w[h]);
+        v[4 * i + h] = rq::f2_pack(gelu_tanh(rq::f2_lo(x)), gelu_tanh(rq::f2_hi(x)));
+      }
+    } else {
+      const uint32_t u[4] = {up[i].x, up[i].y, up[i].z, up[i].w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t g = rq::bf2_to_f2(w[h]), x = rq::bf2_to_f2(u[h]);
+        v[4 * i + h] = rq::f2_pack(swiglu(rq::f2_lo(g), rq::f2_lo(x)), swiglu(rq::f2_hi(g), rq::f2_hi(x)));
+      }
+    }
+  }
+}
+
+// Persistent streaming quantiser (row_stream.cuh): each row team reads its
+// rows from its TMA-fed ring in layout A and runs the same ConvRot / absmax /
+// code steps as convrot_quant_rows.  One team barrier per row (the absmax),
+// after which thread 0 refills the slot just read.
+template <int kAct>
+__global__ void __launch_bounds__(512, 1) convrot_quant_stream(
+    const __grid_constant__ CUtensorMap map_x, int8_t* __restrict__ Q, float* __restrict__ Scales, int64_t M,
+    const rs::Plan plan, int q_vec16, int* status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ rs::RingState st;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int K = plan.k, D = plan.slots_per_team, teams = plan.teams, team_threads = plan.team_threads;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int team = tid / team_threads, tt = tid - team * team_threads;
+  const int g = tt >> 2, q = tt & 3, twarp = tt >> 5, nwarps = team_threads >> 5;
+  const bool active = g < K / 256;
+  const int grid = int(gridDim.x);
+  const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
+  const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
+  unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
+  unsigned char* xbuf = ring + size_t(D) * plan.slot_bytes + size_t(g) * rs::kHalfGroupBytes;
+  uint64_t* full = st.full + team * D;
+  const int bar_id = 1 + team;
+
+  int issued = 0;
+  if (tt == 0) {
+    for (int d = 0; d < D; ++d) sm100::mbar_init(&full[d], 1);
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_map(&map_x);
+    for (; issued < D && issued < n_team; ++issued)
+      rs::issue_row(&map_x, ring + size_t(issued) * plan.slot_bytes, &full[issued],
+                    int(blockIdx.x) + (team + issued * teams) * grid, K, plan.width);
+  }
+  rs::team_sync(bar_id, team_threads);
+
+  int d = 0;
+  uint32_t ph = 0;
+  int parity = 0;
+  int k = 0;
+  for (; k < n_team; ++k, parity ^= 1) {
+    const bool ok = sm100::mbar_wait_bounded(&full[d], ph, nullptr, status, rs::kCodeFull, rs::kWaitNs);
+    const unsigned char* row_buf = ring + size_t(d) * plan.slot_bytes;
+    uint64_t v[32];
+    if (active) {
+      uint4 raw[8], up[8];
+      rs::load_row_a(row_buf, g, q, raw);
+      if constexpr (kAct == kActSwiGLU) rs::load_row_a(row_buf + 2 * K, g, q, up);
+      activate_raw<kAct>(raw, up, v);
+    } else {
+#pragma unroll
+      for (int p = 0; p < 32; ++p) v[p] = 0;
+    }
+    rq::fht_layout_a(v);
+    rs::exchange_a_to_b_halves(v, xbuf, q, g & 1);
+    rq::fht_layout_b(v);
+    const float local = warp_allmax(rq::absmax64(v));
+    if (lane == 0) st.max_fold[team][parity][twarp] = local;
+    if (!rs::team_sync_and(bar_id, team_threads, ok)) break;
+    // Slot d has been read by the whole team: refill it.
+    if (tt == 0 && issued < n_team) {
+      rs::issue_row(&map_x, ring + size_t(d) * plan.slot_bytes, &full[d],
+                    int(blockIdx.x) + (team + issued * teams) * grid, K, plan.width);
+      ++issued;
+    }
+    if (++d == D) { d = 0; ph ^= 1u; }
+    float m = 0.0f;
+    for (int w = 0; w < nwarps; ++w) m = fmaxf(m, st.max_fold[team][parity][w]);
+    const float scale = int8_row_scale(m);
+    const int64_t row = int64_t(blockIdx.x) + int64_t(team + k * teams) * grid;
+    if (tt == 0) Scales[row] = scale;
+    if (active) {
+      const float scale_bf = __bfloat162float(__float2bfloat16_rn(scale));
+      rq::store_codes(Q + row * K + g * 256, q, v, scale_bf, q_vec16);
+    }
+  }
+  // After an abort: no box may still be landing in this team's ring at exit.
+  if (tt == 0)
+    for (int j = k; j < issued; ++j)
+      sm100::mbar_wait_bounded(&full[j % D], uint32_t((j / D) & 1), nullptr, status, rs::kCodeFull, rs::kWaitNs);
+}
+
 bool valid_k(int64_t k) { return k >= 256 && k <= kMaxK && k % 256 == 0; }
+
+// The streaming kernel needs 16-byte aligned rows (TMA); anything else takes the
+// one-CTA-per-row kernel.
+template <int kAct>
+cudaError_t launch_stream(const void* x, int64_t xs, void* q, void* scale, int64_t rows, int k,
+                          cudaStream_t stream, bool* launched) {
+  *launched = false;
+  if ((uintptr_t(x) & 15u) || (xs % 8)) return cudaSuccess;
+  const int width = kAct == kActSwiGLU ? 2 * k : k;
+  const rs::Plan plan = rs::make_plan(k, width, 32);
+  if (plan.teams < 1 || plan.slots_per_team < 2) return cudaSuccess;
+  CUtensorMap map;
+  if (!rs::make_row_map(&map, x, rows, width, k, xs)) return cudaSuccess;
+  auto kernel = convrot_quant_stream<kAct>;
+  int grid = 0;
+  cudaError_t e = rs::stream_grid(reinterpret_cast<const void*>(kernel), plan.smem, rows, &grid);
+  if (e != cudaSuccess) return e;
+  int* status = status_device_ptr();
+  if (!status) return cudaErrorInvalidDevicePointer;
+  kernel<<<grid, plan.threads, plan.smem, stream>>>(map, static_cast<int8_t*>(q), static_cast<float*>(scale), rows,
+                                                    plan, (uintptr_t(q) & 15u) == 0 ? 1 : 0, status);
+  *launched = true;
+  return cudaGetLastError();
+}
 
 template <int kAct, int kMode>
 cudaError_t launch(const void* x, int64_t xs, void* q, void* scale, void* rotated, int64_t rows, int k,
                    cudaStream_t stream) {
+  if constexpr (kMode == kModeQuant) {
+    bool launched = false;
+    const cudaError_t e = launch_stream<kAct>(x, xs, q, scale, rows, k, stream, &launched);
+    if (launched || e != cudaSuccess) return e;
+  }
   auto kernel = convrot_quant_rows<kAct, kMode>;
   const int smem = convrot_smem(k);
   if (smem > 48 * 1024) {

@@ -1,6 +1,8 @@
 // Host-side launch helpers shared by the row-quantiser translation units.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cstdint>
 #include <map>
@@ -12,6 +14,21 @@ namespace h3sk {
 // Device address of the library's pipeline status word on the current device
 // (defined with the GEMM); bounded waits that run out record their code there.
 int* status_device_ptr();
+
+// Driver entry point of cuTensorMapEncodeTiled, resolved once through the
+// runtime (no libcuda link dependency); null if the driver lacks it.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
 
 // Grid of a persistent kernel: as many CTAs as fit on the device at once
 // (occupancy x SM count, computed once per kernel, device, block and smem size),

@@ -20,7 +20,7 @@
 //  * ConvRot256 + row scale + codes as in rq_core.cuh  (:179-211).
 // The reference fixes K = 5376 with 192 threads; this kernel takes any
 // K % 256 == 0 up to 16384 with max(64, K/64 rounded up to a warp) threads.
-#include "rq_core.cuh"
+#include "row_stream.cuh"
 #include "../../include/h3sk_b200.h"
 
 #include <cfloat>
@@ -199,6 +199,173 @@ __global__ void __launch_bounds__(256) norm_quant_rows(
   }
 }
 
+// Persistent streaming prologue (row_stream.cuh).  Per row, a team:
+//  1. waits for the row in its ring slot (swizzled BF16, one TMA box);
+//  2. sum of squares in the reference's order (team threads 0..63 run the
+//     logical threads p and p+64 as f32x2 halves, reading 8-byte chunks);
+//     barrier A (AND of the wait flags), then every thread folds the four
+//     logical-warp sums and computes rrms itself;
+//  3. modulation pass: thread t takes the 16-byte chunks t, t + team, ... of the
+//     row, reads W / shift / scale for those 8 columns with coalesced global
+//     loads (they stay in L1: every row of the CTA uses the same columns), and
+//     writes the modulated BF16 values back into the slot; barrier B;
+//  4. reads its 64 layout-A values from the slot (the slot is then free), FHT
+//     stages 1-3, two-half exchange, stage 4, absmax; barrier C, after which
+//     thread 0 refills the slot with the team's next-but-D row;
+//  5. row scale and codes.
+// The arithmetic is that of norm_quant_rows, value for value.
+template <class ModT>
+__global__ void __launch_bounds__(512, 1) norm_quant_stream(
+    const __grid_constant__ CUtensorMap map_x, const __nv_bfloat16* __restrict__ W,
+    const ModT* __restrict__ Shift, const ModT* __restrict__ Scale, const int32_t* __restrict__ Rows,
+    int8_t* __restrict__ Q, float* __restrict__ QScale, int64_t ss, int64_t cs, float eps, int64_t M,
+    const rs::Plan plan, int w_vec16, int t_vec16, int q_vec16, int* status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ rs::RingState st;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int K = plan.k, D = plan.slots_per_team, teams = plan.teams, team_threads = plan.team_threads;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int team = tid / team_threads, tt = tid - team * team_threads;
+  const int g = tt >> 2, q = tt & 3, twarp = tt >> 5, nwarps = team_threads >> 5;
+  const bool active = g < K / 256;
+  const int grid = int(gridDim.x);
+  const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
+  const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
+  unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
+  unsigned char* xbuf = ring + size_t(D) * plan.slot_bytes + size_t(g) * rs::kHalfGroupBytes;
+  uint64_t* full = st.full + team * D;
+  const int bar_id = 1 + team;
+  const int nchunks = K / 4;       // 8-byte chunks of the sum of squares
+  const int nchunks16 = K / 8;     // 16-byte chunks of the modulation pass
+
+  int issued = 0;
+  if (tt == 0) {
+    for (int d = 0; d < D; ++d) sm100::mbar_init(&full[d], 1);
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_map(&map_x);
+    for (; issued < D && issued < n_team; ++issued)
+      rs::issue_row(&map_x, ring + size_t(issued) * plan.slot_bytes, &full[issued],
+                    int(blockIdx.x) + (team + issued * teams) * grid, K, K);
+  }
+  rs::team_sync(bar_id, team_threads);
+
+  int d = 0;
+  uint32_t ph = 0;
+  int parity = 0;
+  int k = 0;
+  for (; k < n_team; ++k, parity ^= 1) {
+    const int64_t row = int64_t(blockIdx.x) + int64_t(team + k * teams) * grid;
+    const bool ok = sm100::mbar_wait_bounded(&full[d], ph, nullptr, status, rs::kCodeFull, rs::kWaitNs);
+    unsigned char* row_buf = ring + size_t(d) * plan.slot_bytes;
+
+    // 2. sum of squares
+    if (tt < 64) {
+      uint64_t acc = 0;
+#pragma unroll 4
+      for (int base = 0; base < nchunks; base += 128) {
+        const int c0 = base + tt, c1 = base + tt + 64;
+        const uint2 r0 = c0 < nchunks ? *reinterpret_cast<const uint2*>(row_buf + rs::swz128(8u * c0)) : make_uint2(0, 0);
+        const uint2 r1 = c1 < nchunks ? *reinterpret_cast<const uint2*>(row_buf + rs::swz128(8u * c1)) : make_uint2(0, 0);
+        uint64_t e;
+        e = rq::f2_pack(__uint_as_float(r0.x << 16), __uint_as_float(r1.x << 16));
+        acc = rq::f2_fma_ieee(e, e, acc);
+        e = rq::f2_pack(__uint_as_float(r0.x & 0xffff0000u), __uint_as_float(r1.x & 0xffff0000u));
+        acc = rq::f2_fma_ieee(e, e, acc);
+        e = rq::f2_pack(__uint_as_float(r0.y << 16), __uint_as_float(r1.y << 16));
+        acc = rq::f2_fma_ieee(e, e, acc);
+        e = rq::f2_pack(__uint_as_float(r0.y & 0xffff0000u), __uint_as_float(r1.y & 0xffff0000u));
+        acc = rq::f2_fma_ieee(e, e, acc);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float lo = __shfl_down_sync(kFullMask, rq::f2_lo(acc), off);
+        const float hi = __shfl_down_sync(kFullMask, rq::f2_hi(acc), off);
+        acc = rq::f2_add_ieee(acc, rq::f2_pack(lo, hi));
+      }
+      if (lane == 0) {
+        st.stat_fold[team][twarp] = rq::f2_lo(acc);       // logical warp twarp
+        st.stat_fold[team][twarp + 2] = rq::f2_hi(acc);   // logical warp twarp + 2
+      }
+    }
+    if (!rs::team_sync_and(bar_id, team_threads, ok)) break;   // barrier A
+    const float* f = st.stat_fold[team];
+    const float total = ieee_add(ieee_add(f[0], f[2]), ieee_add(f[1], f[3]));
+    const float rrms = hw_rsqrt(ieee_add(ieee_div(total, static_cast<float>(K)), eps));
+
+    // 3. modulation pass, in place
+    {
+      const int table_row = __ldg(Rows + row);
+      const ModT* shift_row = Shift + static_cast<int64_t>(table_row) * ss;
+      const ModT* scale_row = Scale + static_cast<int64_t>(table_row) * cs;
+      const uint64_t rr = rq::f2_pack(rrms, rrms);
+      const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
+      for (int c = tt; c < nchunks16; c += team_threads) {
+        uint4* p = reinterpret_cast<uint4*>(row_buf + rs::swz128(16u * c));
+        const uint4 xv = *p;
+        const uint4 wv = load8(W + 8 * c, w_vec16);
+        const uint4 sv = table8<ModT>(shift_row + 8 * c, t_vec16);
+        const uint4 cv = table8<ModT>(scale_row + 8 * c, t_vec16);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, cw[4] = {cv.x, cv.y, cv.z, cv.w};
+        uint32_t nw[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
+          nw[h] = rq::bf2_add(rq::bf2_mul(rq::f2_to_bf2(t), rq::bf2_add(one2, cw[h])), sw[h]);
+        }
+        *p = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+      }
+    }
+    rs::team_sync(bar_id, team_threads);   // barrier B: the modulated row is complete
+
+    // 4. ConvRot256 + absmax
+    uint64_t v[32];
+    if (active) {
+      uint4 raw[8];
+      rs::load_row_a(row_buf, g, q, raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[4 * i + 0] = rq::bf2_to_f2(raw[i].x);
+        v[4 * i + 1] = rq::bf2_to_f2(raw[i].y);
+        v[4 * i + 2] = rq::bf2_to_f2(raw[i].z);
+        v[4 * i + 3] = rq::bf2_to_f2(raw[i].w);
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < 32; ++p) v[p] = 0;
+    }
+    // This thread's generic-proxy writes to the slot must be ordered before the
+    // TMA (async proxy) that refills it.
+    sm100::fence_async_shared();
+    rq::fht_layout_a(v);
+    rs::exchange_a_to_b_halves(v, xbuf, q, g & 1);
+    rq::fht_layout_b(v);
+    const float local = warp_allmax(rq::absmax64(v));
+    if (lane == 0) st.max_fold[team][parity][twarp] = local;
+    rs::team_sync(bar_id, team_threads);   // barrier C
+    if (tt == 0 && issued < n_team) {
+      rs::issue_row(&map_x, row_buf, &full[d], int(blockIdx.x) + (team + issued * teams) * grid, K, K);
+      ++issued;
+    }
+    if (++d == D) { d = 0; ph ^= 1u; }
+
+    // 5. scale and codes
+    float m = 0.0f;
+    for (int w = 0; w < nwarps; ++w) m = fmaxf(m, st.max_fold[team][parity][w]);
+    const float scale = int8_row_scale(m);
+    if (tt == 0) QScale[row] = scale;
+    if (active) {
+      const float scale_bf = __bfloat162float(__float2bfloat16_rn(scale));
+      rq::store_codes(Q + row * K + g * 256, q, v, scale_bf, q_vec16);
+    }
+  }
+  // After an abort: no box may still be landing in this team's ring at exit.
+  if (tt == 0)
+    for (int j = k; j < issued; ++j)
+      sm100::mbar_wait_bounded(&full[j % D], uint32_t((j / D) & 1), nullptr, status, rs::kCodeFull, rs::kWaitNs);
+}
+
 template <class T, bool D>
 int query_kernel(int k, H3NormQuantResources* out) {
   cudaFuncAttributes a{};
@@ -244,9 +411,32 @@ int run_checked(const void* x, const void* w, const void* shift, const void* sca
   const int64_t tsz = table_dtype ? 2 : 4;
   const int t_vec16 = ((uintptr_t(shift) & 15u) == 0 && (uintptr_t(scale) & 15u) == 0 && (ss * tsz) % 16 == 0 &&
                        (cs * tsz) % 16 == 0) ? 1 : 0;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  if (!debug && x_vec16) {
+    // Streaming kernel: TMA needs 16-byte aligned rows, which x_vec16 states.
+    const rs::Plan plan = rs::make_plan(int(k), int(k), 64);
+    CUtensorMap map;
+    if (plan.teams >= 1 && plan.slots_per_team >= 2 && rs::make_row_map(&map, x, m, int(k), int(k), xs)) {
+      int* status = status_device_ptr();
+      if (!status) return cudaErrorInvalidDevicePointer;
+      int grid = 0;
+#define H3SK_NQ_STREAM(T)                                                                                   \
+  do {                                                                                                      \
+    auto kernel = norm_quant_stream<T>;                                                                     \
+    const cudaError_t e = rs::stream_grid(reinterpret_cast<const void*>(kernel), plan.smem, m, &grid);      \
+    if (e != cudaSuccess) return e;                                                                         \
+    kernel<<<grid, plan.threads, plan.smem, stream>>>(                                                      \
+        map, static_cast<const __nv_bfloat16*>(w), static_cast<const T*>(shift), static_cast<const T*>(scale), \
+        static_cast<const int32_t*>(rows), static_cast<int8_t*>(q), static_cast<float*>(qscale), ss, cs, eps, m, \
+        plan, w_vec16, t_vec16, q_vec16, status);                                                           \
+  } while (0)
+      if (table_dtype == 0) H3SK_NQ_STREAM(float); else H3SK_NQ_STREAM(__nv_bfloat16);
+#undef H3SK_NQ_STREAM
+      return cudaGetLastError();
+    }
+  }
   const int threads = norm_threads(int(k));
   const int smem = norm_smem(int(k));
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
 #define H3SK_NQ_LAUNCH(T, D)                                                                       \
   do {                                                                                             \
     auto kernel = norm_quant_rows<T, D>;                                                           \

@@ -152,7 +152,8 @@ __global__ void __launch_bounds__(512, 1) convrot_quant_stream(
   const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
   const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
   unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
-  unsigned char* xbuf = ring + size_t(D) * plan.slot_bytes + size_t(g) * rs::kHalfGroupBytes;
+  const uint32_t ring_a = sm100::smem_addr(ring);
+  const uint32_t xbuf_a = ring_a + uint32_t(D * plan.slot_bytes + g * rs::kHalfGroupBytes);
   uint64_t* full = st.full + team * D;
   const int bar_id = 1 + team;
 
@@ -173,19 +174,19 @@ __global__ void __launch_bounds__(512, 1) convrot_quant_stream(
   int k = 0;
   for (; k < n_team; ++k, parity ^= 1) {
     const bool ok = sm100::mbar_wait_bounded(&full[d], ph, nullptr, status, rs::kCodeFull, rs::kWaitNs);
-    const unsigned char* row_buf = ring + size_t(d) * plan.slot_bytes;
+    const uint32_t row_a = ring_a + uint32_t(d * plan.slot_bytes);
     uint64_t v[32];
     if (active) {
       uint4 raw[8], up[8];
-      rs::load_row_a(row_buf, g, q, raw);
-      if constexpr (kAct == kActSwiGLU) rs::load_row_a(row_buf + 2 * K, g, q, up);
+      rs::load_row_a(row_a, g, q, raw);
+      if constexpr (kAct == kActSwiGLU) rs::load_row_a(row_a + uint32_t(2 * K), g, q, up);
       activate_raw<kAct>(raw, up, v);
     } else {
 #pragma unroll
       for (int p = 0; p < 32; ++p) v[p] = 0;
     }
     rq::fht_layout_a(v);
-    rs::exchange_a_to_b_halves(v, xbuf, q, g & 1);
+    rs::exchange_a_to_b_halves(v, xbuf_a, q, g & 1);
     rq::fht_layout_b(v);
     const float local = warp_allmax(rq::absmax64(v));
     if (lane == 0) st.max_fold[team][parity][twarp] = local;

@@ -48,37 +48,56 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128;            // tile rows (TMEM lanes)
+constexpr int kBM = 128;            // tile rows per CTA (TMEM lanes)
 constexpr int kBN = 256;            // tile columns (TMEM columns per accumulator)
 constexpr int kBK = 128;            // K bytes per stage (one 128-byte swizzle row)
-constexpr int kStages = 4;
 constexpr int kUmmaK = 32;          // K of one kind::i8 MMA
 constexpr int kATileBytes = kBM * kBK;
-constexpr int kBTileBytes = kBN * kBK;
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kEpilogueWarps = 8;    // two per TMEM lane quarter, one per column half
 constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
 constexpr int kGroupM = 16;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
-constexpr uint32_t kIdesc = idesc_i8(kBM, kBN);
 
 enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
 
+// Tile geometry of the two kernel shapes.
+//   single CTA: a 128 x 256 tile per CTA, B tile 256 rows, 4 stages of 48 KB;
+//   CTA pair (cluster of 2, cta_group::2): a 256 x 256 tile per pair, each CTA
+//   loads 128 rows of A and 128 rows of B per stage (6 stages of 32 KB) and owns
+//   128 accumulator rows; the leader issues M=256 N=256 MMAs over both CTAs'
+//   shared memory, so every B byte crosses L2 -> SM once per 256 rows instead of
+//   once per 128.
+template <bool kPair>
+struct Shape {
+  static constexpr int pair = kPair ? 2 : 1;
+  static constexpr int tile_m = kBM * pair;               // rows per (pair) tile
+  static constexpr int b_rows = kPair ? kBN / 2 : kBN;    // B rows loaded per CTA
+  static constexpr int b_tile_bytes = b_rows * kBK;
+  static constexpr int stage_bytes = kATileBytes + b_tile_bytes;
+  static constexpr int stages = kPair ? 6 : 4;
+  static constexpr uint32_t idesc = idesc_i8(kBM * pair, kBN);
+  static constexpr uint32_t tempty_count = kPair ? 2 * kEpilogueWarps : kEpilogueWarps;
+};
+
+template <bool kPair>
 struct SmemLayout {
+  using S = Shape<kPair>;
   // offsets from the 1024-aligned base
   static constexpr int a = 0;
-  static constexpr int b = kStages * kATileBytes;
-  static constexpr int bars = b + kStages * kBTileBytes;        // full[S], empty[S], tfull[2], tempty[2], drain
-  static constexpr int nbars = 2 * kStages + 5;
-  static constexpr int misc = bars + nbars * 8;                  // tmem slot, abort flag
-  static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float
+  static constexpr int b = S::stages * kATileBytes;
+  static constexpr int bars = b + S::stages * S::b_tile_bytes;  // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int nbars = 2 * S::stages + 5;
+  static constexpr int misc = (bars + nbars * 8 + 15) / 16 * 16;  // tmem slot, abort flag, ready flag
+  static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float (16-byte aligned)
   static constexpr int stage = ((colv + 2 * kBN * 4) + 1023) / 1024 * 1024;   // per-warp output staging
   static constexpr int stage_warp_bytes = 32 * 32 * 2;           // 32 rows x 32 BF16 columns
   static constexpr int total = stage + kEpilogueWarps * stage_warp_bytes;
   static constexpr int dynamic_bytes = total + 1024;             // slack for 1024 alignment
 };
+static_assert(SmemLayout<true>::dynamic_bytes <= 227 * 1024, "pair layout exceeds shared memory");
+static_assert(SmemLayout<false>::dynamic_bytes <= 227 * 1024, "single layout exceeds shared memory");
 
 struct GemmParams {
   const float* xs;
@@ -114,6 +133,17 @@ __device__ __forceinline__ float gelu_tanh_precise(float v) {
   return 0.5f * v * (1.0f + tanhf(inner));
 }
 
+// GELU of a BF16 input, rounded to BF16 (the expression of
+// convrot64_exact.cuh:913-923 evaluated on the BF16 dequant value).
+__device__ __forceinline__ uint32_t bf_round_bits(float a) {
+  unsigned short b;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(b) : "f"(a));
+  return b;
+}
+__device__ __forceinline__ uint32_t gelu_bits(uint32_t b) {
+  return bf_round_bits(gelu_tanh_precise(__uint_as_float(b << 16)));
+}
+
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 // Two FP32 values -> one word of two BF16 (round to nearest even), low half = lo.
@@ -140,22 +170,34 @@ __device__ __forceinline__ void store_chunk_acc(const GemmParams& p, const uint3
 // BF16 epilogue values of 32 consecutive accumulators of one row (columns
 // [col0, col0+32), tile-local chunk c) as 16 packed words.  Rows >= M and
 // columns >= N produce unused values and read no memory.
+// BF16 results of one 32-column chunk of one row: y = bf((acc * xs) * ws + bias)
+// (fc1.cu / gate.cu epilogue order), then GELU or the gate-residual update.
+// Column scales and bias come from shared memory as 16-byte broadcasts.  (Packed
+// f32x2 multiplies and adds were measured to differ from these scalar IEEE
+// operations on rare cancelling inputs, so the dequant stays scalar.)
 template <int kEpi>
 __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t (&r)[32], bool row_ok, int row,
                                              int col0, int c, float xs_row, const __nv_bfloat16* gate_row,
                                              const float* col_ws, const float* col_bias, uint32_t (&packed)[16]) {
+  const float4* wsv = reinterpret_cast<const float4*>(col_ws + c * 32);
+  const float4* bsv = reinterpret_cast<const float4*>(col_bias + c * 32);
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    float y2[2];
+  for (int q = 0; q < 8; ++q) {
+    const float4 w4 = wsv[q], b4 = bsv[q];
+    const float w[4] = {w4.x, w4.y, w4.z, w4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+    float y[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int cc = c * 32 + i + h;
-      const float a = __int2float_rn(int(r[i + h]));
-      y2[h] = __fadd_rn(__fmul_rn(__fmul_rn(a, xs_row), col_ws[cc]), col_bias[cc]);
+    for (int h = 0; h < 4; ++h)
+      y[h] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(int(r[4 * q + h])), xs_row), w[h]), b[h]);
+    packed[2 * q] = pack_bf2(y[0], y[1]);
+    packed[2 * q + 1] = pack_bf2(y[2], y[3]);
+  }
+  if constexpr (kEpi == kEpiGelu) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t w = packed[i];
+      packed[i] = gelu_bits(w & 0xffffu) | (gelu_bits(w >> 16) << 16);
     }
-    packed[i / 2] = pack_bf2(y2[0], y2[1]);
-    if constexpr (kEpi == kEpiGelu)
-      packed[i / 2] = pack_bf2(gelu_tanh_precise(bf_lo(packed[i / 2])), gelu_tanh_precise(bf_hi(packed[i / 2])));
   }
   if constexpr (kEpi == kEpiGate) {
     // D may alias the residual: every element is read here, before its store is issued.
@@ -179,36 +221,48 @@ __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t
   }
 }
 
-template <int kEpi>
+// Persistent warp-specialised INT8 GEMM.  Warp 0: TMA producer; warp 1: MMA
+// issuer (TMEM allocation owner); warps 2..9: epilogue (TMEM -> registers ->
+// dequant / GELU / gate-residual -> BF16 -> swizzled staging -> TMA store).
+// kPair: clusters of two CTAs share one 256 x 256 tile (see Shape); the leader
+// (rank 0) issues the MMAs, both CTAs produce their operand halves and run the
+// epilogue of their 128 accumulator rows.
+template <int kEpi, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
+  using S = Shape<kPair>;
+  using L = SmemLayout<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smem_a = smem + SmemLayout::a;
-  uint8_t* smem_b = smem + SmemLayout::b;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  uint8_t* smem_a = smem + L::a;
+  uint8_t* smem_b = smem + L::b;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars);
+  uint64_t* empty = full + S::stages;
+  uint64_t* tfull = empty + S::stages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc);
-  volatile int* abort = reinterpret_cast<volatile int*>(smem + SmemLayout::misc + 4);
-  volatile int* ready = reinterpret_cast<volatile int*>(smem + SmemLayout::misc + 8);
-  float* col_ws = reinterpret_cast<float*>(smem + SmemLayout::colv);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::misc + 4);
+  volatile int* ready = reinterpret_cast<volatile int*>(smem + L::misc + 8);
+  float* col_ws = reinterpret_cast<float*>(smem + L::colv);
   float* col_bias = col_ws + kBN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* status = p.status;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = kPair ? int(blockIdx.x >> 1) : int(blockIdx.x);        // tile-walking unit (pair or CTA)
+  const int units = kPair ? int(gridDim.x >> 1) : int(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S::stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpilogueThreads);
+      mbar_init(&tempty[a], S::tempty_count);
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -218,11 +272,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kEpi != kEpiAcc) tma_prefetch_map(&map_d);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync_all();   // both CTAs' barriers and TMEM exist before any cross-CTA use
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -230,27 +290,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   // __shfl_sync hands its verdict to the other lanes, so every .sync.aligned
   // tcgen05 instruction and every barrier below is reached by converged warps.
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs of a pair) ----------------
     uint64_t policy_a = 0, policy_b = 0;
+    uint32_t full_leader = 0;
     if (lane == 0) {
       policy_a = l2_policy_evict_normal();
       policy_b = l2_policy_evict_last();
+      if constexpr (kPair) full_leader = map_to_rank(smem_addr(full), 0);
     }
     uint32_t issued_mask = 0, issued_phase_bits = 0;   // per stage: issued at least once / parity of last issue
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+    for (int tile = unit; ok && tile < p.tiles; tile += units) {
       int mt, nt;
       tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      const int a_row = mt * S::tile_m + int(rank) * kBM;
+      const int b_row = nt * kBN + int(rank) * S::b_rows;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         int got = 0;
         if (lane == 0) {
           got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, status, 11, p.timeout_ns) ? 1 : 0;
           if (got) {
-            mbar_arrive_expect_tx(&full[stage], kStageBytes);
-            tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], kb * kBK, mt * kBM, policy_a);
-            tma_load_2d(smem_b + stage * kBTileBytes, &map_b, &full[stage], kb * kBK, nt * kBN, policy_b);
+            uint8_t* da = smem_a + stage * kATileBytes;
+            uint8_t* db = smem_b + stage * S::b_tile_bytes;
+            if constexpr (kPair) {
+              // The leader's full barrier counts both CTAs' bytes; only the leader arms it.
+              if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::stage_bytes);
+              const uint32_t bar = full_leader + uint32_t(stage) * 8u;
+              tma_load_2d_pair(da, &map_a, bar, kb * kBK, a_row, policy_a);
+              tma_load_2d_pair(db, &map_b, bar, kb * kBK, b_row, policy_b);
+            } else {
+              mbar_arrive_expect_tx(&full[stage], S::stage_bytes);
+              tma_load_2d(da, &map_a, &full[stage], kb * kBK, a_row, policy_a);
+              tma_load_2d(db, &map_b, &full[stage], kb * kBK, b_row, policy_b);
+            }
           }
         }
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -260,82 +334,94 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         issued_mask |= 1u << stage;
         issued_phase_bits = (issued_phase_bits & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
+        if (++stage == S::stages) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
-    // Drain: every copy this warp issued lands before the CTA exits.
-    if (lane == 0) {
-      for (int s = 0; s < kStages; ++s)
+    // Drain: every copy this CTA issued lands before the CTA exits.  A pair's
+    // copies complete on the leader's barriers, so the leader drains for both.
+    if (lane == 0 && leader) {
+      for (int s = 0; s < S::stages; ++s)
         if (issued_mask & (1u << s))
           mbar_wait_bounded(&full[s], (issued_phase_bits >> s) & 1u, nullptr, status, 12, p.timeout_ns);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    int stage = 0, acc = 0;
-    uint32_t phase = 0, acc_phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
-      int got = 0;
-      if (lane == 0) {
-        got = mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort, status, 21, p.timeout_ns) ? 1 : 0;
-        if (got) tc_fence_after();
-      }
-      if (!__shfl_sync(0xffffffffu, got, 0)) break;
-      const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        got = 0;
+    // ---------------- MMA issuer (the pair leader only) ----------------
+    if (leader) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = unit; ok && tile < p.tiles; tile += units) {
+        int got = 0;
         if (lane == 0) {
-          got = mbar_wait_bounded(&full[stage], phase, abort, status, 22, p.timeout_ns) ? 1 : 0;
-          if (got) {
-            tc_fence_after();
-            const uint64_t a_desc = smem_desc_k_sw128(smem_a + stage * kATileBytes);
-            const uint64_t b_desc = smem_desc_k_sw128(smem_b + stage * kBTileBytes);
+          got = mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort, status, 21, p.timeout_ns) ? 1 : 0;
+          if (got) tc_fence_after();
+        }
+        if (!__shfl_sync(0xffffffffu, got, 0)) break;
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          got = 0;
+          if (lane == 0) {
+            got = mbar_wait_bounded(&full[stage], phase, abort, status, 22, p.timeout_ns) ? 1 : 0;
+            if (got) {
+              tc_fence_after();
+              const uint64_t a_desc = smem_desc_k_sw128(smem_a + stage * kATileBytes);
+              const uint64_t b_desc = smem_desc_k_sw128(smem_b + stage * S::b_tile_bytes);
 #pragma unroll
-            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-              // +32 bytes along K inside the swizzle atom = +2 in the 16-byte address field
-              mma_i8(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), kIdesc,
-                     (kb > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                // +32 bytes along K inside the swizzle atom = +2 in the 16-byte address field
+                const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                if constexpr (kPair)
+                  mma_i8_pair(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
+                else
+                  mma_i8(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
+              }
+              if constexpr (kPair) mma_commit_pair(&empty[stage], 0x3);   // frees the stage in both CTAs
+              else mma_commit(&empty[stage]);
             }
-            mma_commit(&empty[stage]);
+          }
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          if (++stage == S::stages) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-          ok = false;
-          break;
+        if (!ok) break;
+        if (lane == 0) {
+          if constexpr (kPair) mma_commit_pair(&tfull[acc], 0x3);   // both CTAs' epilogues
+          else mma_commit(&tfull[acc]);
         }
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+        __syncwarp();
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
         }
       }
-      if (!ok) break;
-      if (lane == 0) mma_commit(&tfull[acc]);
+      // Drain: every MMA issued by this warp completes before TMEM is released.
+      if (lane == 0) {
+        if constexpr (kPair) mma_commit_pair(drain, 0x1);
+        else mma_commit(drain);
+        mbar_wait_bounded(drain, 0, nullptr, status, 23, p.timeout_ns);
+      }
       __syncwarp();
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
     }
-    // Drain: every MMA issued by this warp completes before TMEM is released.
-    if (lane == 0) {
-      mma_commit(drain);
-      mbar_wait_bounded(drain, 0, nullptr, status, 23, p.timeout_ns);
-    }
-    __syncwarp();
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue (both CTAs of a pair) ----------------
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;        // column half of the tile
     const int ep_tid = threadIdx.x - 64;     // 0..255
-    uint8_t* stage = smem + SmemLayout::stage + (warp - 2) * SmemLayout::stage_warp_bytes;
+    uint8_t* stage = smem + L::stage + (warp - 2) * L::stage_warp_bytes;
+    const uint32_t tempty_leader = kPair ? map_to_rank(smem_addr(tempty), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+    for (int tile = unit; tile < p.tiles; tile += units) {
       int mt, nt;
       tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
       const int n0 = nt * kBN;
@@ -349,12 +435,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // One thread waits for the accumulator; the named barrier hands the
-      // outcome to the other 127 so all of them leave or continue together.
+      // outcome to the other 255 so all of them leave or continue together.
       if (ep_tid == 0) *ready = mbar_wait_bounded(&tfull[acc], acc_phase, abort, status, 31, p.timeout_ns) ? 1 : 0;
       epilogue_sync();
       if (*ready == 0) break;
       tc_fence_after();
-      const int row_base = mt * kBM + quarter * 32;
+      const int row_base = mt * S::tile_m + int(rank) * kBM + quarter * 32;
       const int row = row_base + lane;
       const bool row_ok = row < p.m;
       const float xs_row = (kEpi != kEpiAcc && row_ok) ? p.xs[row] : 0.0f;
@@ -368,8 +454,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_load_32cols(t_row + uint32_t(c * 32), r);
         tmem_load_wait();
         if (c == (half + 1) * (kBN / 64) - 1) {
+          // This warp's last read of the accumulator: release it to the MMA issuer.
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_remote(tempty_leader + uint32_t(acc) * 8u);
+            else mbar_arrive(&tempty[acc]);
+          }
         }
         const int col0 = n0 + c * 32;
         if constexpr (kEpi == kEpiAcc) {
@@ -405,11 +496,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  __syncthreads();
+  // The pair's TMEM is written by the leader's MMAs and its barriers receive the
+  // peer's arrivals: neither CTA releases TMEM or exits before both are done.
+  tc_fence_before();
+  if constexpr (kPair) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -436,7 +532,7 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int* status
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t done;
   __shared__ uint32_t slot;
-  for (int i = threadIdx.x; i < kStageBytes / 16; i += blockDim.x)
+  for (int i = threadIdx.x; i < Shape<false>::stage_bytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
   if (threadIdx.x == 0) {
     mbar_init(&done, 1);
@@ -458,7 +554,7 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int* status
       const uint64_t b_desc = smem_desc_k_sw128(smem + kATileBytes);
       for (int i = 0; i < iters; ++i) {
         const int kk = i & 3;
-        mma_i8(tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), kIdesc, i > 0 ? 1u : 0u);
+        mma_i8(tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), Shape<false>::idesc, i > 0 ? 1u : 0u);
       }
       mma_commit(&done);
       mbar_wait_bounded(&done, 0, nullptr, status, 41, kWaitTimeoutNs);
@@ -529,7 +625,8 @@ bool make_output_map(CUtensorMap* map, const void* base, int rows, int cols, int
 
 struct DeviceInfo {
   int sms = 0;
-  bool attrs_set[4] = {false, false, false, false};
+  bool attrs_set[2][4] = {};
+  int max_pairs[4] = {};     // co-resident clusters of two CTAs, per epilogue kind
 };
 
 DeviceInfo& device_info(int device) {
@@ -547,24 +644,52 @@ int* status_ptr() {
   return ptr;
 }
 
-template <int kEpi>
+template <int kEpi, bool kPair>
 cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, GemmParams p,
                         cudaStream_t stream) {
+  using L = SmemLayout<kPair>;
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
   DeviceInfo& info = device_info(device);
-  auto kernel = int8_gemm_persistent<kEpi>;
-  if (!info.attrs_set[kEpi]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::dynamic_bytes);
+  auto kernel = int8_gemm_persistent<kEpi, kPair>;
+  if (!info.attrs_set[kPair][kEpi]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::dynamic_bytes);
     if (e != cudaSuccess) return e;
-    info.attrs_set[kEpi] = true;
+    info.attrs_set[kPair][kEpi] = true;
   }
   p.status = status_ptr();
   if (!p.status) return cudaErrorInvalidSymbol;
-  const int grid = p.tiles < info.sms ? p.tiles : info.sms;
-  kernel<<<grid, kThreads, SmemLayout::dynamic_bytes, stream>>>(ma, mb, md, p);
-  return cudaGetLastError();
+  if constexpr (!kPair) {
+    const int grid = p.tiles < info.sms ? p.tiles : info.sms;
+    kernel<<<grid, kThreads, L::dynamic_bytes, stream>>>(ma, mb, md, p);
+    return cudaGetLastError();
+  } else {
+    // As many clusters of two CTAs as can be resident at once (SMs of a GPC pair
+    // up; an odd SM stays idle), no more than there are tiles.
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::dynamic_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (info.max_pairs[kEpi] == 0) {
+      cfg.gridDim = dim3(unsigned(info.sms & ~1));
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+      if (clusters < 1) return cudaErrorInvalidConfiguration;
+      info.max_pairs[kEpi] = clusters;
+    }
+    const int pairs = p.tiles < info.max_pairs[kEpi] ? p.tiles : info.max_pairs[kEpi];
+    cfg.gridDim = dim3(unsigned(2 * pairs));
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, md, p);
+  }
 }
 
 int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
@@ -582,8 +707,11 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
         (uintptr_t(rows) & 3u))
       return fail(cudaErrorInvalidValue, "h3_int8_gate: gate/rows/residual null or misaligned");
   }
+  // CTA pairs whenever the problem has more than one 128-row tile row.
+  const bool pair = M > kBM;
   CUtensorMap ma, mb, md;
-  if (!make_operand_map(&ma, A, M, K, kBM) || !make_operand_map(&mb, B, N, K, kBN))
+  if (!make_operand_map(&ma, A, M, K, kBM) ||
+      !make_operand_map(&mb, B, N, K, pair ? Shape<true>::b_rows : Shape<false>::b_rows))
     return fail(cudaErrorInvalidValue, "h3_int8: tensor map encoding failed");
   std::memset(&md, 0, sizeof(md));
   if (epi != kEpiAcc && !make_output_map(&md, D, M, N, ldd))
@@ -602,17 +730,26 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.m = M;
   p.n = N;
   p.k = K;
-  p.m_tiles = (M + kBM - 1) / kBM;
+  p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.tiles = p.m_tiles * p.n_tiles;
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
-  switch (epi) {
-    case kEpiDequant: e = launch_gemm<kEpiDequant>(ma, mb, md, p, stream); break;
-    case kEpiGelu: e = launch_gemm<kEpiGelu>(ma, mb, md, p, stream); break;
-    case kEpiGate: e = launch_gemm<kEpiGate>(ma, mb, md, p, stream); break;
-    default: e = launch_gemm<kEpiAcc>(ma, mb, md, p, stream); break;
+  if (pair) {
+    switch (epi) {
+      case kEpiDequant: e = launch_gemm<kEpiDequant, true>(ma, mb, md, p, stream); break;
+      case kEpiGelu: e = launch_gemm<kEpiGelu, true>(ma, mb, md, p, stream); break;
+      case kEpiGate: e = launch_gemm<kEpiGate, true>(ma, mb, md, p, stream); break;
+      default: e = launch_gemm<kEpiAcc, true>(ma, mb, md, p, stream); break;
+    }
+  } else {
+    switch (epi) {
+      case kEpiDequant: e = launch_gemm<kEpiDequant, false>(ma, mb, md, p, stream); break;
+      case kEpiGelu: e = launch_gemm<kEpiGelu, false>(ma, mb, md, p, stream); break;
+      case kEpiGate: e = launch_gemm<kEpiGate, false>(ma, mb, md, p, stream); break;
+      default: e = launch_gemm<kEpiAcc, false>(ma, mb, md, p, stream); break;
+    }
   }
   if (e != cudaSuccess) return fail(e, "h3_int8: launch failed");
   t_last_error = 0;

@@ -233,7 +233,8 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
   const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
   const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
   unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
-  unsigned char* xbuf = ring + size_t(D) * plan.slot_bytes + size_t(g) * rs::kHalfGroupBytes;
+  const uint32_t ring_a = sm100::smem_addr(ring);
+  const uint32_t xbuf_a = ring_a + uint32_t(D * plan.slot_bytes + g * rs::kHalfGroupBytes);
   uint64_t* full = st.full + team * D;
   const int bar_id = 1 + team;
   const int nchunks = K / 4;       // 8-byte chunks of the sum of squares
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
   for (; k < n_team; ++k, parity ^= 1) {
     const int64_t row = int64_t(blockIdx.x) + int64_t(team + k * teams) * grid;
     const bool ok = sm100::mbar_wait_bounded(&full[d], ph, nullptr, status, rs::kCodeFull, rs::kWaitNs);
-    unsigned char* row_buf = ring + size_t(d) * plan.slot_bytes;
+    const uint32_t row_a = ring_a + uint32_t(d * plan.slot_bytes);
 
     // 2. sum of squares
     if (tt < 64) {
@@ -265,8 +266,8 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
 #pragma unroll 4
       for (int base = 0; base < nchunks; base += 128) {
         const int c0 = base + tt, c1 = base + tt + 64;
-        const uint2 r0 = c0 < nchunks ? *reinterpret_cast<const uint2*>(row_buf + rs::swz128(8u * c0)) : make_uint2(0, 0);
-        const uint2 r1 = c1 < nchunks ? *reinterpret_cast<const uint2*>(row_buf + rs::swz128(8u * c1)) : make_uint2(0, 0);
+        const uint2 r0 = c0 < nchunks ? rs::lds64(row_a + rs::swz128(8u * c0)) : make_uint2(0, 0);
+        const uint2 r1 = c1 < nchunks ? rs::lds64(row_a + rs::swz128(8u * c1)) : make_uint2(0, 0);
         uint64_t e;
         e = rq::f2_pack(__uint_as_float(r0.x << 16), __uint_as_float(r1.x << 16));
         acc = rq::f2_fma_ieee(e, e, acc);
@@ -301,8 +302,8 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
       const uint64_t rr = rq::f2_pack(rrms, rrms);
       const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
       for (int c = tt; c < nchunks16; c += team_threads) {
-        uint4* p = reinterpret_cast<uint4*>(row_buf + rs::swz128(16u * c));
-        const uint4 xv = *p;
+        const uint32_t pa = row_a + rs::swz128(16u * c);
+        const uint4 xv = rs::lds128(pa);
         const uint4 wv = load8(W + 8 * c, w_vec16);
         const uint4 sv = table8<ModT>(shift_row + 8 * c, t_vec16);
         const uint4 cv = table8<ModT>(scale_row + 8 * c, t_vec16);
@@ -314,7 +315,7 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
           const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
           nw[h] = rq::bf2_add(rq::bf2_mul(rq::f2_to_bf2(t), rq::bf2_add(one2, cw[h])), sw[h]);
         }
-        *p = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+        rs::sts128(pa, nw[0], nw[1], nw[2], nw[3]);
       }
     }
     rs::team_sync(bar_id, team_threads);   // barrier B: the modulated row is complete
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     uint64_t v[32];
     if (active) {
       uint4 raw[8];
-      rs::load_row_a(row_buf, g, q, raw);
+      rs::load_row_a(row_a, g, q, raw);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         v[4 * i + 0] = rq::bf2_to_f2(raw[i].x);
@@ -339,13 +340,14 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     // TMA (async proxy) that refills it.
     sm100::fence_async_shared();
     rq::fht_layout_a(v);
-    rs::exchange_a_to_b_halves(v, xbuf, q, g & 1);
+    rs::exchange_a_to_b_halves(v, xbuf_a, q, g & 1);
     rq::fht_layout_b(v);
     const float local = warp_allmax(rq::absmax64(v));
     if (lane == 0) st.max_fold[team][parity][twarp] = local;
     rs::team_sync(bar_id, team_threads);   // barrier C
     if (tt == 0 && issued < n_team) {
-      rs::issue_row(&map_x, row_buf, &full[d], int(blockIdx.x) + (team + issued * teams) * grid, K, K);
+      rs::issue_row(&map_x, ring + size_t(d) * plan.slot_bytes, &full[d], int(blockIdx.x) + (team + issued * teams) * grid,
+                    K, K);
       ++issued;
     }
     if (++d == D) { d = 0; ph ^= 1u; }

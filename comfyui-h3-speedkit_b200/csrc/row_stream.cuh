@@ -91,14 +91,30 @@ __device__ __forceinline__ bool team_sync_and(int id, int threads, bool ok) {
   return all != 0;
 }
 
-// Layout-A inputs of team thread (group g, q) from a swizzled row: the 64
-// consecutive BF16 values [256g + 64q, +64) as 8 16-byte words (line 4g + q).
-__device__ __forceinline__ void load_row_a(const unsigned char* row, int g, int q, uint4 (&raw)[8]) {
+// Shared-memory vector access through 32-bit shared-window addresses (keeps
+// addresses in one register each).
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// Layout-A inputs of team thread (group g, q) from a swizzled row at shared
+// address `row`: the 64 consecutive BF16 values [256g + 64q, +64) as 8 16-byte
+// words (line 4g + q).
+__device__ __forceinline__ void load_row_a(uint32_t row, int g, int q, uint4 (&raw)[8]) {
   const uint32_t line = uint32_t(4 * g + q);
-  const uint32_t key = (line & 7u) << 4;
+  const uint32_t base = row + line * 128u, key = (line & 7u) << 4;
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    raw[i] = *reinterpret_cast<const uint4*>(row + ((line * 128u + 16u * uint32_t(i)) ^ key));
+  for (int i = 0; i < 8; ++i) raw[i] = lds128(base + ((16u * uint32_t(i)) ^ key));
 }
 
 // ---- exchange A -> B in two halves through a 512-byte buffer per group --------
@@ -109,21 +125,20 @@ __device__ __forceinline__ void load_row_a(const unsigned char* row, int g, int 
 //   line b4b5, bank slot (b4b5 ^ b6b7) | ((b2 ^ odd) << 2)
 // so the 8 lanes of each quarter-warp phase (two groups x four threads) hit 8
 // distinct bank slots on both the writing and the reading side.
-__device__ __forceinline__ uint32_t half_slot(int b2, int b45, int b67, int odd) {
-  return uint32_t(b45 * 128 + ((((b45 ^ b67) | ((b2 ^ odd) << 2))) << 4));
-}
-
+// `buf` = shared address of the group's 512-byte buffer.  With q and odd fixed
+// per thread, the writer's slot for (b2, b45) is  b45*128 + (wkey ^ (b45 << 4 | b2 << 6))
+// with wkey = q << 4 | odd << 6, and the reader's slot for (b2, b67) is
+// q*128 + (wkey ^ (b67 << 4 | b2 << 6)) -- one XOR and one add per access.
 template <int kHalf>
-__device__ __forceinline__ void exchange_half(uint64_t (&v)[32], unsigned char* buf, int q, int odd) {
+__device__ __forceinline__ void exchange_half(uint64_t (&v)[32], uint32_t buf, uint32_t wkey, uint32_t rbase) {
   // layout A (thread q = b6b7): chunk k = b2 | b3 << 1 | b4b5 << 2 in registers 2k, 2k+1
 #pragma unroll
   for (int b45 = 0; b45 < 4; ++b45) {
 #pragma unroll
     for (int b2 = 0; b2 < 2; ++b2) {
       const int k = b2 | (kHalf << 1) | (b45 << 2);
-      *reinterpret_cast<uint4*>(buf + half_slot(b2, b45, q, odd)) =
-          make_uint4(uint32_t(v[2 * k]), uint32_t(v[2 * k] >> 32), uint32_t(v[2 * k + 1]),
-                     uint32_t(v[2 * k + 1] >> 32));
+      const uint32_t addr = buf + uint32_t(b45 * 128) + (wkey ^ uint32_t((b45 << 4) | (b2 << 6)));
+      sts128(addr, uint32_t(v[2 * k]), uint32_t(v[2 * k] >> 32), uint32_t(v[2 * k + 1]), uint32_t(v[2 * k + 1] >> 32));
     }
   }
   __syncwarp();
@@ -133,7 +148,7 @@ __device__ __forceinline__ void exchange_half(uint64_t (&v)[32], unsigned char* 
 #pragma unroll
     for (int b2 = 0; b2 < 2; ++b2) {
       const int m = b2 | (kHalf << 1) | (b67 << 2);
-      const uint4 c = *reinterpret_cast<const uint4*>(buf + half_slot(b2, q, b67, odd));
+      const uint4 c = lds128(rbase + (wkey ^ uint32_t((b67 << 4) | (b2 << 6))));
       v[2 * m] = (uint64_t(c.y) << 32) | c.x;
       v[2 * m + 1] = (uint64_t(c.w) << 32) | c.z;
     }
@@ -141,9 +156,12 @@ __device__ __forceinline__ void exchange_half(uint64_t (&v)[32], unsigned char* 
   __syncwarp();
 }
 
-__device__ __forceinline__ void exchange_a_to_b_halves(uint64_t (&v)[32], unsigned char* buf, int q, int odd) {
-  exchange_half<0>(v, buf, q, odd);
-  exchange_half<1>(v, buf, q, odd);
+// buf: shared address of this group's buffer; q: team index; odd: group parity.
+__device__ __forceinline__ void exchange_a_to_b_halves(uint64_t (&v)[32], uint32_t buf, int q, int odd) {
+  const uint32_t wkey = (uint32_t(q) << 4) | (uint32_t(odd) << 6);
+  const uint32_t rbase = buf + uint32_t(q) * 128u;
+  exchange_half<0>(v, buf, wkey, rbase);
+  exchange_half<1>(v, buf, wkey, rbase);
 }
 
 // ---- shared state of a streaming CTA ---------------------------------------------

@@ -158,11 +158,21 @@ __device__ __forceinline__ void exchange_a_to_b(uint64_t (&v)[32], float* buf, i
 }
 
 // ---- absmax, scale, codes ---------------------------------------------------------
+// Three-input max (sm_100 max.f32 with three sources; NaN inputs are ignored like
+// fmaxf's).  The order of a max reduction does not change its value.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ float absmax64(const uint64_t (&v)[32]) {
-  float m = 0.0f;
+  float m0 = 0.0f, m1 = 0.0f;
 #pragma unroll
-  for (int p = 0; p < 32; ++p) m = fmaxf(m, fmaxf(fabsf(f2_lo(v[p])), fabsf(f2_hi(v[p]))));
-  return m;
+  for (int p = 0; p < 32; p += 2) {
+    m0 = fmax3(m0, fabsf(f2_lo(v[p])), fabsf(f2_hi(v[p])));
+    m1 = fmax3(m1, fabsf(f2_lo(v[p + 1])), fabsf(f2_hi(v[p + 1])));
+  }
+  return fmaxf(m0, m1);
 }
 
 // Codes of four consecutive values (two pairs) packed little-endian.

@@ -44,6 +44,19 @@ def test_accumulators_exact(device, m, n, k):
     assert _lib.pipeline_status() == 0
 
 
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 1024), (5000, 1032, 512)])
+def test_accumulators_exact_many_tiles(device, m, n, k):
+    """Many tiles per CTA pair (every pair walks several tiles, both accumulators
+    and every pipeline stage wrap), checked against torch._int_mm (cuBLAS) as the
+    reference for int32 accumulators."""
+    a, w, *_ = _operands(m, n, k, m + n + k, device)
+    acc = gemm.int8_accumulators(a, w)
+    ref = torch._int_mm(a, w.t())
+    torch.cuda.synchronize()
+    assert torch.equal(acc, ref)
+    assert _lib.pipeline_status() == 0
+
+
 @pytest.mark.parametrize("m,n,k", SHAPES[:5])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_dequant_bitexact(device, m, n, k, with_bias):
@@ -178,3 +191,4 @@ def test_bounded_wait_selftest(device):
     acc = gemm.int8_accumulators(a, w)
     torch.cuda.synchronize()
     assert np.array_equal(np_(acc), ocpu.gemm_s32(np_(a), np_(w)))
+

@@ -154,3 +154,20 @@ def test_prologue_stream_misaligned_vectors(device, m):
     rq, rqs = ref_gpu.norm_quant(x, w, shift, scale, rows, 1e-6)
     torch.cuda.synchronize()
     assert torch.equal(q, rq) and torch.equal(qs, rqs)
+
+
+def test_quant_nan_rows_match_reference(device):
+    """NaN inputs: the row absmax ignores them (fmaxf semantics) and their codes
+    are -128, in the streaming kernel, the row kernel and the reference."""
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn((600, 4096), generator=g) * 2).to(torch.bfloat16).to(device)
+    x[5, 3] = float("nan")
+    x[6, :] = float("nan")
+    x[7, 4095] = float("nan")
+    q0, s0 = _register(x, 0)
+    q1, s1 = _register(x, 1)
+    rq, rs = ref_gpu.kitchen_quant(x, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(s0.reshape(-1).view(torch.int32), rs.view(torch.int32))
+    assert torch.equal(s1, s0) and torch.equal(q1, q0)
+    assert torch.equal(q0, rq)

@@ -151,9 +151,12 @@ __global__ void __launch_bounds__(512, 1) convrot_quant_stream(
   const int grid = int(gridDim.x);
   const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
   const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
-  unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
+  unsigned char* ring = smem + size_t(team) * size_t(D) * plan.slot_bytes;
   const uint32_t ring_a = sm100::smem_addr(ring);
-  const uint32_t xbuf_a = ring_a + uint32_t(D * plan.slot_bytes + g * rs::kHalfGroupBytes);
+  // This group's 512-byte exchange buffer after the rings (the host only takes
+  // this kernel with plan.exch_bytes > 0): the slots see generic reads only.
+  const uint32_t xbuf_a =
+      sm100::smem_addr(smem) + uint32_t(plan.ring_bytes + team * plan.exch_bytes + g * rs::kHalfGroupBytes);
   uint64_t* full = st.full + team * D;
   const int bar_id = 1 + team;
 
@@ -225,7 +228,7 @@ cudaError_t launch_stream(const void* x, int64_t xs, void* q, void* scale, int64
   if ((uintptr_t(x) & 15u) || (xs % 8)) return cudaSuccess;
   const int width = kAct == kActSwiGLU ? 2 * k : k;
   const rs::Plan plan = rs::make_plan(k, width, 32);
-  if (plan.teams < 1 || plan.slots_per_team < 2) return cudaSuccess;
+  if (plan.teams < 1 || plan.slots_per_team < 2 || plan.exch_bytes == 0) return cudaSuccess;
   CUtensorMap map;
   if (!rs::make_row_map(&map, x, rows, width, k, xs)) return cudaSuccess;
   auto kernel = convrot_quant_stream<kAct>;

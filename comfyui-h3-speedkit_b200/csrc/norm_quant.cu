@@ -31,6 +31,7 @@ namespace {
 
 constexpr int kMaxK = 16384;
 constexpr int kNormK = 5376;        // K of the unsuffixed (reference) entry point
+constexpr int kModBatch = 2;        // chunks per modulation round of the streaming prologue
 
 __host__ __device__ constexpr int norm_threads(int k) {
   return ((k / 64 + 31) / 32) * 32 < 64 ? 64 : ((k / 64 + 31) / 32) * 32;
@@ -213,13 +214,17 @@ __global__ void __launch_bounds__(256) norm_quant_rows(
 //     stages 1-3, two-half exchange, stage 4, absmax; barrier C, after which
 //     thread 0 refills the slot with the team's next-but-D row;
 //  5. row scale and codes.
+// kStaged (the number of tables T is known and W plus T tables fit in shared
+// memory): every CTA first stages W, bf(1 + bf(scale_t)) and bf(shift_t) for all
+// tables in shared memory with the rows' 128-byte swizzle, and step 3 happens in
+// layout A straight from shared memory -- no modulation pass, no barrier B.
 // The arithmetic is that of norm_quant_rows, value for value.
-template <class ModT>
+template <class ModT, bool kStaged, bool kInSlot>
 __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     const __grid_constant__ CUtensorMap map_x, const __nv_bfloat16* __restrict__ W,
     const ModT* __restrict__ Shift, const ModT* __restrict__ Scale, const int32_t* __restrict__ Rows,
     int8_t* __restrict__ Q, float* __restrict__ QScale, int64_t ss, int64_t cs, float eps, int64_t M,
-    const rs::Plan plan, int w_vec16, int t_vec16, int q_vec16, int* status) {
+    const rs::Plan plan, int tables, int w_vec16, int t_vec16, int q_vec16, int* status) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ rs::RingState st;
   unsigned char* smem =
@@ -232,13 +237,43 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
   const int grid = int(gridDim.x);
   const int n_local = int((M - int64_t(blockIdx.x) + grid - 1) / grid);
   const int n_team = team < n_local ? (n_local - team + teams - 1) / teams : 0;
-  unsigned char* ring = smem + size_t(team) * (size_t(D) * plan.slot_bytes + plan.exch_bytes);
+  unsigned char* ring = smem + size_t(team) * size_t(D) * plan.slot_bytes;
   const uint32_t ring_a = sm100::smem_addr(ring);
-  const uint32_t xbuf_a = ring_a + uint32_t(D * plan.slot_bytes + g * rs::kHalfGroupBytes);
+  // This group's 512-byte exchange region: its own buffer after the rings, or
+  // (exch_bytes == 0) its part of the row slot it has just read.
+  const uint32_t group_off = uint32_t(g * rs::kHalfGroupBytes);
+  const uint32_t xbuf_a = sm100::smem_addr(smem) + uint32_t(plan.ring_bytes + team * plan.exch_bytes) + group_off;
   uint64_t* full = st.full + team * D;
   const int bar_id = 1 + team;
   const int nchunks = K / 4;       // 8-byte chunks of the sum of squares
   const int nchunks16 = K / 8;     // 16-byte chunks of the modulation pass
+
+  // Staged arrays (kStaged): W, then (onec, shift) per table, each K BF16 values
+  // in its own 1024-byte aligned block, 16-byte chunk c at swz128(16 c).
+  const uint32_t arr_bytes = uint32_t((K * 2 + 1023) / 1024 * 1024);
+  const uint32_t w_a = sm100::smem_addr(smem) + uint32_t(plan.ring_bytes + plan.teams * plan.exch_bytes);
+  if constexpr (kStaged) {
+    const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
+    const int per_array = K / 8;
+    for (int j = tid; j < per_array * (1 + 2 * tables); j += blockDim.x) {
+      const int arr = j / per_array, c = j - arr * per_array;
+      uint4 val;
+      if (arr == 0) {
+        val = load8(W + 8 * c, w_vec16);
+      } else {
+        const int t = (arr - 1) >> 1;
+        if ((arr - 1) & 1) {
+          val = table8<ModT>(Shift + int64_t(t) * ss + 8 * c, t_vec16);
+        } else {
+          const uint4 cv = table8<ModT>(Scale + int64_t(t) * cs + 8 * c, t_vec16);
+          val = make_uint4(rq::bf2_add(one2, cv.x), rq::bf2_add(one2, cv.y), rq::bf2_add(one2, cv.z),
+                           rq::bf2_add(one2, cv.w));
+        }
+      }
+      rs::sts128(w_a + uint32_t(arr) * arr_bytes + rs::swz128(16u * uint32_t(c)), val.x, val.y, val.z, val.w);
+    }
+    __syncthreads();
+  }
 
   int issued = 0;
   if (tt == 0) {
@@ -294,53 +329,101 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     const float total = ieee_add(ieee_add(f[0], f[2]), ieee_add(f[1], f[3]));
     const float rrms = hw_rsqrt(ieee_add(ieee_div(total, static_cast<float>(K)), eps));
 
-    // 3. modulation pass, in place
-    {
-      const int table_row = __ldg(Rows + row);
-      const ModT* shift_row = Shift + static_cast<int64_t>(table_row) * ss;
-      const ModT* scale_row = Scale + static_cast<int64_t>(table_row) * cs;
-      const uint64_t rr = rq::f2_pack(rrms, rrms);
-      const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
-      for (int c = tt; c < nchunks16; c += team_threads) {
-        const uint32_t pa = row_a + rs::swz128(16u * c);
-        const uint4 xv = rs::lds128(pa);
-        const uint4 wv = load8(W + 8 * c, w_vec16);
-        const uint4 sv = table8<ModT>(shift_row + 8 * c, t_vec16);
-        const uint4 cv = table8<ModT>(scale_row + 8 * c, t_vec16);
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
-        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, cw[4] = {cv.x, cv.y, cv.z, cv.w};
-        uint32_t nw[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
-          nw[h] = rq::bf2_add(rq::bf2_mul(rq::f2_to_bf2(t), rq::bf2_add(one2, cw[h])), sw[h]);
-        }
-        rs::sts128(pa, nw[0], nw[1], nw[2], nw[3]);
-      }
-    }
-    rs::team_sync(bar_id, team_threads);   // barrier B: the modulated row is complete
-
-    // 4. ConvRot256 + absmax
     uint64_t v[32];
-    if (active) {
-      uint4 raw[8];
-      rs::load_row_a(row_a, g, q, raw);
+    if constexpr (kStaged) {
+      // 3+4. modulation in layout A from the staged arrays
+      const int table_row = min(max(__ldg(Rows + row), 0), tables - 1);   // memory-safe for bad row maps
+      const uint32_t c_a = w_a + uint32_t(1 + 2 * table_row) * arr_bytes;
+      const uint32_t s_a = c_a + arr_bytes;
+      if (active) {
+        const uint64_t rr = rq::f2_pack(rrms, rrms);
+        const uint32_t line = uint32_t(4 * g + q), key = (line & 7u) << 4;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[4 * i + 0] = rq::bf2_to_f2(raw[i].x);
-        v[4 * i + 1] = rq::bf2_to_f2(raw[i].y);
-        v[4 * i + 2] = rq::bf2_to_f2(raw[i].z);
-        v[4 * i + 3] = rq::bf2_to_f2(raw[i].w);
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t off = line * 128u + ((16u * uint32_t(i)) ^ key);
+          const uint4 xv = rs::lds128(row_a + off), wv = rs::lds128(w_a + off);
+          const uint4 cv = rs::lds128(c_a + off), sv = rs::lds128(s_a + off);
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+          const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
+            v[4 * i + h] = rq::bf2_to_f2(rq::bf2_add(rq::bf2_mul(rq::f2_to_bf2(t), cw[h]), sw[h]));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int p = 0; p < 32; ++p) v[p] = 0;
       }
     } else {
-#pragma unroll
-      for (int p = 0; p < 32; ++p) v[p] = 0;
+      // 3. modulation pass, in place
+      {
+        const int table_row = __ldg(Rows + row);
+        const ModT* shift_row = Shift + static_cast<int64_t>(table_row) * ss;
+        const ModT* scale_row = Scale + static_cast<int64_t>(table_row) * cs;
+        const uint64_t rr = rq::f2_pack(rrms, rrms);
+        const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
+        // kModBatch chunks per round, all loads first: the shared stores are ordered
+        // asm, so batching is what lets the loads of a round overlap.
+        for (int c0 = tt; c0 < nchunks16; c0 += kModBatch * team_threads) {
+          uint4 xv[kModBatch], wv[kModBatch], sv[kModBatch], cv[kModBatch];
+          uint32_t pa[kModBatch];
+  #pragma unroll
+          for (int u = 0; u < kModBatch; ++u) {
+            const int c = c0 + u * team_threads;
+            if (c < nchunks16) {
+              pa[u] = row_a + rs::swz128(16u * c);
+              xv[u] = rs::lds128(pa[u]);
+              wv[u] = load8(W + 8 * c, w_vec16);
+              sv[u] = table8<ModT>(shift_row + 8 * c, t_vec16);
+              cv[u] = table8<ModT>(scale_row + 8 * c, t_vec16);
+            }
+          }
+  #pragma unroll
+          for (int u = 0; u < kModBatch; ++u) {
+            if (c0 + u * team_threads >= nchunks16) continue;
+            const uint32_t xw[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+            const uint32_t ww[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+            const uint32_t sw[4] = {sv[u].x, sv[u].y, sv[u].z, sv[u].w};
+            const uint32_t cw[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w};
+            uint32_t nw[4];
+  #pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const uint64_t t = rq::f2_mul_ieee(rq::bf2_to_f2(ww[h]), rq::f2_mul_ieee(rr, rq::bf2_to_f2(xw[h])));
+              nw[h] = rq::bf2_add(rq::bf2_mul(rq::f2_to_bf2(t), rq::bf2_add(one2, cw[h])), sw[h]);
+            }
+            rs::sts128(pa[u], nw[0], nw[1], nw[2], nw[3]);
+          }
+        }
+      }
+      rs::team_sync(bar_id, team_threads);   // barrier B: the modulated row is complete
+
+      // 4. ConvRot256 + absmax
+      if (active) {
+        uint4 raw[8];
+        rs::load_row_a(row_a, g, q, raw);
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[4 * i + 0] = rq::bf2_to_f2(raw[i].x);
+          v[4 * i + 1] = rq::bf2_to_f2(raw[i].y);
+          v[4 * i + 2] = rq::bf2_to_f2(raw[i].z);
+          v[4 * i + 3] = rq::bf2_to_f2(raw[i].w);
+        }
+      } else {
+  #pragma unroll
+        for (int p = 0; p < 32; ++p) v[p] = 0;
+      }
     }
-    // This thread's generic-proxy writes to the slot must be ordered before the
-    // TMA (async proxy) that refills it.
-    sm100::fence_async_shared();
     rq::fht_layout_a(v);
-    rs::exchange_a_to_b_halves(v, xbuf_a, q, g & 1);
+    if constexpr (kInSlot) {
+      __syncwarp();   // the group's layout-A reads of its region come first
+      rs::exchange_a_to_b_halves(v, row_a + group_off, q, g & 1);
+    } else {
+      rs::exchange_a_to_b_halves(v, xbuf_a, q, g & 1);
+    }
+    // This thread's generic-proxy writes to the slot (modulation pass, in-slot
+    // exchange) are ordered before the TMA (async proxy) that refills it.
+    if constexpr (!kStaged || kInSlot) sm100::fence_async_shared();
     rq::fht_layout_b(v);
     const float local = warp_allmax(rq::absmax64(v));
     if (lane == 0) st.max_fold[team][parity][twarp] = local;
@@ -390,9 +473,10 @@ int query_kernel(int k, H3NormQuantResources* out) {
 
 bool valid_k(int64_t k) { return k >= 256 && k <= kMaxK && k % 256 == 0; }
 
+// tables: number of table rows T (shift/scale are [T, >=K]); 0 = not known.
 int run_checked(const void* x, const void* w, const void* shift, const void* scale,
                 const void* rows, void* q, void* qscale, void* dn, void* dr, void* drs,
-                int64_t m, int64_t k, int64_t xs, int64_t ss, int64_t cs, float eps,
+                int64_t m, int64_t k, int64_t tables, int64_t xs, int64_t ss, int64_t cs, float eps,
                 int table_dtype, int debug, uintptr_t stream_ptr) {
   // Contract of norm_quant.cu:247-255, with K a runtime value.
   if (!valid_k(k)) return cudaErrorInvalidValue;
@@ -414,25 +498,43 @@ int run_checked(const void* x, const void* w, const void* shift, const void* sca
   const int t_vec16 = ((uintptr_t(shift) & 15u) == 0 && (uintptr_t(scale) & 15u) == 0 && (ss * tsz) % 16 == 0 &&
                        (cs * tsz) % 16 == 0) ? 1 : 0;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  if (tables < 0 || tables > INT32_MAX) return cudaErrorInvalidValue;
   if (!debug && x_vec16) {
     // Streaming kernel: TMA needs 16-byte aligned rows, which x_vec16 states.
-    const rs::Plan plan = rs::make_plan(int(k), int(k), 64);
+    // With T known and W plus T tables fitting beside two ring slots per team,
+    // the tables are staged in shared memory.
+    const int arr_bytes = int((k * 2 + 1023) / 1024 * 1024);
+    const int64_t staged_bytes = tables > 0 ? int64_t(arr_bytes) * (1 + 2 * tables) : -1;
+    rs::Plan plan = rs::make_plan(int(k), int(k), 64);
+    bool staged = false;
+    if (staged_bytes > 0 && staged_bytes <= rs::kSmemBudget) {
+      // Stage only when it costs no row team.
+      const rs::Plan sp = rs::make_plan(int(k), int(k), 64, int(staged_bytes));
+      if (sp.teams >= 1 && sp.teams == plan.teams && sp.smem <= rs::kSmemBudget) {
+        plan = sp;
+        staged = true;
+      }
+    }
     CUtensorMap map;
     if (plan.teams >= 1 && plan.slots_per_team >= 2 && rs::make_row_map(&map, x, m, int(k), int(k), xs)) {
       int* status = status_device_ptr();
       if (!status) return cudaErrorInvalidDevicePointer;
       int grid = 0;
-#define H3SK_NQ_STREAM(T)                                                                                   \
+#define H3SK_NQ_STREAM(T, S)                                                                                \
   do {                                                                                                      \
-    auto kernel = norm_quant_stream<T>;                                                                     \
+    auto kernel = plan.exch_bytes ? norm_quant_stream<T, S, false> : norm_quant_stream<T, S, true>;         \
     const cudaError_t e = rs::stream_grid(reinterpret_cast<const void*>(kernel), plan.smem, m, &grid);      \
     if (e != cudaSuccess) return e;                                                                         \
     kernel<<<grid, plan.threads, plan.smem, stream>>>(                                                      \
         map, static_cast<const __nv_bfloat16*>(w), static_cast<const T*>(shift), static_cast<const T*>(scale), \
         static_cast<const int32_t*>(rows), static_cast<int8_t*>(q), static_cast<float*>(qscale), ss, cs, eps, m, \
-        plan, w_vec16, t_vec16, q_vec16, status);                                                           \
+        plan, int(tables), w_vec16, t_vec16, q_vec16, status);                                              \
   } while (0)
-      if (table_dtype == 0) H3SK_NQ_STREAM(float); else H3SK_NQ_STREAM(__nv_bfloat16);
+      if (table_dtype == 0) {
+        if (staged) H3SK_NQ_STREAM(float, true); else H3SK_NQ_STREAM(float, false);
+      } else {
+        if (staged) H3SK_NQ_STREAM(__nv_bfloat16, true); else H3SK_NQ_STREAM(__nv_bfloat16, false);
+      }
 #undef H3SK_NQ_STREAM
       return cudaGetLastError();
     }
@@ -494,7 +596,7 @@ H3SK_EXPORT int h3_norm_quant_run(const void* x, const void* w, const void* shif
                                   int64_t ss, int64_t cs, float eps, int table_dtype, int debug,
                                   uintptr_t stream) {
   return h3sk::run_checked(x, w, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
-                           m, h3sk::kNormK, xs, ss, cs, eps, table_dtype, debug, stream);
+                           m, h3sk::kNormK, 0, xs, ss, cs, eps, table_dtype, debug, stream);
 }
 H3SK_EXPORT int h3_norm_quant_run_k(const void* x, const void* w, const void* shift, const void* scale,
                                     const void* rows, void* q, void* qscale, void* debug_norm,
@@ -502,5 +604,14 @@ H3SK_EXPORT int h3_norm_quant_run_k(const void* x, const void* w, const void* sh
                                     int64_t xs, int64_t ss, int64_t cs, float eps, int table_dtype,
                                     int debug, uintptr_t stream) {
   return h3sk::run_checked(x, w, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
-                           m, k, xs, ss, cs, eps, table_dtype, debug, stream);
+                           m, k, 0, xs, ss, cs, eps, table_dtype, debug, stream);
+}
+H3SK_EXPORT int h3_norm_quant_run_t(const void* x, const void* w, const void* shift, const void* scale,
+                                    const void* rows, void* q, void* qscale, void* debug_norm,
+                                    void* debug_rotated, void* debug_rstd, int64_t m, int64_t k,
+                                    int64_t tables, int64_t xs, int64_t ss, int64_t cs, float eps,
+                                    int table_dtype, int debug, uintptr_t stream) {
+  if (tables < 1) return cudaErrorInvalidValue;
+  return h3sk::run_checked(x, w, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
+                           m, k, tables, xs, ss, cs, eps, table_dtype, debug, stream);
 }

@@ -40,7 +40,7 @@ constexpr int kMaxSlots = 32;
 constexpr int kMaxTeams = 15;                   // named barriers 1..15
 constexpr int kMaxK = 16384;
 constexpr int kSmemBudget = 224 * 1024;         // dynamic shared memory per CTA (227 KB less static state)
-constexpr int kHalfGroupBytes = 512;            // exchange buffer per 256-value group
+constexpr int kHalfGroupBytes = 512;            // exchange region per 256-value group
 constexpr uint64_t kWaitNs = 2000000000ull;
 enum : int { kCodeFull = 0x301 };
 
@@ -156,7 +156,12 @@ __device__ __forceinline__ void exchange_half(uint64_t (&v)[32], uint32_t buf, u
   __syncwarp();
 }
 
-// buf: shared address of this group's buffer; q: team index; odd: group parity.
+// buf: shared address of this group's 512-byte region; q: team index; odd: group
+// parity.  The region is either the group's own exchange buffer or the group's
+// part of the row slot it has just read in layout A (lines 4g .. 4g+3 belong to
+// the group's four threads, all in one warp; slots are sized so that inactive
+// groups past K / 256 also stay inside their slot).  For the in-slot form the
+// caller puts a __syncwarp between its layout-A reads and this call.
 __device__ __forceinline__ void exchange_a_to_b_halves(uint64_t (&v)[32], uint32_t buf, int q, int odd) {
   const uint32_t wkey = (uint32_t(q) << 4) | (uint32_t(odd) << 6);
   const uint32_t rbase = buf + uint32_t(q) * 128u;
@@ -178,37 +183,44 @@ struct Plan {
   int team_threads;    // multiple of 32, >= k / 64
   int teams;           // <= kMaxTeams
   int threads;         // teams * team_threads
-  int slots_per_team;  // >= 2: one row being read, the next ones landing
-  int slot_bytes;      // width * 2 rounded up to 1024
-  int exch_bytes;      // per team: groups * 512
+  int slots_per_team;  // 2: one row being read, the next one landing
+  int slot_bytes;      // max(width * 2, groups * 512) rounded up to 1024
+  int ring_bytes;      // teams * slots_per_team * slot_bytes
+  int exch_bytes;      // per team: groups * 512, or 0 = exchange inside the row slot
+  int extra_bytes;     // caller's shared arrays after the rings and exchange buffers
   int smem;            // dynamic shared memory incl. 1024-byte alignment slack
 };
 
-// Up to 512 threads (16 warps: 4 per SM sub-partition, so 128 registers a thread),
-// at least two ring slots per team.
-inline Plan make_plan(int k, int width, int min_team_threads) {
+// Up to 512 threads (16 warps: 4 per SM sub-partition, so 128 registers a thread)
+// and two ring slots per team (deeper rings measured slower), `extra` bytes
+// reserved after the rings.  The A->B exchange gets its own buffers when they fit
+// (measured faster); otherwise it runs inside the row slot just read.
+inline Plan make_plan(int k, int width, int min_team_threads, int extra = 0) {
   Plan p{};
   p.k = k;
   p.width = width;
   int team = ((k / 64 + 31) / 32) * 32;
   if (team < min_team_threads) team = min_team_threads;
   p.team_threads = team;
-  p.slot_bytes = ((width * 2 + 1023) / 1024) * 1024;
-  p.exch_bytes = (team / 4) * kHalfGroupBytes;
+  const int exch = (team / 4) * kHalfGroupBytes;
+  // A slot holds the row and, for an in-slot exchange, every group's 512 bytes.
+  p.slot_bytes = ((max(width * 2, exch) + 1023) / 1024) * 1024;
+  p.extra_bytes = ((extra + 1023) / 1024) * 1024;
   int teams = 512 / team;
   if (teams < 1) teams = 1;
   if (teams > kMaxTeams) teams = kMaxTeams;
-  int per_team = 0;
+  if (2 * teams > kMaxSlots) teams = kMaxSlots / 2;
   for (; teams >= 1; --teams) {
-    const int rest = kSmemBudget - 1024 - teams * p.exch_bytes;
-    per_team = rest / (teams * p.slot_bytes);
-    if (per_team * teams > kMaxSlots) per_team = kMaxSlots / teams;
-    if (per_team >= 2) break;
+    const int ring = teams * 2 * p.slot_bytes;
+    const int rest = kSmemBudget - 1024 - p.extra_bytes - ring;
+    if (rest >= teams * exch) { p.exch_bytes = exch; break; }
+    if (rest >= 0) { p.exch_bytes = 0; break; }
   }
   p.teams = teams;
-  p.slots_per_team = teams >= 1 ? per_team : 0;
+  p.slots_per_team = teams >= 1 ? 2 : 0;
   p.threads = teams * team;
-  p.smem = 1024 + teams * (per_team * p.slot_bytes + p.exch_bytes);
+  p.ring_bytes = teams * 2 * p.slot_bytes;
+  p.smem = 1024 + p.ring_bytes + teams * p.exch_bytes + p.extra_bytes;
   return p;
 }
 

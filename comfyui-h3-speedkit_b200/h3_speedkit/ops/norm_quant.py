@@ -147,7 +147,7 @@ class NormQuant:
                 raise RuntimeError('NormQuant requires eager execution')
         pointers = [t.data_ptr() for t in (x, weight, shift, scale, rows, q, q_scale)]
         pointers += [t.data_ptr() if t is not None else None for t in (debug_norm, debug_rotated, debug_rstd)]
-        args = pointers + [x.shape[0], x.shape[1], x.stride(0), shift.stride(0), scale.stride(0),
+        args = pointers + [x.shape[0], x.shape[1], shift.shape[0], x.stride(0), shift.stride(0), scale.stride(0),
                            float(eps), int(shift.dtype == torch.bfloat16), int(debug_norm is not None)]
         return Bound(self, x.device, inputs, outputs, args, (q, q_scale))
 
@@ -165,7 +165,7 @@ class Bound:
             stream = torch.cuda.current_stream(self.device)
             for owner in self.owners:
                 owner.record_stream(stream)
-            code = self.library.lib.h3_norm_quant_run_k(*self.args, stream.cuda_stream)
+            code = self.library.lib.h3_norm_quant_run_t(*self.args, stream.cuda_stream)
             # Stores may already be queued when an error is reported: never retried.
             torch.autograd.graph.increment_version(tuple(t for _, t in self.outputs))
             self.library.check(code)

@@ -101,18 +101,20 @@ class BlockPlan:
         w = weights
         tdt = int(w.shift_msa.dtype == torch.bfloat16)
         self.calls = [
-            ("prologue", lib.h3_norm_quant_run_k,
+            ("prologue", lib.h3_norm_quant_run_t,
              (P(x), P(w.norm1), P(w.shift_msa), P(w.scale_msa), P(rows), P(ws.q), P(ws.qs), None, None, None,
-              m, d, x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps), tdt, 0)),
+              m, d, w.shift_msa.shape[0], x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps),
+              tdt, 0)),
             ("qkv", lib.h3_int8_ex,
              (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * d, d, 3 * d, EPI_DEQUANT)),
             ("quant_v", lib.h3_convrot_quant_act,
              (P(ws.qkv) + 2 * d * 2, 3 * d, P(ws.aq), P(ws.as_), m, d, ACT_NONE)),
             ("outproj", lib.h3_int8_gate,
              (P(ws.aq), P(w.out), P(ws.as_), P(w.out_s), P(x), P(w.gate_msa), P(rows), P(x), m, d, d, 13)),
-            ("prologue", lib.h3_norm_quant_run_k,
+            ("prologue", lib.h3_norm_quant_run_t,
              (P(x), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows), P(ws.q), P(ws.qs), None, None, None,
-              m, d, x.stride(0), w.shift_mlp.stride(0), w.scale_mlp.stride(0), float(eps), tdt, 0)),
+              m, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0), w.scale_mlp.stride(0), float(eps),
+              tdt, 0)),
             ("fc1", lib.h3_int8_ex,
              (P(ws.q), P(w.fc1), P(ws.qs), P(w.fc1_s), None, P(ws.h), m, ffn, d, ffn, EPI_GELU)),
             ("quant_h", lib.h3_convrot_quant_act,

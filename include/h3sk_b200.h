@@ -71,6 +71,16 @@ int h3_norm_quant_run_k(const void* x, const void* w, const void* shift, const v
                         void* debug_rotated, void* debug_rstd, int64_t m, int64_t k, int64_t xs,
                         int64_t ss, int64_t cs, float eps, int table_dtype, int debug,
                         uintptr_t stream);
+/* Same contract with the number of modulation-table rows T (shift and scale are
+ * [T, >= K]) stated (no reference counterpart: the reference never needs T).
+ * Knowing T lets the B200 kernel stage W and all T tables in shared memory when
+ * they fit; every entry of `rows` must lie in [0, T), as for the entry points
+ * above (an out-of-range entry reads table T - 1 here instead of out of bounds). */
+int h3_norm_quant_run_t(const void* x, const void* w, const void* shift, const void* scale,
+                        const void* rows, void* q, void* qscale, void* debug_norm,
+                        void* debug_rotated, void* debug_rstd, int64_t m, int64_t k, int64_t tables,
+                        int64_t xs, int64_t ss, int64_t cs, float eps, int table_dtype, int debug,
+                        uintptr_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* ConvRot256 + per-token INT8 quantiser                                    */

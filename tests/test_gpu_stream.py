@@ -171,3 +171,47 @@ def test_quant_nan_rows_match_reference(device):
     assert torch.equal(s0.reshape(-1).view(torch.int32), rs.view(torch.int32))
     assert torch.equal(s1, s0) and torch.equal(q1, q0)
     assert torch.equal(q0, rq)
+
+
+def _prologue_t(x, w, shift, scale, rows, eps=1e-6):
+    """h3_norm_quant_run_t: T known, so W and the tables are staged when they fit."""
+    lib = _lib.load()
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    qs = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    rc = lib.h3_norm_quant_run_t(x.data_ptr(), w.data_ptr(), shift.data_ptr(), scale.data_ptr(), rows.data_ptr(),
+                                 q.data_ptr(), qs.data_ptr(), None, None, None, m, k, shift.shape[0], x.stride(0),
+                                 shift.stride(0), scale.stride(0), ct.c_float(eps),
+                                 1 if shift.dtype == torch.bfloat16 else 0, 0, _stream())
+    assert rc == 0, lib.h3_norm_quant_error(rc)
+    return q, qs
+
+
+@pytest.mark.parametrize("k,tables,table_dtype", [(4096, 1, torch.bfloat16), (4096, 3, torch.float32),
+                                                   (2048, 2, torch.bfloat16), (5376, 1, torch.float32),
+                                                   (5376, 2, torch.bfloat16), (4096, 12, torch.bfloat16)])
+def test_prologue_staged_tables_bitexact_vs_reference_kernel(device, k, tables, table_dtype):
+    """Staged-table streaming prologue (and, for 12 tables, the fallback when they
+    do not fit) against the reference kernel."""
+    x, w, shift, scale, rows = _prologue_inputs(3001, k, tables, table_dtype, 300 + k + tables, device)
+    q, qs = _prologue_t(x, w, shift, scale, rows)
+    rq, rqs = ref_gpu.norm_quant(x, w, shift, scale, rows, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(qs, rqs)
+    assert torch.equal(q, rq)
+    assert _lib.pipeline_status() == 0
+
+
+def test_prologue_staged_misaligned_vectors(device):
+    k, m = 4096, 149
+    x, w, shift, scale, rows = _prologue_inputs(m, k, 2, torch.bfloat16, 77, device)
+    w_big = torch.empty((k + 4,), dtype=torch.bfloat16, device=device)
+    w_big[4:] = w
+    sh_big = torch.empty((2, k + 2), dtype=torch.bfloat16, device=device)
+    sc_big = torch.empty((2, k + 2), dtype=torch.bfloat16, device=device)
+    sh_big[:, 2:] = shift
+    sc_big[:, 2:] = scale
+    q, qs = _prologue_t(x, w_big[4:], sh_big[:, 2:], sc_big[:, 2:], rows)
+    rq, rqs = ref_gpu.norm_quant(x, w, shift, scale, rows, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(q, rq) and torch.equal(qs, rqs)

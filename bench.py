@@ -342,7 +342,8 @@ def run_ours(args):
     if pro:
         pro_bytes = m_local * D * 2 + m_local * D + m_local * 4 + m_local * 4 + 3 * D * 2
         pro_gbs = pro_bytes / (pro["avg_ms"] / 1e3) / 1e9
-        prologue_line = {"bound": "hbm", "kernel": "norm_quant_rows", "achieved": pro_gbs, "peak": hbm_peak,
+        prologue_line = {"bound": "hbm", "kernel": "norm_quant_stream (staged tables)", "achieved": pro_gbs,
+                         "peak": hbm_peak,
                          "unit": "GB/s", "frac": pro_gbs / hbm_peak, "bytes_per_launch": pro_bytes}
     value = args.tokens * args.steps / elapsed
     total_ops = args.tokens * block_ops() * args.blocks

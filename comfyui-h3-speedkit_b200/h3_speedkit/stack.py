@@ -153,11 +153,14 @@ def block_ops_per_token(d: int = 4096, ffn: int = 16384) -> int:
 class LocalStack:
     """All blocks over one contiguous shard of tokens, on the current device."""
 
-    def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6):
+    def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6,
+                 ws: Workspace | None = None):
         m, d = x.shape
         ffn = blocks[0].fc1.shape[0]
         self.x, self.rows = x, rows
-        self.ws = Workspace.allocate(m, d, ffn, x.device)
+        if ws is not None and (ws.q.shape[0] < m or ws.h.shape[1] != ffn):
+            raise ValueError("shared workspace too small for this shard")
+        self.ws = ws if ws is not None else Workspace.allocate(m, d, ffn, x.device)
         self.plans = [BlockPlan(b, x, rows, self.ws, eps) for b in blocks]
         self.graph = None
 
@@ -212,6 +215,7 @@ class ShardedStack:
         self.out = torch.empty((self.per * self.world, d), dtype=dtype, device=device)
         self.x = self.send[: self.rows_local]
         self.local = LocalStack(blocks, self.x, rows_shard, eps) if self.rows_local else None
+        self._blocks, self._rows, self._eps = blocks, rows_shard, eps
 
     @property
     def launches_per_step(self) -> int:
@@ -233,3 +237,97 @@ class ShardedStack:
     def forward(self, events=None) -> torch.Tensor:
         self.forward_local(events)
         return self.gather()
+
+    # ---- end to end from pinned host memory, copies overlapped with compute -------
+    MIN_CHUNK_ROWS = 8192
+
+    def _chunking(self, chunks: int | None):
+        """Chunk boundaries over the padded shard (identical on every rank, so every
+        rank issues the same collectives) and one LocalStack per chunk sharing one
+        workspace sized for a chunk."""
+        if chunks is None:
+            chunks = max(1, min(4, self.per // self.MIN_CHUNK_ROWS))
+        key = ("chunks", chunks)
+        cached = getattr(self, "_chunk_cache", None)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        step = -(-self.per // chunks)
+        bounds = [(c0, min(self.per, c0 + step)) for c0 in range(0, self.per, step)]
+        stacks = []
+        ws = None
+        if self.local is not None:
+            d, ffn = self.x.shape[1], self._blocks[0].fc1.shape[0]
+            ws = Workspace.allocate(step, d, ffn, self.x.device)
+        for c0, c1 in bounds:
+            hi = min(c1, self.rows_local)
+            if self.local is not None and hi > c0:
+                stacks.append(LocalStack(self._blocks, self.x[c0:hi], self._rows[c0:hi], self._eps, ws=ws))
+            else:
+                stacks.append(None)
+        plan = (bounds, stacks, torch.cuda.Stream(self.send.device), torch.cuda.Stream(self.send.device))
+        self._chunk_cache = (key, plan)
+        return plan
+
+    def forward_host(self, host_in: torch.Tensor, host_out: torch.Tensor | None = None,
+                     chunks: int | None = None) -> None:
+        """One end-to-end step from pinned host memory: this rank's input rows are
+        copied in chunk by chunk on a copy stream while the block stack runs on the
+        chunks already resident (every op is row-local), each chunk is gathered
+        across ranks as soon as it is done, and rank 0 (or the only rank) copies
+        finished rows to ``host_out`` on a second copy stream.  Everything is
+        ordered on the current stream: when it reaches the end of this call's work,
+        the output is in ``host_out``."""
+        import torch.distributed as dist
+        if host_in.shape != self.x.shape:
+            raise ValueError(f"expected input shard {tuple(self.x.shape)}, got {tuple(host_in.shape)}")
+        bounds, stacks, h2d, d2h = self._chunking(chunks)
+        comp = torch.cuda.current_stream(self.send.device)
+        start = torch.cuda.Event()
+        start.record(comp)
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        arrived = []
+        with torch.cuda.stream(h2d):
+            for c0, c1 in bounds:
+                hi = min(c1, self.rows_local)
+                if hi > c0:
+                    self.x[c0:hi].copy_(host_in[c0:hi], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                arrived.append(ev)
+        multi = dist.is_initialized() and self.world > 1
+        if multi and getattr(self, "_gather_chunks", None) is None:
+            step = bounds[0][1] - bounds[0][0]
+            self._gather_chunks = [torch.empty((self.world * step, self.x.shape[1]), dtype=self.send.dtype,
+                                               device=self.send.device) for _ in range(2)]
+        copied = [None, None]   # D2H completion of the last chunk gathered into each buffer
+        for i, ((c0, c1), stack, ev) in enumerate(zip(bounds, stacks, arrived)):
+            comp.wait_event(ev)
+            if stack is not None:
+                stack.run()
+            rows = c1 - c0
+            if multi:
+                buf = i % 2
+                if copied[buf] is not None:
+                    comp.wait_event(copied[buf])   # its previous rows are on the host
+                out = self._gather_chunks[buf][: self.world * rows]
+                dist.all_gather_into_tensor(out, self.send[c0:c1], group=self.group)
+            if host_out is None:
+                continue
+            done = torch.cuda.Event()
+            done.record(comp)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                if not multi:
+                    hi = min(c1, self.rows_local)
+                    if hi > c0:
+                        host_out[c0:hi].copy_(self.x[c0:hi], non_blocking=True)
+                else:
+                    for r in range(self.world):
+                        g0, g1 = r * self.per + c0, min(self.total, r * self.per + c1)
+                        if g1 > g0:
+                            host_out[g0:g1].copy_(out[r * rows: r * rows + (g1 - g0)], non_blocking=True)
+                    copied[buf] = torch.cuda.Event()
+                    copied[buf].record(d2h)
+        comp.wait_stream(d2h)
+        comp.wait_stream(h2d)

@@ -94,3 +94,23 @@ def test_sharded_stack_single_rank_gathers_its_rows(device):
     stack.load(x0.cpu().pin_memory())
     torch.cuda.synchronize()
     assert torch.equal(stack.forward(), ref)
+
+
+@pytest.mark.parametrize("chunks", [None, 3])
+def test_forward_host_pipeline_equals_forward(device, chunks):
+    """End-to-end step from pinned host memory (chunked H2D / compute / D2H on
+    three streams) gives the same rows as the device-resident forward."""
+    m = 1000
+    blocks = _blocks(2, device)
+    x0 = synthetic.cfg5_tokens(m, D)
+    rows = torch.zeros((m,), dtype=torch.int32, device=device)
+    ref_stack = ShardedStack(blocks, rows, m, D, device)
+    ref_stack.load(x0.to(device))
+    ref = ref_stack.forward().clone()
+    stack = ShardedStack(blocks, rows, m, D, device)
+    host_in = x0.pin_memory()
+    host_out = torch.empty((m, D), dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):   # twice: the second step reuses the chunk plans and buffers
+        stack.forward_host(host_in, host_out, chunks=chunks)
+        torch.cuda.synchronize()
+        assert torch.equal(host_out, ref.cpu())

@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--blocks", type=int, default=BLOCKS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
+                    help="5 (default): the 8-block stack; 1-4: the single-op BASELINE configs on one GPU")
     return ap.parse_args()
 
 
@@ -372,10 +374,148 @@ def run_ours(args):
     return 0
 
 
+# ---- single-op BASELINE configs 1-4 (one GPU) ------------------------------------
+
+def _median_ms(fn, warmup=20, iters=100, rotate=1):
+    """Median CUDA-event time of fn(i) over `iters` calls; `rotate` buffer sets
+    are cycled so that consecutive calls touch different memory (L2 flushed by
+    volume: every config's rotation spans more than twice the 126 MB L2)."""
+    import torch
+    for i in range(warmup):
+        fn(i % rotate)
+    torch.cuda.synchronize()
+    times = []
+    for i in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn(i % rotate)
+        e.record()
+        times.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in times)
+
+
+def run_config(args):
+    """BASELINE configs 1-4 as single-op lines (SURVEY-style measurement: 20 warm-up
+    and 100 timed launches, median, buffers rotated beyond L2)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import numpy as np
+    import torch
+
+    from h3_speedkit import _lib, synthetic
+    from h3_speedkit.ops import gemm
+    from h3_speedkit.ops.convrot import quantize_int8_rowwise_convrot64
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM))
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    cfg = args.config
+    if cfg == 1:
+        inp = synthetic.cfg1()
+        x, w, bias = inp["x"].to(dev), inp["w"].to(dev), inp["bias"].to(dev)
+        wq, wsc = quantize_int8_rowwise_convrot64(w)          # weights: per output channel, once
+        ws = wsc.reshape(-1).contiguous()
+        out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=dev)
+
+        def op(_):
+            q, qs = quantize_int8_rowwise_convrot64(x)
+            gemm.int8_linear(q, wq, qs.reshape(-1), ws, bias=bias, out=out)
+        ms = _median_ms(op)
+        ops = 2.0 * 1024 * 2048 * 2048
+        value, unit, bound, ach, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", None, int8_peak
+        ach = value
+        from oracle import cpu as ocpu
+        xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        qc, sc = ocpu.convrot_quant(xb)
+        acc = ocpu.gemm_s32(qc, wq.cpu().numpy())
+        ocpu.dequant(acc, sc.reshape(-1), ws.cpu().numpy(), bias.cpu().view(torch.int16).numpy().view(np.uint16))
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+               "sample": "the full config-1 linear (activation quant, int32 GEMM, dequant)"}
+        workload = "cfg1: W8A8 linear, X BF16 [1024,2048] quantised per token (ConvRot256), W [2048,2048] per channel"
+    elif cfg == 2:
+        inp = synthetic.cfg2()
+        m, k = inp["x"].shape
+        sets = 8                                             # 8 x 75.6 MB rotated
+        xs = [inp["x"].to(dev) for _ in range(sets)]
+        qs_ = [torch.empty((m, k), dtype=torch.int8, device=dev) for _ in range(sets)]
+        ss_ = [torch.empty((m, 1), dtype=torch.float32, device=dev) for _ in range(sets)]
+        w, sh, sc, rows = (inp[n].to(dev) for n in ("weight", "shift", "scale", "rows"))
+        import ctypes as ct
+
+        def op(i):
+            rc = lib.h3_norm_quant_run_t(xs[i].data_ptr(), w.data_ptr(), sh.data_ptr(), sc.data_ptr(), rows.data_ptr(),
+                                         qs_[i].data_ptr(), ss_[i].data_ptr(), None, None, None, m, k, 1, k, k, k,
+                                         ct.c_float(1e-6), 1, 0, st())
+            if rc:
+                raise RuntimeError(f"prologue failed: {rc}")
+        ms = _median_ms(op, rotate=sets)
+        nbytes = m * k * 2 + m * k + m * 4 + m * 4 + 3 * k * 2
+        value, unit, bound, peak = nbytes / (ms / 1e3) / 1e9, "GB/s", "hbm", hbm_peak
+        ach = value
+        from oracle import cpu as ocpu
+        sample = 512
+        xb = inp["x"][:sample].view(torch.int16).numpy().view(np.uint16)
+        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        ocpu.norm_quant(xb, bits(inp["weight"]), bits(inp["shift"]), bits(inp["scale"]), inp["rows"][:sample].numpy(),
+                        1e-6, threads=threads)
+        cpu_s = (time.perf_counter() - t0) * m / sample
+        cpu = {"value": nbytes / cpu_s / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{sample} of the 6144 rows, scaled to the full shape"}
+        workload = "cfg2: fused prologue, x BF16 [6144,4096], one BF16 table"
+    else:
+        inp = synthetic.cfg3() if cfg == 3 else synthetic.cfg4()
+        a, w, xs, ws, bias = (inp[n].to(dev) for n in ("a", "w", "xs", "ws", "bias"))
+        m, k = a.shape
+        n = w.shape[0]
+        if cfg == 3:
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            op = lambda _: gemm.int8_linear(a, w, xs, ws, bias=bias, gelu=True, out=out)
+            workload = "cfg3: FC1 INT8 GEMM + GELU-tanh epilogue, [24576,4096] x [16384,4096]^T"
+        else:
+            res, gate, rows = inp["residual"].to(dev), inp["gate"].to(dev), inp["rows"].to(dev)
+            op = lambda _: gemm.int8_gate_residual(a, w, xs, ws, res, gate, rows, bias=bias, requant=True)
+            workload = ("cfg4: FC2 INT8 GEMM + in-place gate-residual + ConvRot256/INT8 requant, "
+                        "[24576,16384] x [4096,16384]^T")
+        ms = _median_ms(op)
+        ops = 2.0 * m * n * k
+        value, unit, bound, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", int8_peak
+        ach = value
+        sample = 1024
+        t0 = time.perf_counter()
+        torch._int_mm(inp["a"][:sample], inp["w"].t())
+        cpu_s = (time.perf_counter() - t0) * m / sample
+        cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+               "sample": f"torch._int_mm on {sample} of the {m} rows (int32 GEMM only), scaled to the full shape"}
+    line = {
+        "metric": f"BASELINE config {cfg} ({unit})", "value": value, "unit": unit, "n_gpus": 1, "steps": 100,
+        "warmup": 20, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic", "config": {"workload": workload, "timing": "median of 100 launches",
+                                                       "l2": "buffers rotated beyond L2 or larger than L2"},
+        "roofline": {"bound": bound, "achieved": ach, "peak": peak, "unit": "TOPS" if bound == "tensor" else "GB/s",
+                     "frac": ach / peak, "traffic": None,
+                     "peak_source": (f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json" if bound == "tensor"
+                                     else f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json")},
+        "cpu_baseline": cpu, "gpu_launches": 2 if cfg in (1, 4) else 1,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.config != 5:
+        return run_config(args)
     return run_ours(args)
 
 

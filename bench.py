@@ -37,6 +37,10 @@ sys.path[:0] = [str(ROOT), str(ROOT / "comfyui-h3-speedkit_b200")]
 
 METRIC = "INT8 DiT-block TOPS and tokens/s at 1/2/4/8 B200; % INT8/HBM roofline"
 D, FFN, BLOCKS, TOKENS = 4096, 16384, 8, 98304
+ATTN, SWIGLU = 4096, False          # cfg5: attention width = D, GELU MLP
+# --geometry h3: the H3 model's block (hidden 5376, attention 7168, SwiGLU MLP of
+# width 14336), the row SURVEY ranks next after config 5
+GEOMETRIES = {"cfg5": (4096, 4096, 16384, False), "h3": (5376, 7168, 14336, True)}
 CPU_SAMPLE_TOKENS = 1024
 FALLBACK_BF16_SUSTAINED = 1400.0   # TFLOP/s, used only if MEASURED_PEAKS.json is absent
 FALLBACK_HBM = 6650.0              # GB/s
@@ -52,6 +56,8 @@ def parse_args():
     ap.add_argument("--blocks", type=int, default=BLOCKS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--geometry", choices=tuple(GEOMETRIES), default="cfg5",
+                    help="block geometry of the stack: cfg5 (default) or the H3 model's own (SwiGLU)")
     ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
                     help="5 (default): the 8-block stack; 1-4: the single-op BASELINE configs on one GPU")
     return ap.parse_args()
@@ -133,7 +139,7 @@ def _cpu_data(tokens: int):
         from h3_speedkit import synthetic
         from oracle import chain
         if "block" not in _CPU_DATA:
-            _CPU_DATA["block"] = chain.NpBlock.from_torch(synthetic.cfg5_block(0, D, FFN))
+            _CPU_DATA["block"] = chain.NpBlock.from_torch(synthetic.cfg5_block(0, D, FFN, attn=ATTN, swiglu=SWIGLU))
         x = synthetic.cfg5_tokens(tokens, D).view(torch.int16).numpy().view(np.uint16)
         _CPU_DATA[tokens] = (x, np.zeros((tokens,), np.int32))
     return _CPU_DATA["block"], *_CPU_DATA[tokens]
@@ -185,7 +191,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_block * 1e3 * args.blocks * TOKENS / CPU_SAMPLE_TOKENS,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "cfg5: 8 DiT blocks D=4096 FFN=16384 M=98304 (CPU sample)", "tokens": TOKENS,
+        "config": {"workload": workload_name(TOKENS) + " (CPU sample)", "tokens": TOKENS,
                    "blocks": args.blocks, "parallelism": "host threads"},
         "tops": CPU_SAMPLE_TOKENS * block_ops() / sec_block / 1e12,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
@@ -196,8 +202,19 @@ def run_reference(args):
     return 0
 
 
-def block_ops(d=D, ffn=FFN):
-    return 2 * d * (3 * d + d + ffn) + 2 * ffn * d
+def fc1_n():
+    return 2 * FFN if SWIGLU else FFN
+
+
+def block_ops():
+    """INT8 ops per token per block: QKV + outproj + FC1 + FC2."""
+    return 2 * D * 3 * ATTN + 2 * ATTN * D + 2 * D * fc1_n() + 2 * FFN * D
+
+
+def workload_name(tokens):
+    mlp = f"SwiGLU FFN={FFN}" if SWIGLU else f"FFN={FFN} GELU"
+    tag = "cfg5" if (D, ATTN, FFN, SWIGLU) == GEOMETRIES["cfg5"] else "H3 geometry"
+    return f"{tag}: 8 DiT blocks D={D} attn={ATTN} {mlp} M={tokens}, identity attention, token-sharded"
 
 
 def run_ours(args):
@@ -219,7 +236,7 @@ def run_ours(args):
     lib = _lib.load()
 
     # ---- inputs: weights replicated, tokens sharded -------------------------------
-    blocks = [synthetic.cfg5_block(i, D, FFN, device=dev) for i in range(args.blocks)]
+    blocks = [synthetic.cfg5_block(i, D, FFN, device=dev, attn=ATTN, swiglu=SWIGLU) for i in range(args.blocks)]
     start, stop = shard_bounds(args.tokens, world, rank)
     x_full = synthetic.cfg5_tokens(args.tokens, D, device=dev)
     x_src = x_full[start:stop].clone()
@@ -327,14 +344,14 @@ def run_ours(args):
     peaks, peak_kind = measured_peaks()
     int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
     m_local = stop - start
-    gemm_ops = {"qkv": 2 * m_local * 3 * D * D, "outproj": 2 * m_local * D * D, "fc1": 2 * m_local * FFN * D,
-                "fc2": 2 * m_local * D * FFN}
+    gemm_ops = {"qkv": 2 * m_local * 3 * ATTN * D, "outproj": 2 * m_local * D * ATTN,
+                "fc1": 2 * m_local * fc1_n() * D, "fc2": 2 * m_local * D * FFN}
     gemms = {k: v for k, v in per_kernel.items() if k in gemm_ops}
     dominant = max(gemms, key=lambda k: gemms[k]["total_ms"])
     achieved = gemm_ops[dominant] / (gemms[dominant]["avg_ms"] / 1e3) / 1e12
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
-    if tfile.exists():
+    if tfile.exists() and args.geometry == "cfg5":   # captured at the cfg5 geometry
         tdata = json.loads(tfile.read_text())
         entry = tdata.get(dominant)
         if entry:
@@ -355,8 +372,9 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "cfg5: 8 DiT blocks D=4096 FFN=16384 M=98304, identity attention, token-sharded",
-                   "tokens": args.tokens, "blocks": args.blocks, "d": D, "ffn": FFN,
+        "config": {"workload": workload_name(args.tokens),
+                   "tokens": args.tokens, "blocks": args.blocks, "d": D, "attn": ATTN, "ffn": FFN,
+                   "mlp": "swiglu" if SWIGLU else "gelu",
                    "parallelism": f"tokens/{world} (weights replicated) + 1 all-gather",
                    "l2": "inputs larger than L2 (weights 1.6 GB, activations > 1 GB per step)"},
         "tops": total_ops * args.steps / elapsed / 1e12,
@@ -511,7 +529,9 @@ def run_config(args):
 
 
 def main():
+    global D, ATTN, FFN, SWIGLU
     args = parse_args()
+    D, ATTN, FFN, SWIGLU = GEOMETRIES[args.geometry]
     if args.impl == "reference":
         return run_reference(args)
     if args.config != 5:

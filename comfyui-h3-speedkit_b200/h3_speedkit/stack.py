@@ -30,7 +30,7 @@ import torch
 from . import _lib
 from .synthetic import BlockWeights
 
-ACT_NONE = 0
+ACT_NONE, ACT_SWIGLU = 0, 2
 EPI_DEQUANT, EPI_GELU = 0, 1
 LAUNCHES_PER_BLOCK = 8   # 2 prologues, 2 quantisers, 4 GEMMs
 GEMM_NAMES = ("qkv", "outproj", "fc1", "fc2")
@@ -71,13 +71,35 @@ class Workspace:
     hs: torch.Tensor
 
     @classmethod
-    def allocate(cls, m: int, d: int, ffn: int, device) -> "Workspace":
+    def allocate(cls, m: int, d: int, ffn: int, device, *, attn: int | None = None,
+                 fc1_n: int | None = None) -> "Workspace":
         e = dict(device=device)
+        attn = d if attn is None else attn
+        fc1_n = ffn if fc1_n is None else fc1_n
         return cls(q=torch.empty((m, d), dtype=torch.int8, **e), qs=torch.empty((m, 1), dtype=torch.float32, **e),
-                   qkv=torch.empty((m, 3 * d), dtype=torch.bfloat16, **e),
-                   aq=torch.empty((m, d), dtype=torch.int8, **e), as_=torch.empty((m, 1), dtype=torch.float32, **e),
-                   h=torch.empty((m, ffn), dtype=torch.bfloat16, **e),
+                   qkv=torch.empty((m, 3 * attn), dtype=torch.bfloat16, **e),
+                   aq=torch.empty((m, attn), dtype=torch.int8, **e),
+                   as_=torch.empty((m, 1), dtype=torch.float32, **e),
+                   h=torch.empty((m, fc1_n), dtype=torch.bfloat16, **e),
                    hq=torch.empty((m, ffn), dtype=torch.int8, **e), hs=torch.empty((m, 1), dtype=torch.float32, **e))
+
+    @classmethod
+    def for_block(cls, m: int, weights: BlockWeights, device) -> "Workspace":
+        g = geometry(weights)
+        return cls.allocate(m, g["d"], g["ffn"], device, attn=g["attn"], fc1_n=g["fc1_n"])
+
+
+def geometry(weights: BlockWeights) -> dict:
+    """Block geometry from the weight shapes: width d, attention width (QKV N / 3),
+    FFN width (FC2 K), FC1 N, and whether the MLP is SwiGLU (FC1 N = 2 FFN)."""
+    d = weights.norm1.shape[0]
+    attn = weights.qkv.shape[0] // 3
+    ffn = weights.fc2.shape[1]
+    fc1_n = weights.fc1.shape[0]
+    if (weights.qkv.shape != (3 * attn, d) or weights.out.shape != (d, attn) or weights.fc1.shape[1] != d
+            or weights.fc2.shape[0] != d or fc1_n not in (ffn, 2 * ffn)):
+        raise ValueError("inconsistent block weight shapes")
+    return {"d": d, "attn": attn, "ffn": ffn, "fc1_n": fc1_n, "swiglu": fc1_n == 2 * ffn}
 
 
 class BlockPlan:
@@ -91,34 +113,38 @@ class BlockPlan:
                  eps: float = 1e-6):
         self.lib = _lib.load()
         m, d = x.shape
-        ffn = weights.fc1.shape[0]
-        if weights.qkv.shape != (3 * d, d) or weights.fc2.shape != (d, ffn) or weights.out.shape != (d, d):
+        g = geometry(weights)
+        attn, ffn, n1 = g["attn"], g["ffn"], g["fc1_n"]
+        if g["d"] != d:
             raise ValueError("block weights do not match the activation width")
         if m < 1:
             raise ValueError("empty shard")
+        if ws.qkv.shape[1] != 3 * attn or ws.h.shape[1] != n1 or ws.hq.shape[1] != ffn or ws.aq.shape[1] != attn:
+            raise ValueError("workspace does not match the block geometry")
         self.keep = (weights, x, rows, ws)   # owners of every pointer below
         lib, P = self.lib, lambda t: t.data_ptr()
         w = weights
         tdt = int(w.shift_msa.dtype == torch.bfloat16)
+        fc1_epi, mlp_act = (EPI_DEQUANT, ACT_SWIGLU) if g["swiglu"] else (EPI_GELU, ACT_NONE)
         self.calls = [
             ("prologue", lib.h3_norm_quant_run_t,
              (P(x), P(w.norm1), P(w.shift_msa), P(w.scale_msa), P(rows), P(ws.q), P(ws.qs), None, None, None,
               m, d, w.shift_msa.shape[0], x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps),
               tdt, 0)),
             ("qkv", lib.h3_int8_ex,
-             (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * d, d, 3 * d, EPI_DEQUANT)),
+             (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * attn, d, 3 * attn, EPI_DEQUANT)),
             ("quant_v", lib.h3_convrot_quant_act,
-             (P(ws.qkv) + 2 * d * 2, 3 * d, P(ws.aq), P(ws.as_), m, d, ACT_NONE)),
+             (P(ws.qkv) + 2 * attn * 2, 3 * attn, P(ws.aq), P(ws.as_), m, attn, ACT_NONE)),
             ("outproj", lib.h3_int8_gate,
-             (P(ws.aq), P(w.out), P(ws.as_), P(w.out_s), P(x), P(w.gate_msa), P(rows), P(x), m, d, d, 13)),
+             (P(ws.aq), P(w.out), P(ws.as_), P(w.out_s), P(x), P(w.gate_msa), P(rows), P(x), m, d, attn, 13)),
             ("prologue", lib.h3_norm_quant_run_t,
              (P(x), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows), P(ws.q), P(ws.qs), None, None, None,
               m, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0), w.scale_mlp.stride(0), float(eps),
               tdt, 0)),
             ("fc1", lib.h3_int8_ex,
-             (P(ws.q), P(w.fc1), P(ws.qs), P(w.fc1_s), None, P(ws.h), m, ffn, d, ffn, EPI_GELU)),
+             (P(ws.q), P(w.fc1), P(ws.qs), P(w.fc1_s), None, P(ws.h), m, n1, d, n1, fc1_epi)),
             ("quant_h", lib.h3_convrot_quant_act,
-             (P(ws.h), ffn, P(ws.hq), P(ws.hs), m, ffn, ACT_NONE)),
+             (P(ws.h), n1, P(ws.hq), P(ws.hs), m, ffn, mlp_act)),
             ("fc2", lib.h3_int8_gate,
              (P(ws.hq), P(w.fc2), P(ws.hs), P(w.fc2_s), P(x), P(w.gate_mlp), P(rows), P(x), m, d, ffn, 13)),
         ]
@@ -141,8 +167,11 @@ class BlockPlan:
                 events.setdefault(name, []).append((start, end))
 
     @staticmethod
-    def gemm_ops(m: int, d: int, ffn: int) -> dict:
-        return {"qkv": 2 * m * 3 * d * d, "outproj": 2 * m * d * d, "fc1": 2 * m * ffn * d, "fc2": 2 * m * d * ffn}
+    def gemm_ops(m: int, d: int, ffn: int, attn: int | None = None, fc1_n: int | None = None) -> dict:
+        attn = d if attn is None else attn
+        fc1_n = ffn if fc1_n is None else fc1_n
+        return {"qkv": 2 * m * 3 * attn * d, "outproj": 2 * m * d * attn, "fc1": 2 * m * fc1_n * d,
+                "fc2": 2 * m * d * ffn}
 
 
 def block_ops_per_token(d: int = 4096, ffn: int = 16384) -> int:
@@ -156,11 +185,10 @@ class LocalStack:
     def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6,
                  ws: Workspace | None = None):
         m, d = x.shape
-        ffn = blocks[0].fc1.shape[0]
         self.x, self.rows = x, rows
-        if ws is not None and (ws.q.shape[0] < m or ws.h.shape[1] != ffn):
+        if ws is not None and ws.q.shape[0] < m:
             raise ValueError("shared workspace too small for this shard")
-        self.ws = ws if ws is not None else Workspace.allocate(m, d, ffn, x.device)
+        self.ws = ws if ws is not None else Workspace.for_block(m, blocks[0], x.device)
         self.plans = [BlockPlan(b, x, rows, self.ws, eps) for b in blocks]
         self.graph = None
 
@@ -239,7 +267,7 @@ class ShardedStack:
         return self.gather()
 
     # ---- end to end from pinned host memory, copies overlapped with compute -------
-    MIN_CHUNK_ROWS = 8192
+    MIN_CHUNK_ROWS = 2048
 
     def _chunking(self, chunks: int | None):
         """Chunk boundaries over the padded shard (identical on every rank, so every
@@ -256,8 +284,7 @@ class ShardedStack:
         stacks = []
         ws = None
         if self.local is not None:
-            d, ffn = self.x.shape[1], self._blocks[0].fc1.shape[0]
-            ws = Workspace.allocate(step, d, ffn, self.x.device)
+            ws = Workspace.for_block(step, self._blocks[0], self.x.device)
         for c0, c1 in bounds:
             hi = min(c1, self.rows_local)
             if self.local is not None and hi > c0:

@@ -117,21 +117,39 @@ class BlockWeights:
         return BlockWeights(**{k: v.to(device) for k, v in self.__dict__.items()})
 
 
-def cfg5_block(index: int, d: int = 4096, ffn: int = 16384, tables: int = 1, device="cpu") -> BlockWeights:
+def cfg5_block(index: int, d: int = 4096, ffn: int = 16384, tables: int = 1, device="cpu", *,
+               attn: int | None = None, swiglu: bool = False) -> BlockWeights:
     """Block `index` of the cfg-5 stack, drawn on `device` (a CPU draw and a CUDA
-    draw of the same block differ: each device has its own generator stream)."""
+    draw of the same block differ: each device has its own generator stream).
+
+    attn: attention width (QKV N = 3 attn, outproj K = attn; default d).
+    swiglu: FC1 has 2 ffn rows ([gate | up]) and the FC2-input quantiser applies
+    SwiGLU (the H3 MLP); otherwise FC1 has ffn rows and a GELU epilogue."""
     g = generator(5, salt=1 + index, device=device)
+    attn = d if attn is None else attn
+    n1 = 2 * ffn if swiglu else ffn
     return BlockWeights(
         norm1=(torch.rand((d,), generator=g, device=g.device) + 0.5).to(torch.bfloat16),
         norm2=(torch.rand((d,), generator=g, device=g.device) + 0.5).to(torch.bfloat16),
-        qkv=int8_uniform(3 * d, d, g), qkv_s=uniform(3 * d, 0.0005, 0.005, g),
-        out=int8_uniform(d, d, g), out_s=uniform(d, 0.0005, 0.005, g),
-        fc1=int8_uniform(ffn, d, g), fc1_s=uniform(ffn, 0.0005, 0.005, g),
+        qkv=int8_uniform(3 * attn, d, g), qkv_s=uniform(3 * attn, 0.0005, 0.005, g),
+        out=int8_uniform(d, attn, g), out_s=uniform(d, 0.0005, 0.005, g),
+        fc1=int8_uniform(n1, d, g), fc1_s=uniform(n1, 0.0005, 0.005, g),
         fc2=int8_uniform(d, ffn, g), fc2_s=uniform(d, 0.0005, 0.005, g),
         shift_msa=normal_bf16((tables, d), 0.1, g), scale_msa=normal_bf16((tables, d), 0.1, g),
         gate_msa=normal_bf16((tables, d), 0.3, g), shift_mlp=normal_bf16((tables, d), 0.1, g),
         scale_mlp=normal_bf16((tables, d), 0.1, g), gate_mlp=normal_bf16((tables, d), 0.3, g),
     )
+
+
+# The H3 model's own block geometry (hidden 5376, attention 7168, SwiGLU MLP of
+# width 14336: FC1 N = 28672, FC2 K = 14336), runtime.py:150-160 of H3 SpeedKit.
+H3_GEOMETRY = {"d": 5376, "attn": 7168, "ffn": 14336, "swiglu": True}
+
+
+def h3_block(index: int, tables: int = 1, device="cpu") -> BlockWeights:
+    """Block `index` at the H3 model geometry (synthetic weights)."""
+    g = H3_GEOMETRY
+    return cfg5_block(index, g["d"], g["ffn"], tables, device, attn=g["attn"], swiglu=g["swiglu"])
 
 
 def cfg5_tokens(rows: int = FULL_ROWS[5], d: int = 4096, device="cpu") -> torch.Tensor:

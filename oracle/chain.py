@@ -4,8 +4,8 @@ baseline / reference arm of bench.py.
 
 Follows the block order of ``Backend.block`` (h3_speedkit/runtime.py:126-164 of
 H3 SpeedKit): prologue -> QKV -> (attention: V passthrough) -> ConvRot quant ->
-outproj gate-residual -> prologue -> FC1 (+GELU epilogue) -> ConvRot quant ->
-FC2 gate-residual.  Each step is the oracle.cpu restatement of the
+outproj gate-residual -> prologue -> FC1 (+GELU epilogue, or SwiGLU in the next
+quantiser) -> ConvRot quant -> FC2 gate-residual.  Each step is the oracle.cpu restatement of the
 corresponding kernel; arrays are numpy (BF16 as uint16 bits).
 """
 from __future__ import annotations
@@ -49,17 +49,28 @@ class NpBlock:
 
 
 def block(x: np.ndarray, b: NpBlock, rows: np.ndarray, eps: float = 1e-6, threads=None) -> np.ndarray:
-    """One block on BF16 rows x (uint16 [M, D]); returns the updated rows."""
-    d = x.shape[1]
+    """One block on BF16 rows x (uint16 [M, D]); returns the updated rows.
+
+    The geometry comes from the weights: attention width A = qkv rows / 3 (V is
+    columns [2A, 3A) of the QKV output), FFN width F = fc2 columns; an FC1 with
+    2F rows is a SwiGLU MLP ([gate | up] halves, the activation applied by the
+    FC2-input quantiser, convrot64_exact.cuh:928-937 and runtime.py:159), an FC1
+    with F rows the GELU-epilogue MLP."""
+    attn = b.qkv.shape[0] // 3
+    ffn = b.fc2.shape[1]
+    swiglu = b.fc1.shape[0] == 2 * ffn
     q, qs = ocpu.norm_quant(x, b.norm1, b.shift_msa, b.scale_msa, rows, eps, threads=threads)
     qkv = ocpu.dequant(ocpu.gemm_s32(q, b.qkv, threads=threads), qs, b.qkv_s, threads=threads)
-    v = np.ascontiguousarray(qkv[:, 2 * d:3 * d])
+    v = np.ascontiguousarray(qkv[:, 2 * attn:3 * attn])
     aq, as_ = ocpu.convrot_quant(v, threads=threads)
     x = ocpu.gate_residual(ocpu.gemm_s32(aq, b.out, threads=threads), as_, b.out_s, b.gate_msa, rows, x,
                            threads=threads)
     q, qs = ocpu.norm_quant(x, b.norm2, b.shift_mlp, b.scale_mlp, rows, eps, threads=threads)
-    h = ocpu.dequant(ocpu.gemm_s32(q, b.fc1, threads=threads), qs, b.fc1_s, gelu=True, threads=threads)
-    hq, hs = ocpu.convrot_quant(h, threads=threads)
+    h = ocpu.dequant(ocpu.gemm_s32(q, b.fc1, threads=threads), qs, b.fc1_s, gelu=not swiglu, threads=threads)
+    if swiglu:
+        hq, hs = ocpu.convrot_quant(h, k=ffn, act=2, threads=threads)
+    else:
+        hq, hs = ocpu.convrot_quant(h, threads=threads)
     return ocpu.gate_residual(ocpu.gemm_s32(hq, b.fc2, threads=threads), hs, b.fc2_s, b.gate_mlp, rows, x,
                               threads=threads)
 

@@ -114,3 +114,31 @@ def test_forward_host_pipeline_equals_forward(device, chunks):
         stack.forward_host(host_in, host_out, chunks=chunks)
         torch.cuda.synchronize()
         assert torch.equal(host_out, ref.cpu())
+
+
+def test_h3_geometry_swiglu_block_matches_cpu_restatement(device):
+    """The H3 model's block shape in miniature: attention width != D (QKV N = 3A,
+    outproj K = A) and a SwiGLU MLP (FC1 N = 2F, the FC2-input quantiser applies
+    SwiGLU to [gate | up])."""
+    m, d, attn, ffn = 384, 512, 768, 512
+    b = synthetic.cfg5_block(0, d, ffn, tables=2, attn=attn, swiglu=True).to(device)
+    x0 = synthetic.cfg5_tokens(m, d)
+    rows = (torch.arange(m) % 2).to(torch.int32)
+    x = x0.to(device)
+    LocalStack([b], x, rows.to(device)).run()
+    torch.cuda.synchronize()
+    ref = chain.block(bf16_bits(x0), chain.NpBlock.from_torch(b), rows.numpy())
+    got = bf16_bits(x)
+    same = float((got == ref).mean())
+    a = torch.from_numpy(got.view(np.int16)).view(torch.bfloat16).float()
+    r = torch.from_numpy(ref.view(np.int16)).view(torch.bfloat16).float()
+    err = ((a - r).abs().max() / r.abs().max()).item()
+    assert same > 0.99, f"only {same:.4f} of the outputs are bit-identical"
+    assert err < 1e-2, f"largest deviation {err:.2e} of the output magnitude"
+    # and row shards stay bit-identical to the whole
+    whole = x0.to(device)
+    LocalStack([b], whole, rows.to(device)).run()
+    part = x0[100:].to(device).contiguous()
+    LocalStack([b], part, rows[100:].to(device).contiguous()).run()
+    torch.cuda.synchronize()
+    assert torch.equal(part, whole[100:])

@@ -218,3 +218,16 @@ def test_node_schema_matches_the_reference():
         assert [o.kind for o in schema.outputs] == ["model", "string"]
         out = node.execute(FakeModel(), enabled=False)
         assert out[1] == "H3 SpeedKit disabled"
+
+
+def test_block_geometry_from_weight_shapes():
+    from h3_speedkit import synthetic
+    from h3_speedkit.stack import geometry
+    g = geometry(synthetic.cfg5_block(0, 512, 1024))
+    assert g == {"d": 512, "attn": 512, "ffn": 1024, "fc1_n": 1024, "swiglu": False}
+    g = geometry(synthetic.cfg5_block(0, 512, 512, attn=768, swiglu=True))
+    assert g == {"d": 512, "attn": 768, "ffn": 512, "fc1_n": 1024, "swiglu": True}
+    b = synthetic.cfg5_block(0, 512, 512, attn=768, swiglu=True)
+    b.out = b.out[:, :512]
+    with pytest.raises(ValueError):
+        geometry(b)

@@ -296,7 +296,29 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     const uint32_t row_a = ring_a + uint32_t(d * plan.slot_bytes);
 
     // 2. sum of squares
-    if (tt < 64) {
+    if (kStaged && tt < 64) {
+      // logical thread tt in acc0, logical thread tt + 64 in acc1; BF16 operands
+      // go straight into the FMAs (fma.rn.f32.bf16, see rq_core.cuh)
+      float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 4
+      for (int base = 0; base < nchunks; base += 128) {
+        const int c0 = base + tt, c1 = base + tt + 64;
+        const uint2 r0 = c0 < nchunks ? rs::lds64(row_a + rs::swz128(8u * c0)) : make_uint2(0, 0);
+        const uint2 r1 = c1 < nchunks ? rs::lds64(row_a + rs::swz128(8u * c1)) : make_uint2(0, 0);
+        acc0 = rq::fma_sq_bf2(r0.y, rq::fma_sq_bf2(r0.x, acc0));
+        acc1 = rq::fma_sq_bf2(r1.y, rq::fma_sq_bf2(r1.x, acc1));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        acc0 = ieee_add(acc0, __shfl_down_sync(kFullMask, acc0, off));
+        acc1 = ieee_add(acc1, __shfl_down_sync(kFullMask, acc1, off));
+      }
+      if (lane == 0) {
+        st.stat_fold[team][twarp] = acc0;       // logical warp twarp
+        st.stat_fold[team][twarp + 2] = acc1;   // logical warp twarp + 2
+      }
+    } else if (!kStaged && tt < 64) {
+      // the same sums as packed f32x2 FMAs (fewer registers for this variant)
       uint64_t acc = 0;
 #pragma unroll 4
       for (int base = 0; base < nchunks; base += 128) {
@@ -320,8 +342,8 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
         acc = rq::f2_add_ieee(acc, rq::f2_pack(lo, hi));
       }
       if (lane == 0) {
-        st.stat_fold[team][twarp] = rq::f2_lo(acc);       // logical warp twarp
-        st.stat_fold[team][twarp + 2] = rq::f2_hi(acc);   // logical warp twarp + 2
+        st.stat_fold[team][twarp] = rq::f2_lo(acc);
+        st.stat_fold[team][twarp + 2] = rq::f2_hi(acc);
       }
     }
     if (!rs::team_sync_and(bar_id, team_threads, ok)) break;   // barrier A

@@ -67,6 +67,17 @@ __device__ __forceinline__ uint64_t f2_add_ieee(uint64_t a, uint64_t b) {
   uint64_t c; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b)); return c;
 }
 
+// acc + x*x for both BF16 halves of `w` in element order (low half first), each an
+// IEEE round-to-nearest FMA without flush (fma.rn.f32.bf16: the BF16 product is
+// exact in FP32, so this is fma.rn.f32 on the widened value, unwidened).
+__device__ __forceinline__ float fma_sq_bf2(uint32_t w, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\t"
+      "fma.rn.f32.bf16 %0, lo, lo, %2;\n\tfma.rn.f32.bf16 %0, hi, hi, %0;\n\t}"
+      : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+
 // ---- BF16 pairs ------------------------------------------------------------------
 // A 32-bit word of two BF16 values (element 2i in the low half) -> float pair.
 __device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) { return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }

@@ -128,9 +128,23 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   nt = local / gm;
 }
 
-__device__ __forceinline__ float gelu_tanh_precise(float v) {
+// GELU-tanh, 0.5 v (1 + tanh(u)) with u = 0.7978845608028654 (v + 0.044715 v^3)
+// (convrot64_exact.cuh:913-923).  tanh(u) comes from the identity
+// tanh(u) = 2 / (1 + e^(-2u)) - 1: e^(-2u) = 2^(-2u / ln 2) by ex2.approx
+// (relative error about 2^-22), the reciprocal by rcp.approx, and the final
+// fma rounds tanh(u) to FP32 once.  Near u << 0 that rounding puts 1 + tanh(u)
+// on the same FP32 grid (multiples of 2^-24) as 1 + tanhf(u), so the tiny
+// negative-side outputs keep the reference's cancellation; elsewhere the
+// relative error of 1 + tanh(u) stays below 2^-19, far inside one BF16 ulp.
+// All 65,280 finite BF16 inputs are checked against the CPU restatement (libm
+// tanhf) to 1 BF16 ulp.  u = +-inf and NaN propagate as in the reference.
+__device__ __forceinline__ float gelu_tanh_fast(float v) {
   const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  return 0.5f * v * (1.0f + tanhf(inner));
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(inner * -2.8853900817779268f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  const float t = __fmaf_rn(2.0f, r, -1.0f);
+  return 0.5f * v * (1.0f + t);
 }
 
 // GELU of a BF16 input, rounded to BF16 (the expression of
@@ -141,7 +155,7 @@ __device__ __forceinline__ uint32_t bf_round_bits(float a) {
   return b;
 }
 __device__ __forceinline__ uint32_t gelu_bits(uint32_t b) {
-  return bf_round_bits(gelu_tanh_precise(__uint_as_float(b << 16)));
+  return bf_round_bits(gelu_tanh_fast(__uint_as_float(b << 16)));
 }
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }

@@ -93,6 +93,30 @@ def test_gelu_within_one_ulp(device, m, n, k):
     assert bf16_ulp_distance(bf16_bits(out), ref).max() <= 1
 
 
+def test_gelu_exhaustive_bf16_inputs(device):
+    """Every finite BF16 value through the FC1 GELU epilogue: with A = W = 0 and
+    xs = ws = 1 the dequant value of column n is exactly bias[n], so one GEMM
+    row with N = 65536 evaluates bf(gelu(v)) for every BF16 input v."""
+    bits = np.arange(1 << 16, dtype=np.uint32)
+    finite = (bits & 0x7F80) != 0x7F80
+    vals = bits[finite].astype(np.uint16)
+    n = (len(vals) + 255) // 256 * 256
+    bias_bits = np.zeros(n, np.uint16)
+    bias_bits[:len(vals)] = vals
+    bias = torch.from_numpy(bias_bits.view(np.int16).copy()).view(torch.bfloat16).to(device)
+    a = torch.zeros((1, 16), dtype=torch.int8, device=device)
+    w = torch.zeros((n, 16), dtype=torch.int8, device=device)
+    xs = torch.ones((1,), device=device)
+    ws = torch.ones((n,), device=device)
+    out = gemm.int8_linear(a, w, xs, ws, bias=bias, gelu=True)
+    torch.cuda.synchronize()
+    ref = ocpu.dequant(np.zeros((1, n), np.int32), np.ones(1, np.float32), np.ones(n, np.float32), bias_bits,
+                       gelu=True)
+    dist = bf16_ulp_distance(bf16_bits(out), ref)[0, :len(vals)]
+    assert dist.max() <= 1, f"{int((dist > 1).sum())} inputs beyond 1 ulp, e.g. {vals[np.argmax(dist)]:#06x}"
+    assert (dist != 0).mean() < 0.01
+
+
 @pytest.mark.parametrize("m,n,k,tables", [(256, 512, 1024, 1), (333, 1024, 4096, 4)])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_gate_residual_in_place_bitexact(device, m, n, k, tables, with_bias):

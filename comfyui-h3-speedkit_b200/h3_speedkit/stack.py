@@ -46,6 +46,65 @@ def shard_bounds(total: int, world: int, rank: int) -> tuple[int, int]:
     return start, min(total, start + per)
 
 
+def _round_up(v: int, unit: int) -> int:
+    return -(-v // unit) * unit
+
+
+def uniform_chunks(per: int, chunks: int) -> list[tuple[int, int]]:
+    """``chunks`` contiguous row ranges of (nearly) equal size covering [0, per)."""
+    step = -(-per // max(1, chunks))
+    return [(c0, min(per, c0 + step)) for c0 in range(0, per, step)]
+
+
+def chunk_schedule(per: int, world: int, unit: int = 128, min_rows: int = 1024) -> list[tuple[int, int]]:
+    """Row ranges of the end-to-end pipeline over one rank's padded shard of
+    ``per`` rows (identical on every rank).
+
+    The copy in of the first chunk and the copy out of the last chunk are the
+    only transfers not hidden behind compute, so both end chunks are small
+    (per/16 rows, at least ``min_rows``; smaller chunks lose more to kernel ramp
+    and tail than they save in copy time).  Chunks grow 4x at the head (a chunk's
+    host->device copy takes about a tenth of its compute) and shrink at the tail
+    by a factor that follows the device->host share: rank 0 copies out the rows
+    of all ``world`` ranks, about 0.1 x world of a chunk's compute, so each tail
+    chunk is at least that fraction of the one before it and the copy-out queue
+    never grows.  Middle chunks are per/4 rows.  Sizes are multiples of ``unit``
+    (one remainder chunk in the middle takes the rest)."""
+    if per < 8 * min_rows:
+        return uniform_chunks(per, max(1, min(4, per // 2048)))
+    big = _round_up(per // 4, unit)
+    small = max(min_rows, _round_up(per // 16, unit))
+    down = min(0.8, max(0.25, 0.1 * world))
+    head, s = [], small
+    while s < big:
+        head.append(s)
+        s = _round_up(4 * s, unit)
+    tail, s = [], small
+    while s < big:
+        tail.append(s)
+        s = _round_up(int(s / down), unit)
+    while sum(head) + sum(tail) > per and len(head) + len(tail) > 2:
+        (head if len(head) > 1 else tail).pop()   # drop the largest ramp chunk
+    mid = per - sum(head) - sum(tail)
+    if mid < 0:
+        return uniform_chunks(per, 4)
+    middle = []
+    if 0 < mid < small and len(head) > 1:
+        head[-1] += mid   # a small remainder joins the largest head chunk
+        mid = 0
+    if mid:
+        n_mid = -(-mid // big)
+        part = _round_up(-(-mid // n_mid), unit)
+        while mid > 0:
+            middle.append(min(part, mid))
+            mid -= middle[-1]
+    bounds, c0 = [], 0
+    for size in head + middle + tail[::-1]:
+        bounds.append((c0, c0 + size))
+        c0 += size
+    return bounds
+
+
 def gather_shards(send: torch.Tensor, out: torch.Tensor, total: int, group=None) -> torch.Tensor:
     """Assemble the token-sharded output: every rank contributes its padded shard
     ``send`` [ceil(total/world), D]; ``out`` [world * ceil(total/world), D]
@@ -267,20 +326,18 @@ class ShardedStack:
         return self.gather()
 
     # ---- end to end from pinned host memory, copies overlapped with compute -------
-    MIN_CHUNK_ROWS = 2048
-
     def _chunking(self, chunks: int | None):
         """Chunk boundaries over the padded shard (identical on every rank, so every
         rank issues the same collectives) and one LocalStack per chunk sharing one
-        workspace sized for a chunk."""
-        if chunks is None:
-            chunks = max(1, min(4, self.per // self.MIN_CHUNK_ROWS))
+        workspace sized for the largest chunk.  ``chunks=None`` takes
+        ``chunk_schedule`` (small end chunks, ramped tail); an int gives that many
+        equal chunks."""
         key = ("chunks", chunks)
         cached = getattr(self, "_chunk_cache", None)
         if cached is not None and cached[0] == key:
             return cached[1]
-        step = -(-self.per // chunks)
-        bounds = [(c0, min(self.per, c0 + step)) for c0 in range(0, self.per, step)]
+        bounds = chunk_schedule(self.per, self.world) if chunks is None else uniform_chunks(self.per, chunks)
+        step = max(c1 - c0 for c0, c1 in bounds)
         stacks = []
         ws = None
         if self.local is not None:
@@ -323,21 +380,16 @@ class ShardedStack:
                 ev.record(h2d)
                 arrived.append(ev)
         multi = dist.is_initialized() and self.world > 1
-        if multi and getattr(self, "_gather_chunks", None) is None:
-            step = bounds[0][1] - bounds[0][0]
-            self._gather_chunks = [torch.empty((self.world * step, self.x.shape[1]), dtype=self.send.dtype,
-                                               device=self.send.device) for _ in range(2)]
-        copied = [None, None]   # D2H completion of the last chunk gathered into each buffer
-        for i, ((c0, c1), stack, ev) in enumerate(zip(bounds, stacks, arrived)):
+        for (c0, c1), stack, ev in zip(bounds, stacks, arrived):
             comp.wait_event(ev)
             if stack is not None:
                 stack.run()
             rows = c1 - c0
             if multi:
-                buf = i % 2
-                if copied[buf] is not None:
-                    comp.wait_event(copied[buf])   # its previous rows are on the host
-                out = self._gather_chunks[buf][: self.world * rows]
+                # chunk [c0, c1) of every rank, rank-major, in its own region of the
+                # gather buffer: no region is reused within a call, so no gather
+                # waits for an earlier chunk's copy out
+                out = self.out[self.world * c0: self.world * c1]
                 dist.all_gather_into_tensor(out, self.send[c0:c1], group=self.group)
             if host_out is None:
                 continue
@@ -354,7 +406,5 @@ class ShardedStack:
                         g0, g1 = r * self.per + c0, min(self.total, r * self.per + c1)
                         if g1 > g0:
                             host_out[g0:g1].copy_(out[r * rows: r * rows + (g1 - g0)], non_blocking=True)
-                    copied[buf] = torch.cuda.Event()
-                    copied[buf].record(d2h)
         comp.wait_stream(d2h)
         comp.wait_stream(h2d)

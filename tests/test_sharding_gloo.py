@@ -77,3 +77,28 @@ def test_shard_bounds_cover_every_token_once():
                 assert b == c and a <= b
     with pytest.raises(ValueError):
         shard_bounds(10, 2, 2)
+
+
+def test_chunk_schedule_covers_the_shard_with_small_end_chunks():
+    """The end-to-end pipeline's chunks cover [0, per) once, in order; the first
+    and last chunks are the smallest; the tail never shrinks faster than the
+    copy-out share allows (up to the 128-row rounding), and every chunk but one
+    is a multiple of 128 rows."""
+    from h3_speedkit.stack import chunk_schedule
+    for per in (1, 1001, 7000, 8192, 12288, 16128, 24576, 30000, 49152, 98304, 98305):
+        for world in (1, 2, 4, 8):
+            bounds = chunk_schedule(per, world)
+            assert bounds[0][0] == 0 and bounds[-1][1] == per
+            for (a, b), (c, d) in zip(bounds, bounds[1:]):
+                assert b == c and a < b
+            sizes = [b - a for a, b in bounds]
+            if per < 8 * 1024:
+                assert len(sizes) <= 4
+                continue
+            small = max(1024, -(-(per // 16) // 128) * 128)
+            assert sizes[0] == small and sizes[-1] == small
+            assert sum(s % 128 != 0 for s in sizes) <= 1
+            down = min(0.8, max(0.25, 0.1 * world))
+            tail = sizes[sizes.index(max(sizes)):]
+            for prev, nxt in zip(tail, tail[1:]):
+                assert nxt >= down * prev - 128

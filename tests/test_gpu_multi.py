@@ -22,7 +22,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, m, result_path):
+def _worker(rank, world, port, m, result_path, chunks=3):
     import datetime
     import sys
     from pathlib import Path
@@ -47,7 +47,7 @@ def _worker(rank, world, port, m, result_path):
         host_in = x_all[start:stop].contiguous().pin_memory()
         host_out = torch.empty((m, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
         for _ in range(2):
-            stack.forward_host(host_in, host_out, chunks=3)
+            stack.forward_host(host_in, host_out, chunks=chunks)
         torch.cuda.synchronize()
         if rank == 0:
             ref = x_all.to(dev)
@@ -60,10 +60,13 @@ def _worker(rank, world, port, m, result_path):
         dist.destroy_process_group()
 
 
-def test_two_gpu_token_sharding_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("m,chunks", [(1001, 3), (20011, None)])
+def test_two_gpu_token_sharding_matches_one_gpu(tmp_path, m, chunks):
+    """(20011, None): 10006 rows per rank take the ramped chunk schedule, with a
+    ragged last shard and a chunk that is not a multiple of 128 rows."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     result = tmp_path / "result.txt"
-    mp.spawn(_worker, args=(2, _free_port(), 1001, str(result)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), m, str(result), chunks), nprocs=2, join=True)
     assert result.read_text() == "ok"

@@ -72,31 +72,81 @@ template <> __device__ __forceinline__ uint4 table8<float>(const float* p, int v
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <class ModT, bool kDebug>
+// Eight consecutive BF16 values through plain (coherent) loads, for rows this
+// kernel also writes.
+__device__ __forceinline__ uint4 load8_rw(const __nv_bfloat16* p, int vec16) {
+  if (vec16) return *reinterpret_cast<const uint4*>(p);
+  const uint2 a = reinterpret_cast<const uint2*>(p)[0], b = reinterpret_cast<const uint2*>(p)[1];
+  return make_uint4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, uint4 v, int vec16) {
+  if (vec16) {
+    *reinterpret_cast<uint4*>(p) = v;
+  } else {
+    reinterpret_cast<uint2*>(p)[0] = make_uint2(v.x, v.y);
+    reinterpret_cast<uint2*>(p)[1] = make_uint2(v.z, v.w);
+  }
+}
+// bf(fma(branch, bf(gate), x)) of eight elements (residual_quant.cu:59-71).
+__device__ __forceinline__ uint4 residual8(uint4 b, uint4 g, uint4 x) {
+  return make_uint4(rq::residual_bf2(b.x, g.x, x.x), rq::residual_bf2(b.y, g.y, x.y),
+                    rq::residual_bf2(b.z, g.z, x.z), rq::residual_bf2(b.w, g.w, x.w));
+}
+
+// One CTA per row.  kResidual (the fused residual prologue of
+// kernels/residual_quant/residual_quant.cu:134-224): the row is first updated
+// in place, XOut[row] = bf(fma(Branch[row], bf(Gate[Rows[row]]), XOut[row]))
+// (contiguous rows of K), into a shared-memory copy that the prologue below
+// then reads instead of X.
+template <class ModT, bool kDebug, class GateT = float, bool kResidual = false>
 __global__ void __launch_bounds__(256) norm_quant_rows(
     const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ W,
     const ModT* __restrict__ Shift, const ModT* __restrict__ Scale,
     const int32_t* __restrict__ Rows, int8_t* __restrict__ Q, float* __restrict__ QScale,
     __nv_bfloat16* __restrict__ DebugNorm, float* __restrict__ DebugRotated,
     float* __restrict__ DebugRstd, int64_t xs, int64_t ss, int64_t cs, float eps, int K,
-    int x_vec16, int w_vec16, int t_vec16, int q_vec16) {
+    int x_vec16, int w_vec16, int t_vec16, int q_vec16, __nv_bfloat16* __restrict__ XOut = nullptr,
+    const __nv_bfloat16* __restrict__ Branch = nullptr, const GateT* __restrict__ Gate = nullptr,
+    int64_t gs = 0, int b_vec16 = 0, int g_vec16 = 0) {
   extern __shared__ __align__(16) float exch[];
   __shared__ float fold[8];
   __shared__ float row_stat;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x;
-  const __nv_bfloat16* xr = X + row * xs;
+  const __nv_bfloat16* xr = kResidual ? nullptr : X + row * xs;
+  // kResidual: the updated row, after the exchange buffers
+  uint4* xrow = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(exch) + norm_smem(K));
+
+  // 0. Residual update (kResidual).
+  if constexpr (kResidual) {
+    __nv_bfloat16* xw = XOut + row * K;
+    const __nv_bfloat16* br = Branch + row * K;
+    const GateT* gr = Gate + int64_t(Rows[row]) * gs;
+    for (int c = tid; c < K / 8; c += int(blockDim.x)) {
+      const uint4 nv = residual8(load8(br + 8 * c, b_vec16), table8<GateT>(gr + 8 * c, g_vec16),
+                                 load8_rw(xw + 8 * c, x_vec16));
+      xrow[c] = nv;
+      store8(xw + 8 * c, nv, x_vec16);
+    }
+    __syncthreads();
+  }
 
   // 1. Sum of squares in the reference's order: logical threads tid and tid+64.
   if (tid < 64) {
-    const uint2* chunks = reinterpret_cast<const uint2*>(xr);
+    const uint2* chunks = kResidual ? reinterpret_cast<const uint2*>(xrow) : reinterpret_cast<const uint2*>(xr);
     const int nchunks = K / 4;
     uint64_t acc = 0;   // (+0.0f, +0.0f)
 #pragma unroll 4
     for (int base = 0; base < nchunks; base += 128) {
       const int c0 = base + tid, c1 = base + tid + 64;
-      const uint2 r0 = c0 < nchunks ? __ldg(chunks + c0) : make_uint2(0, 0);
-      const uint2 r1 = c1 < nchunks ? __ldg(chunks + c1) : make_uint2(0, 0);
+      uint2 r0 = make_uint2(0, 0), r1 = make_uint2(0, 0);
+      if constexpr (kResidual) {
+        if (c0 < nchunks) r0 = chunks[c0];
+        if (c1 < nchunks) r1 = chunks[c1];
+      } else {
+        if (c0 < nchunks) r0 = __ldg(chunks + c0);
+        if (c1 < nchunks) r1 = __ldg(chunks + c1);
+      }
       // element order inside a chunk: r.x low, r.x high, r.y low, r.y high
       uint64_t e;
       e = rq::f2_pack(__uint_as_float(r0.x << 16), __uint_as_float(r1.x << 16));
@@ -141,7 +191,7 @@ __global__ void __launch_bounds__(256) norm_quant_rows(
     const uint32_t one2 = 0x3F803F80u;   // BF16 (1, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint4 xv = load8(xr + col0 + 8 * i, x_vec16);
+      const uint4 xv = kResidual ? xrow[(col0 >> 3) + i] : load8(xr + col0 + 8 * i, x_vec16);
       const uint4 wv = load8(W + col0 + 8 * i, w_vec16);
       const uint4 sv = table8<ModT>(shift_row + 8 * i, t_vec16);
       const uint4 cv = table8<ModT>(scale_row + 8 * i, t_vec16);
@@ -218,13 +268,19 @@ __global__ void __launch_bounds__(256) norm_quant_rows(
 // memory): every CTA first stages W, bf(1 + bf(scale_t)) and bf(shift_t) for all
 // tables in shared memory with the rows' 128-byte swizzle, and step 3 happens in
 // layout A straight from shared memory -- no modulation pass, no barrier B.
+// kResidual (the fused residual prologue, residual_quant.cu:134-224): each slot
+// also receives the Branch row (second TMA box at byte `boff`); before step 2 the
+// team rewrites the row in the slot as bf(fma(branch, bf(Gate[Rows[row]]), x))
+// and stores it to XOut (contiguous rows of K), then barrier R.
 // The arithmetic is that of norm_quant_rows, value for value.
-template <class ModT, bool kStaged, bool kInSlot>
+template <class ModT, bool kStaged, bool kInSlot, class GateT = float, bool kResidual = false>
 __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     const __grid_constant__ CUtensorMap map_x, const __nv_bfloat16* __restrict__ W,
     const ModT* __restrict__ Shift, const ModT* __restrict__ Scale, const int32_t* __restrict__ Rows,
     int8_t* __restrict__ Q, float* __restrict__ QScale, int64_t ss, int64_t cs, float eps, int64_t M,
-    const rs::Plan plan, int tables, int w_vec16, int t_vec16, int q_vec16, int* status) {
+    const rs::Plan plan, int tables, int w_vec16, int t_vec16, int q_vec16, int* status,
+    const __grid_constant__ CUtensorMap map_b, __nv_bfloat16* __restrict__ XOut,
+    const GateT* __restrict__ Gate, int64_t gs, int g_vec16, uint32_t boff) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ rs::RingState st;
   unsigned char* smem =
@@ -275,14 +331,26 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     __syncthreads();
   }
 
+  // One row (and, kResidual, its branch row) into a slot.
+  auto issue = [&](unsigned char* slot, uint64_t* bar, int r) {
+    if constexpr (kResidual) {
+      const uint64_t policy = rs::l2_policy_evict_first();
+      sm100::mbar_arrive_expect_tx(bar, uint32_t(K) * 4u);
+      rs::tma_load_3d(slot, &map_x, bar, 0, 0, r, policy);
+      rs::tma_load_3d(slot + boff, &map_b, bar, 0, 0, r, policy);
+    } else {
+      rs::issue_row(&map_x, slot, bar, r, K, K);
+    }
+  };
+
   int issued = 0;
   if (tt == 0) {
     for (int d = 0; d < D; ++d) sm100::mbar_init(&full[d], 1);
     sm100::fence_mbar_init();
     sm100::tma_prefetch_map(&map_x);
+    if constexpr (kResidual) sm100::tma_prefetch_map(&map_b);
     for (; issued < D && issued < n_team; ++issued)
-      rs::issue_row(&map_x, ring + size_t(issued) * plan.slot_bytes, &full[issued],
-                    int(blockIdx.x) + (team + issued * teams) * grid, K, K);
+      issue(ring + size_t(issued) * plan.slot_bytes, &full[issued], int(blockIdx.x) + (team + issued * teams) * grid);
   }
   rs::team_sync(bar_id, team_threads);
 
@@ -294,6 +362,22 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     const int64_t row = int64_t(blockIdx.x) + int64_t(team + k * teams) * grid;
     const bool ok = sm100::mbar_wait_bounded(&full[d], ph, nullptr, status, rs::kCodeFull, rs::kWaitNs);
     const uint32_t row_a = ring_a + uint32_t(d * plan.slot_bytes);
+
+    // 1b. residual update in the slot and in XOut (kResidual)
+    if constexpr (kResidual) {
+      const int gate_row = kStaged ? min(max(__ldg(Rows + row), 0), tables - 1) : __ldg(Rows + row);
+      const GateT* grow = Gate + int64_t(gate_row) * gs;
+      if (ok) {
+        for (int c = tt; c < nchunks16; c += team_threads) {
+          const uint32_t off = rs::swz128(16u * uint32_t(c));
+          const uint4 nv = residual8(rs::lds128(row_a + boff + off), table8<GateT>(grow + 8 * c, g_vec16),
+                                     rs::lds128(row_a + off));
+          rs::sts128(row_a + off, nv.x, nv.y, nv.z, nv.w);
+          *reinterpret_cast<uint4*>(XOut + row * K + 8 * c) = nv;
+        }
+      }
+      if (!rs::team_sync_and(bar_id, team_threads, ok)) break;   // barrier R
+    }
 
     // 2. sum of squares
     if (kStaged && tt < 64) {
@@ -445,14 +529,13 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
     }
     // This thread's generic-proxy writes to the slot (modulation pass, in-slot
     // exchange) are ordered before the TMA (async proxy) that refills it.
-    if constexpr (!kStaged || kInSlot) sm100::fence_async_shared();
+    if constexpr (!kStaged || kInSlot || kResidual) sm100::fence_async_shared();
     rq::fht_layout_b(v);
     const float local = warp_allmax(rq::absmax64(v));
     if (lane == 0) st.max_fold[team][parity][twarp] = local;
     rs::team_sync(bar_id, team_threads);   // barrier C
     if (tt == 0 && issued < n_team) {
-      rs::issue_row(&map_x, ring + size_t(d) * plan.slot_bytes, &full[d], int(blockIdx.x) + (team + issued * teams) * grid,
-                    K, K);
+      issue(ring + size_t(d) * plan.slot_bytes, &full[d], int(blockIdx.x) + (team + issued * teams) * grid);
       ++issued;
     }
     if (++d == D) { d = 0; ph ^= 1u; }
@@ -473,15 +556,15 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
       sm100::mbar_wait_bounded(&full[j % D], uint32_t((j / D) & 1), nullptr, status, rs::kCodeFull, rs::kWaitNs);
 }
 
-template <class T, bool D>
+template <class T, bool D, class G = float, bool R = false>
 int query_kernel(int k, H3NormQuantResources* out) {
   cudaFuncAttributes a{};
-  auto kernel = norm_quant_rows<T, D>;
+  auto kernel = norm_quant_rows<T, D, G, R>;
   const int threads = norm_threads(k);
   int active = 0, device = 0, sms = 0, max_threads = 0;
   cudaError_t e = cudaFuncGetAttributes(&a, kernel);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, norm_smem(k));
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, kernel, threads, norm_smem(k) + (R ? 2 * k : 0));
   if (e != cudaSuccess) return e;
   if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return e;
@@ -495,12 +578,24 @@ int query_kernel(int k, H3NormQuantResources* out) {
 
 bool valid_k(int64_t k) { return k >= 256 && k <= kMaxK && k % 256 == 0; }
 
+// Operands of the fused residual prologue (residual_quant.cu:238-289): x is
+// updated in place (contiguous rows of K) from branch (contiguous rows of K)
+// and the gate table [T, >= gs] (gate_dtype 0 = FP32, 1 = BF16).
+struct ResidualArgs {
+  void* x;
+  const void* branch;
+  const void* gate;
+  int64_t gs;
+  int gate_dtype;
+};
+
 // tables: number of table rows T (shift/scale are [T, >=K]); 0 = not known.
+// res: the residual operands, or null for the plain prologue.
 int run_checked(const void* x, const void* w, const void* shift, const void* scale,
                 const void* rows, void* q, void* qscale, void* dn, void* dr, void* drs,
                 int64_t m, int64_t k, int64_t tables, int64_t xs, int64_t ss, int64_t cs, float eps,
-                int table_dtype, int debug, uintptr_t stream_ptr) {
-  // Contract of norm_quant.cu:247-255, with K a runtime value.
+                int table_dtype, int debug, uintptr_t stream_ptr, const ResidualArgs* res = nullptr) {
+  // Contract of norm_quant.cu:247-255 (residual_quant.cu:259-270), with K a runtime value.
   if (!valid_k(k)) return cudaErrorInvalidValue;
   if (!x || !w || !shift || !scale || !rows || !q || !qscale || m < 1 || m > INT32_MAX ||
       xs < k || xs % 4 || ss < k || cs < k || table_dtype < 0 || table_dtype > 1 || debug < 0 ||
@@ -509,6 +604,9 @@ int run_checked(const void* x, const void* w, const void* shift, const void* sca
   if ((uintptr_t(x) & 7u) || (uintptr_t(w) & 7u) || (uintptr_t(q) & 7u) || (uintptr_t(qscale) & 3u) ||
       (uintptr_t(rows) & 3u) || (uintptr_t(shift) % (table_dtype ? 2 : 4)) ||
       (uintptr_t(scale) % (table_dtype ? 2 : 4)))
+    return cudaErrorInvalidValue;
+  if (res && (!res->branch || !res->gate || res->gs < k || res->gate_dtype < 0 || res->gate_dtype > 1 ||
+              xs != k || (uintptr_t(res->branch) & 7u) || (uintptr_t(res->gate) % (res->gate_dtype ? 2 : 4))))
     return cudaErrorInvalidValue;
   if (debug && (!dn || !dr || !drs || (uintptr_t(dn) & 1u) || (uintptr_t(dr) & 3u) || (uintptr_t(drs) & 3u)))
     return cudaErrorInvalidValue;
@@ -519,69 +617,98 @@ int run_checked(const void* x, const void* w, const void* shift, const void* sca
   const int64_t tsz = table_dtype ? 2 : 4;
   const int t_vec16 = ((uintptr_t(shift) & 15u) == 0 && (uintptr_t(scale) & 15u) == 0 && (ss * tsz) % 16 == 0 &&
                        (cs * tsz) % 16 == 0) ? 1 : 0;
+  const int b_vec16 = res && (uintptr_t(res->branch) & 15u) == 0 ? 1 : 0;
+  const int64_t gsz = res && res->gate_dtype ? 2 : 4;
+  const int g_vec16 = res && (uintptr_t(res->gate) & 15u) == 0 && (res->gs * gsz) % 16 == 0 ? 1 : 0;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (tables < 0 || tables > INT32_MAX) return cudaErrorInvalidValue;
-  if (!debug && x_vec16) {
-    // Streaming kernel: TMA needs 16-byte aligned rows, which x_vec16 states.
-    // With T known and W plus T tables fitting beside two ring slots per team,
-    // the tables are staged in shared memory.
+  if (!debug && x_vec16 && (!res || b_vec16)) {
+    // Streaming kernel: TMA needs 16-byte aligned rows, which x_vec16 (and, for the
+    // residual form, b_vec16) states.  With T known and W plus T tables fitting
+    // beside two ring slots per team, the tables are staged in shared memory.
+    // The residual form's slot holds the row and its branch row at `boff`.
+    const uint32_t boff = uint32_t((k * 2 + 1023) / 1024 * 1024);
+    const int width = res ? int(boff / 2 + k) : int(k);
     const int arr_bytes = int((k * 2 + 1023) / 1024 * 1024);
     const int64_t staged_bytes = tables > 0 ? int64_t(arr_bytes) * (1 + 2 * tables) : -1;
-    rs::Plan plan = rs::make_plan(int(k), int(k), 64);
+    rs::Plan plan = rs::make_plan(int(k), width, 64);
     bool staged = false;
     if (staged_bytes > 0 && staged_bytes <= rs::kSmemBudget) {
       // Stage only when it costs no row team.
-      const rs::Plan sp = rs::make_plan(int(k), int(k), 64, int(staged_bytes));
+      const rs::Plan sp = rs::make_plan(int(k), width, 64, int(staged_bytes));
       if (sp.teams >= 1 && sp.teams == plan.teams && sp.smem <= rs::kSmemBudget) {
         plan = sp;
         staged = true;
       }
     }
-    CUtensorMap map;
-    if (plan.teams >= 1 && plan.slots_per_team >= 2 && rs::make_row_map(&map, x, m, int(k), int(k), xs)) {
+    CUtensorMap map, map_b;
+    bool maps = plan.teams >= 1 && plan.slots_per_team >= 2 && rs::make_row_map(&map, x, m, int(k), int(k), xs);
+    if (maps && res) maps = rs::make_row_map(&map_b, res->branch, m, int(k), int(k), k);
+    if (maps) {
+      if (!res) map_b = map;
       int* status = status_device_ptr();
       if (!status) return cudaErrorInvalidDevicePointer;
       int grid = 0;
-#define H3SK_NQ_STREAM(T, S)                                                                                \
+#define H3SK_NQ_STREAM(T, S, G, R)                                                                          \
   do {                                                                                                      \
-    auto kernel = plan.exch_bytes ? norm_quant_stream<T, S, false> : norm_quant_stream<T, S, true>;         \
+    auto kernel = plan.exch_bytes ? norm_quant_stream<T, S, false, G, R> : norm_quant_stream<T, S, true, G, R>; \
     const cudaError_t e = rs::stream_grid(reinterpret_cast<const void*>(kernel), plan.smem, m, &grid);      \
     if (e != cudaSuccess) return e;                                                                         \
     kernel<<<grid, plan.threads, plan.smem, stream>>>(                                                      \
         map, static_cast<const __nv_bfloat16*>(w), static_cast<const T*>(shift), static_cast<const T*>(scale), \
         static_cast<const int32_t*>(rows), static_cast<int8_t*>(q), static_cast<float*>(qscale), ss, cs, eps, m, \
-        plan, int(tables), w_vec16, t_vec16, q_vec16, status);                                              \
+        plan, int(tables), w_vec16, t_vec16, q_vec16, status, map_b,                                        \
+        static_cast<__nv_bfloat16*>(res ? res->x : nullptr), static_cast<const G*>(res ? res->gate : nullptr), \
+        res ? res->gs : 0, g_vec16, boff);                                                                  \
   } while (0)
-      if (table_dtype == 0) {
-        if (staged) H3SK_NQ_STREAM(float, true); else H3SK_NQ_STREAM(float, false);
-      } else {
-        if (staged) H3SK_NQ_STREAM(__nv_bfloat16, true); else H3SK_NQ_STREAM(__nv_bfloat16, false);
-      }
+#define H3SK_NQ_STREAM_T(T, G, R)                                                                            \
+  do {                                                                                                      \
+    if (staged) H3SK_NQ_STREAM(T, true, G, R); else H3SK_NQ_STREAM(T, false, G, R);                         \
+  } while (0)
+#define H3SK_NQ_STREAM_G(G, R)                                                                               \
+  do {                                                                                                      \
+    if (table_dtype == 0) H3SK_NQ_STREAM_T(float, G, R); else H3SK_NQ_STREAM_T(__nv_bfloat16, G, R);        \
+  } while (0)
+      if (!res) H3SK_NQ_STREAM_G(float, false);
+      else if (res->gate_dtype == 0) H3SK_NQ_STREAM_G(float, true);
+      else H3SK_NQ_STREAM_G(__nv_bfloat16, true);
+#undef H3SK_NQ_STREAM_G
+#undef H3SK_NQ_STREAM_T
 #undef H3SK_NQ_STREAM
       return cudaGetLastError();
     }
   }
   const int threads = norm_threads(int(k));
-  const int smem = norm_smem(int(k));
-#define H3SK_NQ_LAUNCH(T, D)                                                                       \
+  const int smem = norm_smem(int(k)) + (res ? int(k) * 2 : 0);
+#define H3SK_NQ_LAUNCH(T, D, G, R)                                                                 \
   do {                                                                                             \
-    auto kernel = norm_quant_rows<T, D>;                                                           \
+    auto kernel = norm_quant_rows<T, D, G, R>;                                                     \
     if (smem > 48 * 1024) {                                                                        \
       const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
       if (e != cudaSuccess) return e;                                                              \
     }                                                                                              \
     kernel<<<dim3(unsigned(m)), threads, smem, stream>>>(                                          \
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),               \
+        static_cast<const __nv_bfloat16*>(res ? nullptr : x), static_cast<const __nv_bfloat16*>(w), \
         static_cast<const T*>(shift), static_cast<const T*>(scale), static_cast<const int32_t*>(rows), \
         static_cast<int8_t*>(q), static_cast<float*>(qscale), static_cast<__nv_bfloat16*>(dn),     \
         static_cast<float*>(dr), static_cast<float*>(drs), xs, ss, cs, eps, int(k), x_vec16, w_vec16, \
-        t_vec16, q_vec16);                                                                                  \
+        t_vec16, q_vec16, static_cast<__nv_bfloat16*>(res ? res->x : nullptr),                      \
+        static_cast<const __nv_bfloat16*>(res ? res->branch : nullptr),                            \
+        static_cast<const G*>(res ? res->gate : nullptr), res ? res->gs : 0, b_vec16, g_vec16);    \
   } while (0)
-  if (table_dtype == 0) {
-    if (debug) H3SK_NQ_LAUNCH(float, true); else H3SK_NQ_LAUNCH(float, false);
-  } else {
-    if (debug) H3SK_NQ_LAUNCH(__nv_bfloat16, true); else H3SK_NQ_LAUNCH(__nv_bfloat16, false);
-  }
+#define H3SK_NQ_LAUNCH_T(T, G, R)                                                                  \
+  do {                                                                                             \
+    if (debug) H3SK_NQ_LAUNCH(T, true, G, R); else H3SK_NQ_LAUNCH(T, false, G, R);                 \
+  } while (0)
+#define H3SK_NQ_LAUNCH_G(G, R)                                                                     \
+  do {                                                                                             \
+    if (table_dtype == 0) H3SK_NQ_LAUNCH_T(float, G, R); else H3SK_NQ_LAUNCH_T(__nv_bfloat16, G, R); \
+  } while (0)
+  if (!res) H3SK_NQ_LAUNCH_G(float, false);
+  else if (res->gate_dtype == 0) H3SK_NQ_LAUNCH_G(float, true);
+  else H3SK_NQ_LAUNCH_G(__nv_bfloat16, true);
+#undef H3SK_NQ_LAUNCH_G
+#undef H3SK_NQ_LAUNCH_T
 #undef H3SK_NQ_LAUNCH
   return cudaGetLastError();
 }
@@ -592,6 +719,32 @@ int query_checked(int64_t k, int table_dtype, int debug, H3NormQuantResources* o
     return cudaErrorInvalidValue;
   if (table_dtype == 0) return debug ? query_kernel<float, true>(int(k), out) : query_kernel<float, false>(int(k), out);
   return debug ? query_kernel<__nv_bfloat16, true>(int(k), out) : query_kernel<__nv_bfloat16, false>(int(k), out);
+}
+
+// Resources of the one-CTA-per-row residual kernel (residual_quant.cu:230-252).
+int query_residual(int64_t k, int gate_dtype, int table_dtype, int debug, H3NormQuantResources* out, size_t bytes) {
+  if (!out || bytes != sizeof(H3NormQuantResources) || !valid_k(k) || gate_dtype < 0 || gate_dtype > 1 ||
+      table_dtype < 0 || table_dtype > 1 || debug < 0 || debug > 1)
+    return cudaErrorInvalidValue;
+  const int kk = int(k);
+#define H3SK_RQ_QUERY(G, T) \
+  return debug ? query_kernel<T, true, G, true>(kk, out) : query_kernel<T, false, G, true>(kk, out)
+  if (gate_dtype == 0) {
+    if (table_dtype == 0) H3SK_RQ_QUERY(float, float);
+    H3SK_RQ_QUERY(float, __nv_bfloat16);
+  }
+  if (table_dtype == 0) H3SK_RQ_QUERY(__nv_bfloat16, float);
+  H3SK_RQ_QUERY(__nv_bfloat16, __nv_bfloat16);
+#undef H3SK_RQ_QUERY
+}
+
+int run_residual(void* x, const void* branch, const void* w, const void* gate, const void* shift, const void* scale,
+                 const void* rows, void* q, void* qscale, void* dn, void* dr, void* drs, int64_t m, int64_t k,
+                 int64_t tables, int64_t gs, int64_t ss, int64_t cs, float eps, int gate_dtype, int table_dtype,
+                 int debug, uintptr_t stream) {
+  const ResidualArgs res{x, branch, gate, gs, gate_dtype};
+  return run_checked(x, w, shift, scale, rows, q, qscale, dn, dr, drs, m, k, tables, k, ss, cs, eps, table_dtype,
+                     debug, stream, &res);
 }
 
 }  // namespace
@@ -636,4 +789,45 @@ H3SK_EXPORT int h3_norm_quant_run_t(const void* x, const void* w, const void* sh
   if (tables < 1) return cudaErrorInvalidValue;
   return h3sk::run_checked(x, w, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
                            m, k, tables, xs, ss, cs, eps, table_dtype, debug, stream);
+}
+
+// Fused residual prologue: x <- bf(fma(branch, bf(gate[rows]), x)) in place, then
+// the prologue on the updated rows (kernels/residual_quant/residual_quant.cu).
+H3SK_EXPORT int h3_residual_quant_abi(void) { return 1; }
+H3SK_EXPORT size_t h3_residual_quant_resources_size(void) { return sizeof(H3NormQuantResources); }
+H3SK_EXPORT const char* h3_residual_quant_error(int code) {
+  return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
+H3SK_EXPORT int h3_residual_quant_query(int gate_dtype, int table_dtype, int debug, H3NormQuantResources* out,
+                                        size_t bytes) {
+  return h3sk::query_residual(h3sk::kNormK, gate_dtype, table_dtype, debug, out, bytes);
+}
+H3SK_EXPORT int h3_residual_quant_query_k(int64_t k, int gate_dtype, int table_dtype, int debug,
+                                          H3NormQuantResources* out, size_t bytes) {
+  return h3sk::query_residual(k, gate_dtype, table_dtype, debug, out, bytes);
+}
+H3SK_EXPORT int h3_residual_quant_run(void* x, const void* branch, const void* w, const void* gate,
+                                      const void* shift, const void* scale, const void* rows, void* q,
+                                      void* qscale, void* debug_norm, void* debug_rotated, void* debug_rstd,
+                                      int64_t m, int64_t gs, int64_t ss, int64_t cs, float eps, int gate_dtype,
+                                      int table_dtype, int debug, uintptr_t stream) {
+  return h3sk::run_residual(x, branch, w, gate, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
+                            m, h3sk::kNormK, 0, gs, ss, cs, eps, gate_dtype, table_dtype, debug, stream);
+}
+H3SK_EXPORT int h3_residual_quant_run_k(void* x, const void* branch, const void* w, const void* gate,
+                                        const void* shift, const void* scale, const void* rows, void* q,
+                                        void* qscale, void* debug_norm, void* debug_rotated, void* debug_rstd,
+                                        int64_t m, int64_t k, int64_t gs, int64_t ss, int64_t cs, float eps,
+                                        int gate_dtype, int table_dtype, int debug, uintptr_t stream) {
+  return h3sk::run_residual(x, branch, w, gate, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
+                            m, k, 0, gs, ss, cs, eps, gate_dtype, table_dtype, debug, stream);
+}
+H3SK_EXPORT int h3_residual_quant_run_t(void* x, const void* branch, const void* w, const void* gate,
+                                        const void* shift, const void* scale, const void* rows, void* q,
+                                        void* qscale, void* debug_norm, void* debug_rotated, void* debug_rstd,
+                                        int64_t m, int64_t k, int64_t tables, int64_t gs, int64_t ss, int64_t cs,
+                                        float eps, int gate_dtype, int table_dtype, int debug, uintptr_t stream) {
+  if (tables < 1) return cudaErrorInvalidValue;
+  return h3sk::run_residual(x, branch, w, gate, shift, scale, rows, q, qscale, debug_norm, debug_rotated, debug_rstd,
+                            m, k, tables, gs, ss, cs, eps, gate_dtype, table_dtype, debug, stream);
 }

@@ -78,6 +78,22 @@ __device__ __forceinline__ float fma_sq_bf2(uint32_t w, float acc) {
   return d;
 }
 
+// Residual update of two BF16 elements (residual_quant.cu:59-71):
+// bf(fma(b, g, x)) per half, where the FMA is the IEEE round-to-nearest
+// fma.rn.f32.bf16 (exact BF16 product, FP32 addend x widened, one rounding, no
+// flush) and the FP32 result is rounded once more to BF16.  b, g, x: BF16 pair
+// words, element 2i in the low half; g already rounded to BF16.
+__device__ __forceinline__ uint32_t residual_bf2(uint32_t b, uint32_t g, uint32_t x) {
+  float lo, hi;
+  asm("{\n\t.reg .b16 bl, bh, gl, gh;\n\tmov.b32 {bl, bh}, %2;\n\tmov.b32 {gl, gh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, bl, gl, %4;\n\tfma.rn.f32.bf16 %1, bh, gh, %5;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(b), "r"(g), "f"(__uint_as_float(x << 16)), "f"(__uint_as_float(x & 0xffff0000u)));
+  uint32_t w;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
+  return w;
+}
+
 // ---- BF16 pairs ------------------------------------------------------------------
 // A 32-bit word of two BF16 values (element 2i in the low half) -> float pair.
 __device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) { return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }

@@ -26,6 +26,14 @@ EXPORTS = {
     "h3_norm_quant_run": ([_P] * 10 + [_I64] * 4 + [_F, _I, _I, _SZ], _I),
     "h3_norm_quant_run_k": ([_P] * 10 + [_I64] * 5 + [_F, _I, _I, _SZ], _I),
     "h3_norm_quant_run_t": ([_P] * 10 + [_I64] * 6 + [_F, _I, _I, _SZ], _I),
+    "h3_residual_quant_abi": ([], _I),
+    "h3_residual_quant_resources_size": ([], _SZ),
+    "h3_residual_quant_error": ([_I], ct.c_char_p),
+    "h3_residual_quant_query": ([_I, _I, _I, _P, _SZ], _I),
+    "h3_residual_quant_query_k": ([_I64, _I, _I, _I, _P, _SZ], _I),
+    "h3_residual_quant_run": ([_P] * 12 + [_I64] * 4 + [_F, _I, _I, _I, _SZ], _I),
+    "h3_residual_quant_run_k": ([_P] * 12 + [_I64] * 5 + [_F, _I, _I, _I, _SZ], _I),
+    "h3_residual_quant_run_t": ([_P] * 12 + [_I64] * 6 + [_F, _I, _I, _I, _SZ], _I),
     "h3_convrot_register_abi": ([], _I),
     "h3_convrot_register_resources_size": ([], _SZ),
     "h3_convrot_register_error": ([_I], ct.c_char_p),

@@ -83,6 +83,56 @@ int h3_norm_quant_run_t(const void* x, const void* w, const void* shift, const v
                         uintptr_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Fused residual prologue: x = bf(fma(branch, bf(gate[rows]), x)) in place,  */
+/* then the prologue above on the updated rows                               */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces h3_residual_quant_abi (residual_quant.cu:254). Returns 1. */
+int h3_residual_quant_abi(void);
+/* Replaces h3_residual_quant_resources_size (residual_quant.cu:255); the report
+ * has the field order of H3NormQuantResources (residual_quant.cu:230-233). */
+size_t h3_residual_quant_resources_size(void);
+/* Replaces h3_residual_quant_error (residual_quant.cu:256): cudaGetErrorString. */
+const char* h3_residual_quant_error(int code);
+/* Replaces h3_residual_quant_query (residual_quant.cu:257-264) for K=5376;
+ * gate_dtype and table_dtype 0 = FP32, 1 = BF16. */
+int h3_residual_quant_query(int gate_dtype, int table_dtype, int debug, H3NormQuantResources* out,
+                            size_t bytes);
+/* K-generic query (no reference counterpart). */
+int h3_residual_quant_query_k(int64_t k, int gate_dtype, int table_dtype, int debug,
+                              H3NormQuantResources* out, size_t bytes);
+/*
+ * Replaces h3_residual_quant_run (residual_quant.cu:267-289), K fixed at 5376.
+ *   x      BF16 [m, K] contiguous, 8-byte aligned, updated in place:
+ *          x = bf(fma(branch, bf(gate[rows[i]]), x))
+ *   branch BF16 [m, K] contiguous, 8-byte aligned
+ *   gate   table [T, >= K] (row stride gs), gate_dtype 0 = FP32, 1 = BF16
+ *   w, shift, scale, rows, q, qscale, debug outputs, eps: as h3_norm_quant_run
+ *          (ss, cs row strides; table_dtype for shift/scale)
+ * Returns a cudaError_t (0 = success); nothing is launched on a failed check.
+ */
+int h3_residual_quant_run(void* x, const void* branch, const void* w, const void* gate,
+                          const void* shift, const void* scale, const void* rows, void* q, void* qscale,
+                          void* debug_norm, void* debug_rotated, void* debug_rstd, int64_t m, int64_t gs,
+                          int64_t ss, int64_t cs, float eps, int gate_dtype, int table_dtype, int debug,
+                          uintptr_t stream);
+/* Same contract with K explicit (K % 256 == 0, 256 <= K <= 16384); the
+ * reference fixes K at compile time (residual_quant.cu:16). */
+int h3_residual_quant_run_k(void* x, const void* branch, const void* w, const void* gate,
+                            const void* shift, const void* scale, const void* rows, void* q, void* qscale,
+                            void* debug_norm, void* debug_rotated, void* debug_rstd, int64_t m, int64_t k,
+                            int64_t gs, int64_t ss, int64_t cs, float eps, int gate_dtype, int table_dtype,
+                            int debug, uintptr_t stream);
+/* Same contract with the table count T stated (no reference counterpart), so
+ * that W and the shift/scale tables can be staged in shared memory; every entry
+ * of `rows` must lie in [0, T) (an out-of-range entry reads table T - 1). */
+int h3_residual_quant_run_t(void* x, const void* branch, const void* w, const void* gate,
+                            const void* shift, const void* scale, const void* rows, void* q, void* qscale,
+                            void* debug_norm, void* debug_rotated, void* debug_rstd, int64_t m, int64_t k,
+                            int64_t tables, int64_t gs, int64_t ss, int64_t cs, float eps, int gate_dtype,
+                            int table_dtype, int debug, uintptr_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* ConvRot256 + per-token INT8 quantiser                                    */
 /* ------------------------------------------------------------------------ */
 

@@ -15,6 +15,9 @@
        (K in {5376, 7168});
      * ``ref_kitchen.so``    oracle/ref_kitchen_launch.cu, which instantiates the
        vendored Kitchen quantiser of kernels/convrot/vendor/convrot64_exact.cuh.
+     * ``ref_residual_k{K}.so`` kernels/residual_quant/residual_quant.cu (the
+       reference's residual update fused with the prologue; K fixed the same way
+       as norm_quant.cu, rewritten the same way for K = 4096);
    The reference's INT8 GEMMs (kernels/gemm/fc1.cu, gate.cu) need the external
    CUTLASS library and are therefore not built; the GEMM oracle is the exact C
    restatement (int32 accumulation + IEEE epilogue, reproducible bit for bit).
@@ -35,6 +38,7 @@ REF_OUT = HERE / "_ref"
 REFERENCE = Path(os.environ.get("H3SK_REFERENCE", "/root/reference"))
 C_LIB = HERE / "libh3_oracle.so"
 NORM_WIDTHS = (2048, 4096, 5376)
+RESIDUAL_WIDTHS = (4096, 5376)
 REF_FLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "--expt-relaxed-constexpr", "--expt-extended-lambda",
              "--shared", "-Xcompiler=-fPIC", "-gencode=arch=compute_100a,code=sm_100a"]
 
@@ -96,6 +100,22 @@ def build_ref(force: bool = False) -> list[Path]:
             try:
                 _compile(nvcc, source, target, [norm_src.parent, norm_src.parent / "vendor"],
                          ["--use_fast_math"])
+            finally:
+                if k != 5376:
+                    source.unlink(missing_ok=True)
+        built.append(target)
+    res_src = kernels / "residual_quant" / "residual_quant.cu"
+    res_text = res_src.read_text()
+    if len(pattern.findall(res_text)) != 1:
+        raise RuntimeError("residual_quant.cu no longer has the single K constant this recipe rewrites")
+    for k in RESIDUAL_WIDTHS:
+        target = REF_OUT / f"ref_residual_k{k}.so"
+        if force or not _newer(target, res_src, Path(__file__)):
+            source = res_src if k == 5376 else gen / f"residual_quant_k{k}.cu"
+            if k != 5376:
+                source.write_text(pattern.sub(f"constexpr int K = {k},", res_text))
+            try:
+                _compile(nvcc, source, target, [res_src.parent, res_src.parent / "vendor"], ["--use_fast_math"])
             finally:
                 if k != 5376:
                     source.unlink(missing_ok=True)

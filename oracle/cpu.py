@@ -38,6 +38,7 @@ def lib():
             "h3o_gemm_s32": ([_P, _P, _I64, _I64, _I64, _P, ct.c_int], None),
             "h3o_dequant": ([_P, _P, _P, _P, _I64, _I64, ct.c_int, _P, _I64, ct.c_int], None),
             "h3o_gate": ([_P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _P, ct.c_int], None),
+            "h3o_residual_update": ([_P, _P, _P, ct.c_int, _I64, _P, _I64, _I64, ct.c_int], ct.c_int),
             "h3o_max_threads": ([], ct.c_int),
         }
         for name, (args, res) in sig.items():
@@ -105,6 +106,33 @@ def norm_quant(x, w, shift, scale, rows, eps, *, xs=None, rrms=None, debug=False
     if rc:
         raise ValueError("oracle norm_quant rejected its arguments")
     return (q, qs, dn, dr, drs) if debug else (q, qs)
+
+
+def residual_update(x, branch, gate, rows, *, threads=None) -> np.ndarray:
+    """x <- bf(fma(branch, bf(gate[rows]), x)) (residual_quant.cu:59-78) on a copy.
+
+    x, branch uint16 [m, k] (BF16 bits); gate [T, >=k] float32 or uint16."""
+    x = np.array(x, dtype=np.uint16, copy=True, order="C")
+    branch = _c(branch, np.uint16)
+    gate = np.ascontiguousarray(gate)
+    if gate.dtype not in (np.uint16, np.float32):
+        raise ValueError("gate table must be float32 or BF16 bits")
+    m, k = x.shape
+    rc = lib().h3o_residual_update(_ptr(x), _ptr(branch), _ptr(gate), 1 if gate.dtype == np.uint16 else 0,
+                                   gate.shape[1], _ptr(_c(rows, np.int32)), m, k,
+                                   threads_default() if threads is None else threads)
+    if rc:
+        raise ValueError("oracle residual_update rejected its arguments")
+    return x
+
+
+def residual_quant(x, branch, w, gate, shift, scale, rows, eps, *, rrms=None, debug=False, threads=None):
+    """Fused residual prologue, kernels/residual_quant/residual_quant.cu:59-224:
+    the residual update, then the prologue on the updated rows.  Returns
+    (x_new, q, qscale) or, with debug, (x_new, q, qscale, norm_bits, rotated, rstd)."""
+    x_new = residual_update(x, branch, gate, rows, threads=threads)
+    out = norm_quant(x_new, w, shift, scale, rows, eps, rrms=rrms, debug=debug, threads=threads)
+    return (x_new,) + tuple(out)
 
 
 def rms_variance(x_row) -> float:

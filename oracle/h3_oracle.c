@@ -216,6 +216,26 @@ H3O_EXPORT int h3o_norm_quant(const uint16_t* x, int64_t xs, const uint16_t* w, 
   return 0;
 }
 
+/* ---- residual update of the fused residual prologue ----------------------------
+ * residual_quant.cu:59-78: x[i] <- bf(fma(branch[i], bf(gate[rows[r]][i]), x[i]))
+ * (IEEE fused multiply-add, no flush), in place; the prologue (h3o_norm_quant)
+ * then runs on the updated rows.  gate_dtype 0 = FP32 table, 1 = BF16 bits.   */
+H3O_EXPORT int h3o_residual_update(uint16_t* x, const uint16_t* branch, const void* gate, int gate_dtype,
+                                   int64_t gs, const int32_t* rows, int64_t m, int64_t k, int threads) {
+  if (k < 1 || gs < k) return 1;
+  set_threads(threads);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const int64_t tr = rows[r];
+    for (int64_t i = 0; i < k; ++i) {
+      const float g = gate_dtype ? bf_to_f(((const uint16_t*)gate)[tr * gs + i])
+                                 : bf_round(((const float*)gate)[tr * gs + i]);
+      x[r * k + i] = f_to_bf(fmaf(bf_to_f(branch[r * k + i]), g, bf_to_f(x[r * k + i])));
+    }
+  }
+  return 0;
+}
+
 /* ---- ConvRot quantiser with input activation --------------------------------------
  * convrot64_exact.cuh:913-1027 (act none / GELU-tanh / SwiGLU) and
  * convrot_register_v2.cu:67-138 (act none).  x rows have stride xs elements;

@@ -92,3 +92,33 @@ def kitchen_quant(x, act=0):
     if rc:
         raise RuntimeError(f"reference Kitchen quantiser failed with CUDA error {rc}")
     return q, sc
+
+
+def residual_widths() -> list[int]:
+    return sorted(int(p.stem.split("_k")[1]) for p in REF.glob("ref_residual_k*.so"))
+
+
+def residual_quant(x, branch, w, gate, shift, scale, rows, eps, *, debug=False):
+    """Reference residual_quant_kernel (residual_quant.cu:134-224) at K = x.shape[1]:
+    x <- bf(fma(branch, bf(gate[rows]), x)) in place on a copy of ``x``, then the
+    prologue on the updated rows.  Returns (x_new, q, qs[, dn, dr, drs])."""
+    import torch
+    m, k = x.shape
+    so = _load(f"ref_residual_k{k}.so")
+    fn = so.h3_residual_quant_run
+    fn.argtypes = [ct.c_void_p] * 12 + [ct.c_int64] * 4 + [ct.c_float, ct.c_int, ct.c_int, ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    dev = x.device
+    xn = x.clone()
+    q = torch.empty((m, k), dtype=torch.int8, device=dev)
+    qs = torch.empty((m, 1), dtype=torch.float32, device=dev)
+    dn = torch.empty((m, k), dtype=torch.bfloat16, device=dev) if debug else None
+    dr = torch.empty((m, k), dtype=torch.float32, device=dev) if debug else None
+    drs = torch.empty((m,), dtype=torch.float32, device=dev) if debug else None
+    ptrs = [t.data_ptr() if t is not None else None
+            for t in (xn, branch, w, gate, shift, scale, rows, q, qs, dn, dr, drs)]
+    rc = fn(*ptrs, m, gate.stride(0), shift.stride(0), scale.stride(0), float(eps),
+            int(gate.dtype == torch.bfloat16), int(shift.dtype == torch.bfloat16), int(debug), _stream(x))
+    if rc:
+        raise RuntimeError(f"reference residual_quant failed with CUDA error {rc}")
+    return (xn, q, qs, dn, dr, drs) if debug else (xn, q, qs)

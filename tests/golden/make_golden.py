@@ -1,10 +1,13 @@
 """Generate the golden fixtures from the reference's own CUDA kernels.
 
 Run on a B200 box from the repository root after ``oracle/build.py`` has built
-``oracle/_ref`` (the reference's norm_quant.cu, convrot_register_v2.cu and the
-vendored Kitchen quantiser, compiled from the reference sources):
+``oracle/_ref`` (the reference's norm_quant.cu, residual_quant.cu,
+convrot_register_v2.cu and the vendored Kitchen quantiser, compiled from the
+reference sources):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [name-prefix ...]
+
+With prefixes, only the fixtures whose names start with one of them are written.
 
 Inputs are seeded CPU draws; every fixture stores the inputs (BF16 as uint16
 bits) and the reference kernel's outputs.  The CPU oracle is pinned against
@@ -67,17 +70,51 @@ def kitchen_case(name, k, m, act, seed):
                         scale=sc.cpu().numpy().reshape(-1))
 
 
-def main():
-    norm_case("norm_k4096_bf16", 4096, 8, 2, torch.bfloat16, 101)
-    norm_case("norm_k5376_f32", 5376, 6, 3, torch.float32, 102)
-    norm_case("norm_k2048_bf16", 2048, 8, 1, torch.bfloat16, 103)
-    convrot_case("convrot_k5376", 5376, 6, 104)
-    convrot_case("convrot_k7168", 7168, 4, 105)
-    kitchen_case("kitchen_k4096_none", 4096, 8, 0, 106)
-    kitchen_case("kitchen_k4096_gelu", 4096, 8, 1, 107)
-    kitchen_case("kitchen_k2048_swiglu", 2048, 8, 2, 108)
+def residual_case(name, k, m, tables, gate_dtype, table_dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((m, k), generator=g)
+    x[:, torch.randperm(k, generator=g)[:16]] *= 20.0
+    x = x.to(torch.bfloat16)
+    branch = (torch.randn((m, k), generator=g) * 2).to(torch.bfloat16)
+    w = (torch.rand((k,), generator=g) + 0.5).to(torch.bfloat16)
+    gate = (torch.randn((tables, k), generator=g) * 0.3).to(gate_dtype)
+    shift = (torch.randn((tables, k), generator=g) * 0.1).to(table_dtype)
+    scale = (torch.randn((tables, k), generator=g) * 0.1).to(table_dtype)
+    rows = torch.randint(0, tables, (m,), generator=g, dtype=torch.int32)
+    dev = torch.device("cuda")
+    xn, q, qs, dn, _, drs = ref_gpu.residual_quant(x.to(dev), branch.to(dev), w.to(dev), gate.to(dev), shift.to(dev),
+                                                   scale.to(dev), rows.to(dev), 1e-6, debug=True)
+    torch.cuda.synchronize()
+
+    def tab(t):
+        return bits(t) if t.dtype == torch.bfloat16 else t.numpy()
+
+    np.savez_compressed(HERE / f"{name}.npz", kind="residual_quant", k=k, eps=np.float32(1e-6), x=bits(x),
+                        branch=bits(branch), w=bits(w), gate=tab(gate), shift=tab(shift), scale=tab(scale),
+                        rows=rows.numpy(), x_new=bits(xn), q=q.cpu().numpy(), qscale=qs.cpu().numpy().reshape(-1),
+                        norm=bits(dn), rstd=drs.cpu().numpy())
+
+
+CASES = [
+    ("norm_k4096_bf16", lambda n: norm_case(n, 4096, 8, 2, torch.bfloat16, 101)),
+    ("norm_k5376_f32", lambda n: norm_case(n, 5376, 6, 3, torch.float32, 102)),
+    ("norm_k2048_bf16", lambda n: norm_case(n, 2048, 8, 1, torch.bfloat16, 103)),
+    ("convrot_k5376", lambda n: convrot_case(n, 5376, 6, 104)),
+    ("convrot_k7168", lambda n: convrot_case(n, 7168, 4, 105)),
+    ("kitchen_k4096_none", lambda n: kitchen_case(n, 4096, 8, 0, 106)),
+    ("kitchen_k4096_gelu", lambda n: kitchen_case(n, 4096, 8, 1, 107)),
+    ("kitchen_k2048_swiglu", lambda n: kitchen_case(n, 2048, 8, 2, 108)),
+    ("residual_k5376_bf16", lambda n: residual_case(n, 5376, 6, 2, torch.bfloat16, torch.bfloat16, 109)),
+    ("residual_k4096_f32", lambda n: residual_case(n, 4096, 8, 3, torch.float32, torch.float32, 110)),
+]
+
+
+def main(prefixes):
+    for name, make in CASES:
+        if not prefixes or any(name.startswith(p) for p in prefixes):
+            make(name)
     print("golden fixtures:", sorted(p.name for p in HERE.glob("*.npz")))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

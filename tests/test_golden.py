@@ -53,3 +53,16 @@ def test_oracle_quantiser_matches_reference_kernel(name):
     else:
         assert np.allclose(s, g["scale"], rtol=1e-6, atol=0)
     assert_codes_close(q, g["q"], 1e-3, name)
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c.startswith("residual_")])
+def test_oracle_residual_prologue_matches_reference_kernel(name):
+    """residual_quant.cu fixtures: the updated rows bit for bit, then the prologue
+    on them as above (rrms injected from the reference's hardware rsqrt)."""
+    g = load(name)
+    x_new, q, qs, norm, _, _ = ocpu.residual_quant(g["x"], g["branch"], g["w"], g["gate"], g["shift"], g["scale"],
+                                                   g["rows"], float(g["eps"]), rrms=g["rstd"], debug=True)
+    assert np.array_equal(x_new, g["x_new"]), "residual-updated rows"
+    assert np.array_equal(norm, g["norm"]), "normalised/modulated BF16 values"
+    assert np.array_equal(qs, g["qscale"]), "row scales"
+    assert_codes_close(q, g["q"], 1e-3, name)

@@ -47,3 +47,29 @@ def test_quantiser_reproduces_golden(device, name):
     torch.cuda.synchronize()
     assert np.array_equal(q.cpu().numpy(), g["q"])
     assert np.array_equal(s.cpu().numpy().reshape(-1), g["scale"])
+
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in GOLDEN.glob("residual_*.npz")))
+@pytest.mark.parametrize("debug", [False, True])
+def test_residual_prologue_reproduces_golden(device, name, debug):
+    from h3_speedkit.ops.residual_quant import ResidualQuant
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    x, branch, w = _tensor(g["x"], device), _tensor(g["branch"], device), _tensor(g["w"], device)
+    gate, shift, scale = _tensor(g["gate"], device), _tensor(g["shift"], device), _tensor(g["scale"], device)
+    rows = _tensor(g["rows"], device)
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=device)
+    qs = torch.empty((m, 1), dtype=torch.float32, device=device)
+    dbg = {}
+    if debug:
+        dbg = dict(debug_norm=torch.empty((m, k), dtype=torch.bfloat16, device=device),
+                   debug_rotated=torch.empty((m, k), dtype=torch.float32, device=device),
+                   debug_rstd=torch.empty((m,), dtype=torch.float32, device=device))
+    ResidualQuant().bind(x, branch, w, gate, shift, scale, rows, q, qs, eps=float(g["eps"]), **dbg)()
+    torch.cuda.synchronize()
+    assert np.array_equal(x.cpu().view(torch.int16).numpy().view(np.uint16), g["x_new"])
+    assert np.array_equal(q.cpu().numpy(), g["q"])
+    assert np.array_equal(qs.cpu().numpy().reshape(-1), g["qscale"])
+    if debug:
+        assert np.array_equal(dbg["debug_rstd"].cpu().numpy(), g["rstd"])
+        assert np.array_equal(dbg["debug_norm"].cpu().view(torch.int16).numpy().view(np.uint16), g["norm"])

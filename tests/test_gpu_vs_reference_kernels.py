@@ -1,7 +1,8 @@
 """Same-GPU speed of the row kernels against the reference's own kernels.
 
-The reference's prologue (norm_quant.cu), register ConvRot quantiser
-(convrot_register_v2.cu) and Kitchen quantiser (convrot64_exact.cuh), compiled
+The reference's prologue (norm_quant.cu), fused residual prologue
+(residual_quant.cu), register ConvRot quantiser (convrot_register_v2.cu) and
+Kitchen quantiser (convrot64_exact.cuh), compiled
 from their sources for sm_100a into oracle/_ref, run on the same B200 at the
 same shapes as this build's kernels.  Each case times both with CUDA events on
 the launching stream (3 warm-up launches, then the median of 3 runs of 10
@@ -150,4 +151,45 @@ def test_register_quantiser_faster_than_reference_kernel(device):
     torch.cuda.synchronize()
     assert torch.equal(q[0], q[1]) and torch.equal(sc[0], sc[1])
     _report(f"register ConvRot quantiser [{m},{k}]", nbytes, t_ours, t_ref)
+    assert t_ours < t_ref
+
+
+@pytest.mark.parametrize("m,k", [(98304, 4096), (65536, 5376)])
+def test_residual_prologue_faster_than_reference_kernel(device, m, k):
+    if f"ref_residual_k{k}.so" not in [p.name for p in ref_gpu.REF.glob("ref_residual_k*.so")]:
+        pytest.skip(f"reference residual prologue for K={k} not built")
+    lib = _lib.load()
+    ref = _ref_fn(f"ref_residual_k{k}.so", "h3_residual_quant_run", [ct.c_void_p] * 12 + [ct.c_int64] * 4 +
+                  [ct.c_float, ct.c_int, ct.c_int, ct.c_int, ct.c_size_t])
+    # x and branch read, x written back, codes + scale written
+    nbytes = 3 * m * k * 2 + m * k + m * 4 + m * 4 + 4 * k * 2
+    g = torch.Generator().manual_seed(m + k)
+    x0 = (torch.randn((m, k), generator=g) * 2).to(torch.bfloat16).to(device)
+    branch = (torch.randn((m, k), generator=g) * 0.1).to(torch.bfloat16).to(device)
+    w = (torch.rand((k,), generator=g) + 0.5).to(torch.bfloat16).to(device)
+    gate = (torch.randn((1, k), generator=g) * 0.01).to(torch.bfloat16).to(device)
+    shift = (torch.randn((1, k), generator=g) * 0.1).to(torch.bfloat16).to(device)
+    scale = (torch.randn((1, k), generator=g) * 0.1).to(torch.bfloat16).to(device)
+    rows = torch.zeros((m,), dtype=torch.int32, device=device)
+    xs = [x0.clone(), x0.clone()]
+    q = [torch.empty((m, k), dtype=torch.int8, device=device) for _ in range(2)]
+    qs = [torch.empty((m, 1), dtype=torch.float32, device=device) for _ in range(2)]
+    st = torch.cuda.current_stream().cuda_stream
+
+    def ours(i):
+        assert lib.h3_residual_quant_run_t(xs[0].data_ptr(), branch.data_ptr(), w.data_ptr(), gate.data_ptr(),
+                                           shift.data_ptr(), scale.data_ptr(), rows.data_ptr(), q[0].data_ptr(),
+                                           qs[0].data_ptr(), None, None, None, m, k, 1, k, k, k, ct.c_float(1e-6),
+                                           1, 1, 0, st) == 0
+
+    def theirs(i):
+        assert ref(xs[1].data_ptr(), branch.data_ptr(), w.data_ptr(), gate.data_ptr(), shift.data_ptr(),
+                   scale.data_ptr(), rows.data_ptr(), q[1].data_ptr(), qs[1].data_ptr(), None, None, None, m, k, k, k,
+                   1e-6, 1, 1, 0, st) == 0
+
+    # x is updated in place by every launch: both kernels see the same sequence
+    t_ours, t_ref = _time_ms(ours, 1), _time_ms(theirs, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(xs[0], xs[1]) and torch.equal(q[0], q[1]) and torch.equal(qs[0], qs[1])
+    _report(f"residual prologue [{m},{k}]", nbytes, t_ours, t_ref)
     assert t_ours < t_ref

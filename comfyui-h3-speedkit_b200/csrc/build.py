@@ -1,7 +1,7 @@
 """Build the sm_100a kernel library in-tree and write its manifest.
 
 Output: ``h3_speedkit/_native/libh3sk_b200.so`` plus one symlink per library
-name the reference loads (``norm.so``, ``convrot.so``, ``fc1.so``, ``gate.so``)
+name the reference loads (``norm.so``, ``residual.so``, ``convrot.so``, ``fc1.so``, ``gate.so``)
 and ``build.json`` in the reference's manifest schema
 (tools/build_kernels.py:41-63 of H3 SpeedKit: schema, kernels[name].sha256 ...).
 
@@ -26,7 +26,7 @@ PKG = CSRC.parent
 NATIVE = PKG / "h3_speedkit" / "_native"
 BUILD = PKG / "_build"
 LIB_NAME = "libh3sk_b200.so"
-ALIASES = ("norm", "convrot", "fc1", "gate")
+ALIASES = ("norm", "residual", "convrot", "fc1", "gate")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-std=c++17", "-O3", "-DNDEBUG", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
           "--expt-relaxed-constexpr"]
@@ -87,8 +87,8 @@ def build(nvcc: str | None = None, force: bool = False, quiet: bool = True) -> P
         raise RuntimeError(f"link failed:\n{result.stderr[-4000:]}")
     os.replace(tmp, lib)
     digest = sha256(lib)
-    sources = {"norm": "norm_quant.cu", "convrot": "convrot_quant.cu", "fc1": "int8_gemm.cu",
-               "gate": "int8_gemm.cu"}
+    sources = {"norm": "norm_quant.cu", "residual": "norm_quant.cu", "convrot": "convrot_quant.cu",
+               "fc1": "int8_gemm.cu", "gate": "int8_gemm.cu"}
     for name in ALIASES:
         alias = NATIVE / (name + ".so")
         if alias.is_symlink() or alias.exists():

@@ -36,7 +36,7 @@ def test_manifest_and_aliases():
     native = _lib.NATIVE
     manifest = json.loads((native / "build.json").read_text())
     assert manifest["schema"] == 1
-    for name in ("norm", "convrot", "fc1", "gate"):
+    for name in ("norm", "residual", "convrot", "fc1", "gate"):
         alias = native / f"{name}.so"
         assert alias.exists() and alias.resolve() == (native / _lib.LIB_NAME).resolve()
         assert manifest["kernels"][name]["sha256"]
@@ -47,6 +47,7 @@ def test_abi_versions_and_resource_sizes():
     assert lib.h3_norm_quant_abi() == 1 and lib.h3_norm_quant_abi_ex() == 2
     assert lib.h3_convrot_register_abi() == 1
     assert lib.h3_norm_quant_resources_size() == 13 * 8
+    assert lib.h3_residual_quant_abi() == 1 and lib.h3_residual_quant_resources_size() == 13 * 8
     assert lib.h3_convrot_register_resources_size() == 14 * 8
     assert b"sm_100a" in lib.h3sk_version()
     assert lib.h3_norm_quant_error(INVALID)

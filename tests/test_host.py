@@ -231,3 +231,34 @@ def test_block_geometry_from_weight_shapes():
     b.out = b.out[:, :512]
     with pytest.raises(ValueError):
         geometry(b)
+
+
+def test_residual_validate_rejects_before_gpu_work():
+    """ops.residual_quant.validate: the reference's metadata checks (residual_quant.py:57-112) on CPU."""
+    from h3_speedkit.ops import residual_quant as rq
+    m, k = 4, 512
+    x = torch.zeros((m, k), dtype=torch.bfloat16)
+    branch = torch.zeros_like(x)
+    w = torch.ones((k,), dtype=torch.bfloat16)
+    gate = torch.zeros((2, k))
+    shift = torch.zeros((2, k), dtype=torch.bfloat16)
+    scale = torch.zeros_like(shift)
+    rows = torch.zeros((m,), dtype=torch.int32)
+    q = torch.empty((m, k), dtype=torch.int8)
+    qs = torch.empty((m, 1))
+    ok = dict(eps=1e-6, require_cuda=False)
+    rq.validate(x, branch, w, gate, shift, scale, rows, q, qs, **ok)
+    with pytest.raises(ValueError, match="overlaps"):
+        rq.validate(x, x, w, gate, shift, scale, rows, q, qs, **ok)
+    with pytest.raises(ValueError, match="Branch requires"):
+        rq.validate(x, branch[:, :256], w, gate, shift, scale, rows, q, qs, **ok)
+    with pytest.raises(ValueError, match="Gate requires"):
+        rq.validate(x, branch, w, gate[:1], shift, scale, rows, q, qs, **ok)
+    with pytest.raises(ValueError, match="Rows outside"):
+        rq.validate(x, branch, w, gate, shift, scale, rows + 2, q, qs, **ok)
+    with pytest.raises(ValueError, match="Nonfinite"):
+        bad = branch.clone()
+        bad[1, 3] = float("inf")
+        rq.validate(x, bad, w, gate, shift, scale, rows, q, qs, **ok)
+    with pytest.raises(ValueError, match="Epsilon"):
+        rq.validate(x, branch, w, gate, shift, scale, rows, q, qs, eps=0.0, require_cuda=False)

@@ -126,6 +126,8 @@ class Backend:
         return q, qs
 
     def gate_projection(self, linear, q, qs, x, gate, rows, skip=0):
+        if skip >= len(x):
+            return
         w, ws = self.plain_weight(linear, x)
         g = gate.to(dtype=torch.bfloat16).contiguous()
         operands = (q[skip:], w, qs[skip:], ws, x[skip:], g, rows[skip:], x[skip:])
@@ -151,15 +153,35 @@ class Backend:
         self.gate_projection(block.attn.out_proj, aq, asc, x, gate_msa, rows, skip)
         qi, qs = self.normalize(block.norm2, x, shift_mlp, scale_mlp, rows)
         w1, ws1 = self.plain_weight(block.mlp.fc1, x)
+        # FC1 only for the rows past the window; the rows below it stay zero
+        # (runtime.py:149-157)
+        hidden = torch.empty((len(x), w1.shape[0]), device=x.device, dtype=torch.bfloat16)
+        if skip:
+            hidden[:skip].zero_()
+        if skip < len(x):
+            int8_linear(qi[skip:], w1, qs[skip:], ws1, gelu=mlp_act != "swiglu", out=hidden[skip:])
         if mlp_act == "swiglu":
-            hidden = int8_linear(qi, w1, qs, ws1)
             fq, fs = quantize_int8_rowwise_convrot64(hidden, 256, input_act="swiglu")
         else:
-            hidden = int8_linear(qi, w1, qs, ws1, gelu=True)
             fq, fs = quantize_int8_rowwise_convrot64(hidden)
         self.gate_projection(block.mlp.fc2, fq, fs, x, gate_mlp, rows, skip)
         counts.update(qkv=1, attention=1, norm_quant=2, fc1=1, gate=2)
+        if skip:
+            counts.update(last_block_window=1)
         return x
+
+
+def last_block_window(payload, tokens: int) -> int:
+    """The last block's row window (runtime.py:205-215): the first target
+    (video/audio) token rounded down to 128, when the prepared layout holds two
+    contiguous target spans that end the sequence; 0 (every row) otherwise."""
+    layout = payload.get("layout") if isinstance(payload, dict) else None
+    if layout is None or getattr(layout, "seq_len", None) != tokens:
+        return 0
+    targets = [(a, b) for a, b, kind in layout.segments if kind in ("video", "audio")]
+    if len(targets) != 2 or targets[-1][1] != tokens or targets[0][1] != targets[1][0]:
+        return 0
+    return min(a for a, _ in targets) // 128 * 128
 
 
 class ModelPatch:
@@ -187,8 +209,10 @@ class ModelPatch:
         if self.attention is None:
             raise Unsupported("No attention provider for the B200 linear path")
         tokens = int(x.shape[-2]) if x.ndim >= 2 else 0
-        return {"skip": 0, "rows": None, "row_key": None, "counts": Counter(), "tokens": tokens,
-                "shape_key": (tokens, 0), "verify": self.verified_shapes[(tokens, 0)] < 8 and self.verify_new_shapes}
+        skip = last_block_window(kwargs.get("minimax_payload") or (args[4] if len(args) > 4 else None), tokens)
+        key = (tokens, skip)
+        return {"skip": skip, "rows": None, "row_key": None, "counts": Counter(), "tokens": tokens,
+                "shape_key": key, "verify": self.verified_shapes[key] < 8 and self.verify_new_shapes}
 
     def wrapper(self, executor, *args, **kwargs):
         with self.lock:
@@ -227,10 +251,13 @@ class ModelPatch:
                 frame["row_key"] = key
             work = x.clone() if frame["verify"] else x
             reference = extra["original_block"](inputs)["img"] if frame["verify"] else None
+            last = index == self.blocks - 1
             output = self.backend.block(self.model.blocks[index], work, inputs["t_emb"], segments,
-                                        inputs.get("rope_freqs"), rows=frame["rows"], skip=0,
+                                        inputs.get("rope_freqs"), rows=frame["rows"],
+                                        skip=frame["skip"] if last else 0,
                                         counts=frame["counts"], attention=self.attention)
-            if reference is not None and not torch.equal(output, reference):
+            start = frame["skip"] if last else 0   # the final layer reads rows [skip, M) only
+            if reference is not None and not torch.equal(output[start:], reference[start:]):
                 self.rejected_shapes.add(frame["shape_key"])
                 frame["verification_failed"] = index
                 frame["fallback"] = "Exact layout verification failed at block " + str(index)

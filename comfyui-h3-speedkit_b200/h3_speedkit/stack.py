@@ -32,7 +32,7 @@ from .synthetic import BlockWeights
 
 ACT_NONE, ACT_SWIGLU = 0, 2
 EPI_DEQUANT, EPI_GELU = 0, 1
-LAUNCHES_PER_BLOCK = 8   # 2 prologues, 2 quantisers, 4 GEMMs
+LAUNCHES_PER_BLOCK = 8   # 2 prologues, 2 quantisers, 4 GEMMs (no row window)
 GEMM_NAMES = ("qkv", "outproj", "fc1", "fc2")
 
 
@@ -162,14 +162,20 @@ def geometry(weights: BlockWeights) -> dict:
 
 
 class BlockPlan:
-    """One block's eight launches, bound to fixed buffers.
+    """One block's launches, bound to fixed buffers.
 
     ``x`` is updated in place.  ``rows`` maps each token to a row of the adaLN /
-    gate tables.  Nothing is allocated when the plan runs.
+    gate tables.  ``skip`` is the reference's last-block row window
+    (runtime.py:117-160, applied to block 49 only, runtime.py:296): rows
+    [0, skip) keep their residual -- no outproj, FC1 or FC2 work for them --
+    while QKV still covers every row (attention reads all keys and values).
+    With identity attention the V quantiser and the second prologue also start
+    at ``skip``: their rows below it feed nothing.  Nothing is allocated when
+    the plan runs.
     """
 
     def __init__(self, weights: BlockWeights, x: torch.Tensor, rows: torch.Tensor, ws: Workspace,
-                 eps: float = 1e-6):
+                 eps: float = 1e-6, skip: int = 0):
         self.lib = _lib.load()
         m, d = x.shape
         g = geometry(weights)
@@ -178,35 +184,50 @@ class BlockPlan:
             raise ValueError("block weights do not match the activation width")
         if m < 1:
             raise ValueError("empty shard")
+        if not 0 <= skip <= m:
+            raise ValueError("row window outside the shard")
         if ws.qkv.shape[1] != 3 * attn or ws.h.shape[1] != n1 or ws.hq.shape[1] != ffn or ws.aq.shape[1] != attn:
             raise ValueError("workspace does not match the block geometry")
         self.keep = (weights, x, rows, ws)   # owners of every pointer below
-        lib, P = self.lib, lambda t: t.data_ptr()
+        self.skip = skip
+        lib = self.lib
         w = weights
         tdt = int(w.shift_msa.dtype == torch.bfloat16)
         fc1_epi, mlp_act = (EPI_DEQUANT, ACT_SWIGLU) if g["swiglu"] else (EPI_GELU, ACT_NONE)
-        self.calls = [
+        s, n = skip, m - skip   # the window: rows [s, m)
+
+        def P(t, row=0):
+            """Address of row `row` of a 2-D tensor (or element `row` of a 1-D one)."""
+            return t.data_ptr() + row * t.stride(0) * t.element_size()
+
+        calls = [
             ("prologue", lib.h3_norm_quant_run_t,
              (P(x), P(w.norm1), P(w.shift_msa), P(w.scale_msa), P(rows), P(ws.q), P(ws.qs), None, None, None,
               m, d, w.shift_msa.shape[0], x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps),
               tdt, 0)),
             ("qkv", lib.h3_int8_ex,
              (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * attn, d, 3 * attn, EPI_DEQUANT)),
-            ("quant_v", lib.h3_convrot_quant_act,
-             (P(ws.qkv) + 2 * attn * 2, 3 * attn, P(ws.aq), P(ws.as_), m, attn, ACT_NONE)),
-            ("outproj", lib.h3_int8_gate,
-             (P(ws.aq), P(w.out), P(ws.as_), P(w.out_s), P(x), P(w.gate_msa), P(rows), P(x), m, d, attn, 13)),
-            ("prologue", lib.h3_norm_quant_run_t,
-             (P(x), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows), P(ws.q), P(ws.qs), None, None, None,
-              m, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0), w.scale_mlp.stride(0), float(eps),
-              tdt, 0)),
-            ("fc1", lib.h3_int8_ex,
-             (P(ws.q), P(w.fc1), P(ws.qs), P(w.fc1_s), None, P(ws.h), m, n1, d, n1, fc1_epi)),
-            ("quant_h", lib.h3_convrot_quant_act,
-             (P(ws.h), n1, P(ws.hq), P(ws.hs), m, ffn, mlp_act)),
-            ("fc2", lib.h3_int8_gate,
-             (P(ws.hq), P(w.fc2), P(ws.hs), P(w.fc2_s), P(x), P(w.gate_mlp), P(rows), P(x), m, d, ffn, 13)),
         ]
+        if n:
+            calls += [
+                ("quant_v", lib.h3_convrot_quant_act,
+                 (P(ws.qkv, s) + 2 * attn * 2, 3 * attn, P(ws.aq, s), P(ws.as_, s), n, attn, ACT_NONE)),
+                ("outproj", lib.h3_int8_gate,
+                 (P(ws.aq, s), P(w.out), P(ws.as_, s), P(w.out_s), P(x, s), P(w.gate_msa), P(rows, s), P(x, s), n, d,
+                  attn, 13)),
+                ("prologue", lib.h3_norm_quant_run_t,
+                 (P(x, s), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows, s), P(ws.q, s), P(ws.qs, s), None,
+                  None, None, n, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0),
+                  w.scale_mlp.stride(0), float(eps), tdt, 0)),
+                ("fc1", lib.h3_int8_ex,
+                 (P(ws.q, s), P(w.fc1), P(ws.qs, s), P(w.fc1_s), None, P(ws.h, s), n, n1, d, n1, fc1_epi)),
+                ("quant_h", lib.h3_convrot_quant_act,
+                 (P(ws.h, s), n1, P(ws.hq, s), P(ws.hs, s), n, ffn, mlp_act)),
+                ("fc2", lib.h3_int8_gate,
+                 (P(ws.hq, s), P(w.fc2), P(ws.hs, s), P(w.fc2_s), P(x, s), P(w.gate_mlp), P(rows, s), P(x, s), n, d,
+                  ffn, 13)),
+            ]
+        self.calls = calls
 
     def launch(self, stream: int, events=None) -> None:
         """Enqueue the eight launches on `stream`.  With `events` (a dict of
@@ -242,18 +263,21 @@ class LocalStack:
     """All blocks over one contiguous shard of tokens, on the current device."""
 
     def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6,
-                 ws: Workspace | None = None):
+                 ws: Workspace | None = None, skip: int = 0):
+        """``skip``: the last block's row window (rows [0, skip) of this shard keep
+        the residual the previous blocks left; see BlockPlan)."""
         m, d = x.shape
         self.x, self.rows = x, rows
         if ws is not None and ws.q.shape[0] < m:
             raise ValueError("shared workspace too small for this shard")
         self.ws = ws if ws is not None else Workspace.for_block(m, blocks[0], x.device)
-        self.plans = [BlockPlan(b, x, rows, self.ws, eps) for b in blocks]
+        self.plans = [BlockPlan(b, x, rows, self.ws, eps, skip=skip if i == len(blocks) - 1 else 0)
+                      for i, b in enumerate(blocks)]
         self.graph = None
 
     @property
     def launches_per_step(self) -> int:
-        return LAUNCHES_PER_BLOCK * len(self.plans)
+        return sum(len(plan.calls) for plan in self.plans)
 
     def run(self, events=None) -> torch.Tensor:
         if self.graph is not None and events is None:
@@ -287,7 +311,10 @@ class ShardedStack:
     """
 
     def __init__(self, blocks, rows_shard: torch.Tensor, total_rows: int, d: int, device, group=None,
-                 eps: float = 1e-6, dtype=torch.bfloat16):
+                 eps: float = 1e-6, dtype=torch.bfloat16, skip: int = 0):
+        """``skip``: the last block's row window as a global row index (the first
+        target token rounded down to 128 in the reference, runtime.py:207); each
+        rank applies the part that falls in its shard."""
         import torch.distributed as dist
         self.dist, self.group = dist, group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -301,7 +328,10 @@ class ShardedStack:
         self.send = torch.zeros((self.per, d), dtype=dtype, device=device)
         self.out = torch.empty((self.per * self.world, d), dtype=dtype, device=device)
         self.x = self.send[: self.rows_local]
-        self.local = LocalStack(blocks, self.x, rows_shard, eps) if self.rows_local else None
+        if not 0 <= skip <= total_rows:
+            raise ValueError("row window outside the token range")
+        self.skip_local = min(max(skip - self.start, 0), self.rows_local)
+        self.local = LocalStack(blocks, self.x, rows_shard, eps, skip=self.skip_local) if self.rows_local else None
         self._blocks, self._rows, self._eps = blocks, rows_shard, eps
 
     @property
@@ -345,7 +375,9 @@ class ShardedStack:
         for c0, c1 in bounds:
             hi = min(c1, self.rows_local)
             if self.local is not None and hi > c0:
-                stacks.append(LocalStack(self._blocks, self.x[c0:hi], self._rows[c0:hi], self._eps, ws=ws))
+                window = min(max(self.skip_local - c0, 0), hi - c0)
+                stacks.append(LocalStack(self._blocks, self.x[c0:hi], self._rows[c0:hi], self._eps, ws=ws,
+                                         skip=window))
             else:
                 stacks.append(None)
         plan = (bounds, stacks, torch.cuda.Stream(self.send.device), torch.cuda.Stream(self.send.device))

@@ -48,14 +48,24 @@ class NpBlock:
         return cls(**{k: conv(v) for k, v in bw.__dict__.items()})
 
 
-def block(x: np.ndarray, b: NpBlock, rows: np.ndarray, eps: float = 1e-6, threads=None) -> np.ndarray:
+def block(x: np.ndarray, b: NpBlock, rows: np.ndarray, eps: float = 1e-6, threads=None, skip: int = 0) -> np.ndarray:
     """One block on BF16 rows x (uint16 [M, D]); returns the updated rows.
+
+    ``skip``: the reference's row window (runtime.py:117-160): rows [0, skip)
+    get no outproj/FC1/FC2 update and keep their residual.  Every op is
+    row-local and attention is the identity here, so the window is the block on
+    rows [skip, M) with the rows below copied through.
 
     The geometry comes from the weights: attention width A = qkv rows / 3 (V is
     columns [2A, 3A) of the QKV output), FFN width F = fc2 columns; an FC1 with
     2F rows is a SwiGLU MLP ([gate | up] halves, the activation applied by the
     FC2-input quantiser, convrot64_exact.cuh:928-937 and runtime.py:159), an FC1
     with F rows the GELU-epilogue MLP."""
+    if skip:
+        out = np.array(x, copy=True)
+        if skip < x.shape[0]:
+            out[skip:] = block(np.ascontiguousarray(x[skip:]), b, np.ascontiguousarray(rows[skip:]), eps, threads)
+        return out
     attn = b.qkv.shape[0] // 3
     ffn = b.fc2.shape[1]
     swiglu = b.fc1.shape[0] == 2 * ffn
@@ -75,7 +85,9 @@ def block(x: np.ndarray, b: NpBlock, rows: np.ndarray, eps: float = 1e-6, thread
                               threads=threads)
 
 
-def stack(x: np.ndarray, blocks: list[NpBlock], rows: np.ndarray, eps: float = 1e-6, threads=None) -> np.ndarray:
-    for b in blocks:
-        x = block(x, b, rows, eps, threads)
+def stack(x: np.ndarray, blocks: list[NpBlock], rows: np.ndarray, eps: float = 1e-6, threads=None,
+          skip: int = 0) -> np.ndarray:
+    """All blocks; ``skip`` is the last block's row window (runtime.py:296)."""
+    for i, b in enumerate(blocks):
+        x = block(x, b, rows, eps, threads, skip=skip if i == len(blocks) - 1 else 0)
     return x

@@ -142,3 +142,91 @@ def test_h3_geometry_swiglu_block_matches_cpu_restatement(device):
     LocalStack([b], part, rows[100:].to(device).contiguous()).run()
     torch.cuda.synchronize()
     assert torch.equal(part, whole[100:])
+
+
+@pytest.mark.parametrize("skip", [0, 128, 640, 1000])
+def test_last_block_row_window(device, skip):
+    """The reference's last-block window (runtime.py:117-160, 296): rows >= skip
+    equal the full stack's rows bit for bit, rows < skip equal the output of all
+    blocks but the last (outproj and FC2 leave them alone)."""
+    m = 1000
+    blocks = _blocks(3, device)
+    x0 = synthetic.cfg5_tokens(m, D).to(device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    full, head, win = x0.clone(), x0.clone(), x0.clone()
+    LocalStack(blocks, full, rows).run()
+    LocalStack(blocks[:-1], head, rows).run()
+    stack = LocalStack(blocks, win, rows, skip=skip)
+    stack.run()
+    torch.cuda.synchronize()
+    assert torch.equal(win[skip:], full[skip:])
+    assert torch.equal(win[:skip], head[:skip])
+    assert stack.launches_per_step == 8 * 3 - (6 if skip == m else 0)
+
+
+def test_last_block_row_window_matches_cpu_restatement(device):
+    m, skip = 384, 128
+    blocks = _blocks(2, device)
+    x0 = synthetic.cfg5_tokens(m, D)
+    rows = (torch.arange(m) % 2).to(torch.int32)
+    x = x0.to(device)
+    LocalStack(blocks, x, rows.to(device), skip=skip).run()
+    torch.cuda.synchronize()
+    ref = chain.stack(bf16_bits(x0), [chain.NpBlock.from_torch(b) for b in blocks], rows.numpy(), skip=skip)
+    got = bf16_bits(x)
+    assert float((got == ref).mean()) > 0.99
+    # the window's untouched rows went through the first block only: the same rows
+    # of a one-block run, bit for bit
+    one = x0.to(device)
+    LocalStack(blocks[:1], one, rows.to(device)).run()
+    torch.cuda.synchronize()
+    assert np.array_equal(got[:skip], bf16_bits(one)[:skip])
+
+
+@pytest.mark.parametrize("chunks", [None, 3])
+def test_row_window_through_sharded_and_chunked_paths(device, chunks):
+    """A global skip through ShardedStack (device forward and the chunked
+    end-to-end path, whose chunks cut the window) equals LocalStack with it."""
+    m, skip = 9000, 2560
+    blocks = _blocks(2, device)
+    x0 = synthetic.cfg5_tokens(m, D)
+    rows = torch.zeros((m,), dtype=torch.int32, device=device)
+    ref = x0.to(device)
+    LocalStack(blocks, ref, rows, skip=skip).run()
+    stack = ShardedStack(blocks, rows, m, D, device, skip=skip)
+    stack.load(x0.to(device))
+    got = stack.forward().clone()
+    host_out = torch.empty((m, D), dtype=torch.bfloat16).pin_memory()
+    stack2 = ShardedStack(blocks, rows, m, D, device, skip=skip)
+    stack2.forward_host(x0.pin_memory(), host_out, chunks=chunks)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    assert torch.equal(host_out, ref.cpu())
+
+
+@pytest.mark.parametrize("skip", [0, 256])
+def test_runtime_backend_block_matches_the_block_plan(device, skip):
+    """runtime.Backend.block (the reference-facing Python path: NormQuant, the
+    GEMM C-ABI, the Kitchen-style quantiser) gives the same rows as the bound
+    BlockPlan, with and without the last-block window."""
+    from types import SimpleNamespace as NS
+    from h3_speedkit.runtime import Backend
+    m = 768
+    bw = _blocks(1, device)[0]
+
+    def linear(w, s):
+        return NS(weight=w, weight_int8=w, weight_scale=s)
+
+    block = NS(adaln_proj=lambda t: (bw.shift_msa, bw.scale_msa, bw.gate_msa, bw.shift_mlp, bw.scale_mlp,
+                                     bw.gate_mlp),
+               norm1=NS(weight=bw.norm1, eps=1e-6), norm2=NS(weight=bw.norm2, eps=1e-6),
+               attn=NS(qkv_proj=linear(bw.qkv, bw.qkv_s), out_proj=linear(bw.out, bw.out_s)),
+               mlp=NS(fc1=linear(bw.fc1, bw.fc1_s), fc2=linear(bw.fc2, bw.fc2_s)))
+    x0 = synthetic.cfg5_tokens(m, D).to(device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    via_runtime = x0.clone()
+    Backend().block(block, via_runtime, None, None, rows=rows, skip=skip)
+    via_plan = x0.clone()
+    LocalStack([bw], via_plan, rows, skip=skip).run()
+    torch.cuda.synchronize()
+    assert torch.equal(via_runtime, via_plan)

@@ -262,3 +262,16 @@ def test_residual_validate_rejects_before_gpu_work():
         rq.validate(x, bad, w, gate, shift, scale, rows, q, qs, **ok)
     with pytest.raises(ValueError, match="Epsilon"):
         rq.validate(x, branch, w, gate, shift, scale, rows, q, qs, eps=0.0, require_cuda=False)
+
+
+def test_last_block_window_from_the_prepared_layout():
+    """runtime.py:205-215: the first target token rounded down to 128 when two
+    contiguous target spans end the sequence; 0 otherwise."""
+    lay = SimpleNamespace(seq_len=5000, segments=[(0, 700, "text"), (700, 4000, "video"), (4000, 5000, "audio")])
+    assert runtime.last_block_window({"layout": lay}, 5000) == 640
+    assert runtime.last_block_window({"layout": lay}, 4999) == 0          # layout of another sequence
+    assert runtime.last_block_window(None, 5000) == 0
+    gap = SimpleNamespace(seq_len=5000, segments=[(0, 700, "text"), (700, 3900, "video"), (4000, 5000, "audio")])
+    assert runtime.last_block_window({"layout": gap}, 5000) == 0          # spans not contiguous
+    one = SimpleNamespace(seq_len=5000, segments=[(0, 700, "text"), (700, 5000, "video")])
+    assert runtime.last_block_window({"layout": one}, 5000) == 0          # the reference needs two spans

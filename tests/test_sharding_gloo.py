@@ -102,3 +102,16 @@ def test_chunk_schedule_covers_the_shard_with_small_end_chunks():
             tail = sizes[sizes.index(max(sizes)):]
             for prev, nxt in zip(tail, tail[1:]):
                 assert nxt >= down * prev - 128
+
+
+def test_oracle_row_window_is_the_block_on_the_window():
+    """chain.block(skip=s): rows < s copied through, rows >= s the block on them alone."""
+    from oracle import chain
+    m, skip = 40, 16
+    b = chain.NpBlock.from_torch(synthetic.cfg5_block(0, 256, 512, tables=2))
+    x = np.ascontiguousarray(synthetic.cfg5_tokens(m, 256).view(torch.int16).numpy().view(np.uint16))
+    rows = (np.arange(m) % 2).astype(np.int32)
+    full = chain.block(x, b, rows, threads=1)
+    win = chain.block(x, b, rows, threads=1, skip=skip)
+    assert np.array_equal(win[:skip], x[:skip])
+    assert np.array_equal(win[skip:], full[skip:])

@@ -230,3 +230,66 @@ def test_runtime_backend_block_matches_the_block_plan(device, skip):
     LocalStack([bw], via_plan, rows, skip=skip).run()
     torch.cuda.synchronize()
     assert torch.equal(via_runtime, via_plan)
+
+
+def _reference_kernel_chain(x, blocks, rows, eps=1e-6):
+    """The block chain with every row kernel replaced by the reference's own
+    (norm_quant.cu, the Kitchen quantiser, compiled into oracle/_ref) and the
+    GEMMs by this build's (int32 accumulation and IEEE epilogue, pinned exact by
+    tests/test_gpu_gemm.py).  x is updated in place."""
+    from h3_speedkit.ops import gemm
+    from oracle import ref_gpu
+    for b in blocks:
+        attn = b.qkv.shape[0] // 3
+        q, qs = ref_gpu.norm_quant(x, b.norm1, b.shift_msa, b.scale_msa, rows, eps)
+        qkv = gemm.int8_linear(q, b.qkv, qs.view(-1), b.qkv_s)
+        aq, as_ = ref_gpu.kitchen_quant(qkv[:, 2 * attn:].contiguous(), 0)
+        del qkv
+        gemm.int8_gate_residual(aq, b.out, as_, b.out_s, x, b.gate_msa, rows)
+        q, qs = ref_gpu.norm_quant(x, b.norm2, b.shift_mlp, b.scale_mlp, rows, eps)
+        h = gemm.int8_linear(q, b.fc1, qs.view(-1), b.fc1_s, gelu=True)
+        hq, hs = ref_gpu.kitchen_quant(h, 0)
+        del h
+        gemm.int8_gate_residual(hq, b.fc2, hs, b.fc2_s, x, b.gate_mlp, rows)
+    return x
+
+
+def test_cfg5_full_size_against_reference_kernels(device):
+    """The benchmark workload itself (8 blocks, D=4096, FFN=16384, M=98304, the
+    bench's device-drawn weights and tokens):
+      * every one of the 98304 output rows equals, bit for bit, the same chain
+        built from the reference's own row kernels;
+      * 24 sampled rows of the full run equal the same rows run on their own
+        (row locality at full size, the basis of token sharding);
+      * those rows match the CPU restatement of the 8-block chain within a
+        tolerance: its two documented departures (rsqrt in double, IEEE instead
+        of fast division) flip rare codes, and the flips compound over blocks
+        (measured: 92 % of the values bit-identical, deviation < 1 %)."""
+    d, ffn, m, n_blocks = 4096, 16384, 98304, 8
+    blocks = [synthetic.cfg5_block(i, d, ffn, device=device) for i in range(n_blocks)]
+    x0 = synthetic.cfg5_tokens(m, d, device=device)
+    rows = torch.zeros((m,), dtype=torch.int32, device=device)
+    full = x0.clone()
+    LocalStack(blocks, full, rows).run()
+    torch.cuda.synchronize()
+    assert _lib.pipeline_status() == 0
+    ref = _reference_kernel_chain(x0.clone(), blocks, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(full, ref)
+    del ref
+    g = torch.Generator().manual_seed(55)
+    idx = torch.sort(torch.randperm(m, generator=g)[:24]).values.to(device)
+    alone = x0[idx].contiguous()
+    LocalStack(blocks, alone, rows[:24].contiguous()).run()
+    torch.cuda.synchronize()
+    got = full[idx]
+    assert torch.equal(got, alone)
+    cpu = chain.stack(bf16_bits(x0[idx]), [chain.NpBlock.from_torch(b) for b in blocks], np.zeros(24, np.int32))
+    got_bits = bf16_bits(got)
+    same = float((got_bits == cpu).mean())
+    a = torch.from_numpy(got_bits.view(np.int16)).view(torch.bfloat16).float()
+    b = torch.from_numpy(cpu.view(np.int16)).view(torch.bfloat16).float()
+    err = ((a - b).abs().max() / b.abs().max()).item()
+    print(f"\ncfg5 full size, 24 sampled rows: {same:.5f} bit-identical to the CPU chain, max deviation {err:.2e}")
+    assert same > 0.85, f"only {same:.4f} of the sampled outputs are bit-identical"
+    assert err < 2e-2, f"largest deviation {err:.2e} of the output magnitude"

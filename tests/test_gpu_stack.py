@@ -241,17 +241,42 @@ def _reference_kernel_chain(x, blocks, rows, eps=1e-6):
     from oracle import ref_gpu
     for b in blocks:
         attn = b.qkv.shape[0] // 3
+        swiglu = b.fc1.shape[0] == 2 * b.fc2.shape[1]
         q, qs = ref_gpu.norm_quant(x, b.norm1, b.shift_msa, b.scale_msa, rows, eps)
         qkv = gemm.int8_linear(q, b.qkv, qs.view(-1), b.qkv_s)
-        aq, as_ = ref_gpu.kitchen_quant(qkv[:, 2 * attn:].contiguous(), 0)
+        v = qkv[:, 2 * attn:].contiguous()
         del qkv
+        if attn in (5376, 7168):   # the reference's register quantiser (runtime.py:144-146)
+            aq, as_, _ = ref_gpu.convrot_register(v, 0)
+            as_ = as_.view(-1)
+        else:
+            aq, as_ = ref_gpu.kitchen_quant(v, 0)
         gemm.int8_gate_residual(aq, b.out, as_, b.out_s, x, b.gate_msa, rows)
         q, qs = ref_gpu.norm_quant(x, b.norm2, b.shift_mlp, b.scale_mlp, rows, eps)
-        h = gemm.int8_linear(q, b.fc1, qs.view(-1), b.fc1_s, gelu=True)
-        hq, hs = ref_gpu.kitchen_quant(h, 0)
+        h = gemm.int8_linear(q, b.fc1, qs.view(-1), b.fc1_s, gelu=not swiglu)
+        hq, hs = ref_gpu.kitchen_quant(h, 2 if swiglu else 0)
         del h
         gemm.int8_gate_residual(hq, b.fc2, hs, b.fc2_s, x, b.gate_mlp, rows)
     return x
+
+
+def test_h3_geometry_stack_against_reference_kernels(device):
+    """The H3 model geometry (D=5376, attention 7168, SwiGLU FFN 14336, two
+    adaLN table rows): two blocks on 8192 tokens equal, bit for bit, the chain
+    built from the reference's own row kernels (its K=5376 prologue, register
+    ConvRot quantiser for the 7168-wide attention output, Kitchen SwiGLU
+    quantiser) and the pinned GEMMs."""
+    g = synthetic.H3_GEOMETRY
+    m = 8192
+    blocks = [synthetic.cfg5_block(i, g["d"], g["ffn"], tables=2, device=device, attn=g["attn"], swiglu=True)
+              for i in range(2)]
+    x0 = synthetic.cfg5_tokens(m, g["d"], device=device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    ours = x0.clone()
+    LocalStack(blocks, ours, rows).run()
+    ref = _reference_kernel_chain(x0.clone(), blocks, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(ours, ref)
 
 
 def test_cfg5_full_size_against_reference_kernels(device):

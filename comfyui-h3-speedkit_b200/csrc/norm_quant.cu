@@ -32,6 +32,7 @@ namespace {
 constexpr int kMaxK = 16384;
 constexpr int kNormK = 5376;        // K of the unsuffixed (reference) entry point
 constexpr int kModBatch = 2;        // chunks per modulation round of the streaming prologue
+constexpr int kResBatch = 2;        // chunks per round of the residual pass (staged form; 1 otherwise)
 
 __host__ __device__ constexpr int norm_threads(int k) {
   return ((k / 64 + 31) / 32) * 32 < 64 ? 64 : ((k / 64 + 31) / 32) * 32;
@@ -368,12 +369,29 @@ __global__ void __launch_bounds__(512, 1) norm_quant_stream(
       const int gate_row = kStaged ? min(max(__ldg(Rows + row), 0), tables - 1) : __ldg(Rows + row);
       const GateT* grow = Gate + int64_t(gate_row) * gs;
       if (ok) {
-        for (int c = tt; c < nchunks16; c += team_threads) {
-          const uint32_t off = rs::swz128(16u * uint32_t(c));
-          const uint4 nv = residual8(rs::lds128(row_a + boff + off), table8<GateT>(grow + 8 * c, g_vec16),
-                                     rs::lds128(row_a + off));
-          rs::sts128(row_a + off, nv.x, nv.y, nv.z, nv.w);
-          *reinterpret_cast<uint4*>(XOut + row * K + 8 * c) = nv;
+        // kB chunks per round, every load of a round before its math: the gate
+        // loads go to L1/L2 and would otherwise stall one at a time.
+        constexpr int kB = kStaged ? kResBatch : 1;   // wider rounds spill in the modulation-pass form
+        for (int c0 = tt; c0 < nchunks16; c0 += kB * team_threads) {
+          uint4 gv[kB], xv[kB], bv[kB];
+#pragma unroll
+          for (int u = 0; u < kB; ++u) {
+            const int c = c0 + u * team_threads;
+            if (c < nchunks16) {
+              const uint32_t off = rs::swz128(16u * uint32_t(c));
+              gv[u] = table8<GateT>(grow + 8 * c, g_vec16);
+              xv[u] = rs::lds128(row_a + off);
+              bv[u] = rs::lds128(row_a + boff + off);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kB; ++u) {
+            const int c = c0 + u * team_threads;
+            if (c >= nchunks16) continue;
+            const uint4 nv = residual8(bv[u], gv[u], xv[u]);
+            rs::sts128(row_a + rs::swz128(16u * uint32_t(c)), nv.x, nv.y, nv.z, nv.w);
+            *reinterpret_cast<uint4*>(XOut + row * K + 8 * c) = nv;
+          }
         }
       }
       if (!rs::team_sync_and(bar_id, team_threads, ok)) break;   // barrier R

@@ -32,7 +32,6 @@ from .synthetic import BlockWeights
 
 ACT_NONE, ACT_SWIGLU = 0, 2
 EPI_DEQUANT, EPI_GELU = 0, 1
-LAUNCHES_PER_BLOCK = 8   # 2 prologues, 2 quantisers, 4 GEMMs (no row window)
 GEMM_NAMES = ("qkv", "outproj", "fc1", "fc2")
 
 

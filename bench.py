@@ -14,7 +14,9 @@ BF16 [98304, 4096] output.  A step = one pass of the 8-block stack over all
 Rank 0 prints one JSON line.  `value` is device-timed tokens/s (inputs resident
 in HBM, CUDA events on the compute stream, max over ranks); `e2e` is the same
 metric through the public API with the step's input copied from pinned host
-memory and the gathered output read back inside the timed region.  The
+memory and the whole [M, D] output read back to host memory inside the timed
+region (N>1: every rank writes its rows into one node-shared pinned buffer;
+`e2e.output` says which form ran).  The
 per-kernel roofline comes from CUDA events around every launch of the timed
 region.  `--impl reference` times the CPU restatement of the path (oracle/) on
 the host cores: the reference has no CPU implementation of its own.
@@ -222,7 +224,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from h3_speedkit import _lib, synthetic
-    from h3_speedkit.stack import ShardedStack, shard_bounds
+    from h3_speedkit.stack import ShardedStack, shard_bounds, shared_host_output
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -306,24 +308,34 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         host_in = x_src.cpu().pin_memory()
-        host_out = torch.empty((args.tokens, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
-        stack.forward_host(host_in, host_out)   # untimed: builds the chunk plans and copy streams
+        # N>1: one node-shared pinned output that every rank fills over its own PCIe
+        # link; without room for it, rank 0 receives the gathered rows
+        host_out = shared_host_output(args.tokens, D) if world > 1 else None
+        shared = host_out is not None
+        if not shared:
+            host_out = torch.empty((args.tokens, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
+            out_desc = ("rank 0 pinned host buffer after the per-chunk NCCL all-gather" if world > 1
+                        else "pinned host buffer")
+        else:
+            out_desc = "node-shared pinned host buffer [M, D]; every rank copies its own rows (no device gather)"
+        stack.forward_host(host_in, host_out, shared_out=shared)   # untimed: builds the chunk plans and streams
         barrier()
         torch.cuda.synchronize()
         e_start = torch.cuda.Event(enable_timing=True)
         e_end = torch.cuda.Event(enable_timing=True)
         e_start.record(stream)
         for _ in range(args.steps):
-            # public API: H2D of the input chunks, the block stack, the per-chunk
-            # gather and rank 0's D2H, with the copies overlapping the compute
-            stack.forward_host(host_in, host_out)
+            # public API: H2D of the input chunks, the block stack and the D2H of
+            # the output rows (per rank into the shared buffer, or the per-chunk
+            # gather and rank 0's D2H), the copies overlapping the compute
+            stack.forward_host(host_in, host_out, shared_out=shared)
         e_end.record(stream)
         torch.cuda.synchronize()
         barrier()
         e_elapsed = max_over_ranks(e_start.elapsed_time(e_end) / 1e3)
         e2e = {"value": args.tokens * args.steps / e_elapsed, "unit": "tokens/s",
                "h2d_bytes_per_step": args.tokens * D * 2, "d2h_bytes_per_step": args.tokens * D * 2,
-               "ms_per_step": e_elapsed * 1e3 / args.steps}
+               "ms_per_step": e_elapsed * 1e3 / args.steps, "output": out_desc}
 
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------
     cpu = None

@@ -104,6 +104,70 @@ def chunk_schedule(per: int, world: int, unit: int = 128, min_rows: int = 1024) 
     return bounds
 
 
+def shared_host_output(rows: int, d: int, dtype=torch.bfloat16, group=None,
+                       directory: str = "/dev/shm") -> torch.Tensor | None:
+    """A pinned host tensor [rows, d] that every rank of ``group`` (one node)
+    maps: a POSIX shared-memory file under ``directory``, mapped MAP_SHARED in
+    each process and page-locked there with cudaHostRegister, so that every
+    rank's device-to-host copies land in the one buffer over the rank's own PCIe
+    link (``ShardedStack.forward_host(..., shared_out=True)``).  The file is
+    unlinked once every rank has mapped it.  Returns None on every rank when the
+    file system lacks the room or a process cannot page-lock the mapping."""
+    import os
+    import uuid
+
+    import torch.distributed as dist
+    multi = dist.is_initialized() and dist.get_world_size(group) > 1
+    rank = dist.get_rank(group) if multi else 0
+    nbytes = rows * d * torch.empty((), dtype=dtype).element_size()
+    path = ""
+    if rank == 0:
+        try:
+            st = os.statvfs(directory)
+            if st.f_bavail * st.f_frsize >= nbytes + (64 << 20):
+                path = os.path.join(directory, f"h3sk_out_{os.getpid()}_{uuid.uuid4().hex[:12]}")
+        except OSError:
+            path = ""
+    if multi:
+        box = [path]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        path = box[0]
+    if not path:
+        return None
+    base = None
+    ok = 1
+    try:
+        if rank == 0:
+            base = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+        if multi:
+            dist.barrier(group=group)
+        if rank != 0:
+            base = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+        rc = torch.cuda.cudart().cudaHostRegister(base.data_ptr(), nbytes, 0)
+        if int(rc) != 0:
+            torch.cuda.cudart().cudaGetLastError()   # clear the failed call's error state
+            ok = 0
+    except (OSError, RuntimeError):
+        ok = 0
+    if multi:
+        flag = torch.tensor([ok], dtype=torch.int32, device=torch.cuda.current_device())
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        all_ok = bool(flag.item())
+        dist.barrier(group=group)
+    else:
+        all_ok = bool(ok)
+    if rank == 0:
+        try:
+            os.unlink(path)
+        except OSError:
+            pass
+    if not all_ok:
+        if ok and base is not None:
+            torch.cuda.cudart().cudaHostUnregister(base.data_ptr())
+        return None
+    return base.view(dtype).view(rows, d)
+
+
 def gather_shards(send: torch.Tensor, out: torch.Tensor, total: int, group=None) -> torch.Tensor:
     """Assemble the token-sharded output: every rank contributes its padded shard
     ``send`` [ceil(total/world), D]; ``out`` [world * ceil(total/world), D]
@@ -355,17 +419,18 @@ class ShardedStack:
         return self.gather()
 
     # ---- end to end from pinned host memory, copies overlapped with compute -------
-    def _chunking(self, chunks: int | None):
+    def _chunking(self, chunks: int | None, schedule_world: int | None = None):
         """Chunk boundaries over the padded shard (identical on every rank, so every
         rank issues the same collectives) and one LocalStack per chunk sharing one
         workspace sized for the largest chunk.  ``chunks=None`` takes
         ``chunk_schedule`` (small end chunks, ramped tail); an int gives that many
         equal chunks."""
-        key = ("chunks", chunks)
+        schedule_world = self.world if schedule_world is None else schedule_world
+        key = ("chunks", chunks, schedule_world)
         cached = getattr(self, "_chunk_cache", None)
         if cached is not None and cached[0] == key:
             return cached[1]
-        bounds = chunk_schedule(self.per, self.world) if chunks is None else uniform_chunks(self.per, chunks)
+        bounds = chunk_schedule(self.per, schedule_world) if chunks is None else uniform_chunks(self.per, chunks)
         step = max(c1 - c0 for c0, c1 in bounds)
         stacks = []
         ws = None
@@ -384,18 +449,26 @@ class ShardedStack:
         return plan
 
     def forward_host(self, host_in: torch.Tensor, host_out: torch.Tensor | None = None,
-                     chunks: int | None = None) -> None:
+                     chunks: int | None = None, *, shared_out: bool = False) -> None:
         """One end-to-end step from pinned host memory: this rank's input rows are
         copied in chunk by chunk on a copy stream while the block stack runs on the
-        chunks already resident (every op is row-local), each chunk is gathered
-        across ranks as soon as it is done, and rank 0 (or the only rank) copies
-        finished rows to ``host_out`` on a second copy stream.  Everything is
-        ordered on the current stream: when it reaches the end of this call's work,
-        the output is in ``host_out``."""
+        chunks already resident (every op is row-local).  Then either
+          * (default) each chunk is gathered across ranks as soon as it is done and
+            rank 0 (or the only rank) copies the gathered rows to ``host_out`` on a
+            second copy stream, or
+          * (``shared_out``: ``host_out`` is a node-shared pinned buffer of all
+            [total, D] rows, see ``shared_host_output``) every rank copies its own
+            finished rows into it over its own PCIe link -- no device gather; the
+            output is complete when every rank has reached the end of this call.
+        Everything is ordered on the current stream: when it reaches the end of
+        this call's work, this rank's part of the output is in ``host_out``."""
         import torch.distributed as dist
         if host_in.shape != self.x.shape:
             raise ValueError(f"expected input shard {tuple(self.x.shape)}, got {tuple(host_in.shape)}")
-        bounds, stacks, h2d, d2h = self._chunking(chunks)
+        if shared_out and (host_out is None or host_out.shape[0] < self.total):
+            raise ValueError("shared_out needs the node-shared [total, D] output buffer")
+        # with every rank copying out its own rows, the copy-out share is one rank's
+        bounds, stacks, h2d, d2h = self._chunking(chunks, schedule_world=1 if shared_out else self.world)
         comp = torch.cuda.current_stream(self.send.device)
         start = torch.cuda.Event()
         start.record(comp)
@@ -410,7 +483,7 @@ class ShardedStack:
                 ev = torch.cuda.Event()
                 ev.record(h2d)
                 arrived.append(ev)
-        multi = dist.is_initialized() and self.world > 1
+        multi = dist.is_initialized() and self.world > 1 and not shared_out
         for (c0, c1), stack, ev in zip(bounds, stacks, arrived):
             comp.wait_event(ev)
             if stack is not None:
@@ -430,8 +503,9 @@ class ShardedStack:
             with torch.cuda.stream(d2h):
                 if not multi:
                     hi = min(c1, self.rows_local)
+                    base = self.start if shared_out else 0
                     if hi > c0:
-                        host_out[c0:hi].copy_(self.x[c0:hi], non_blocking=True)
+                        host_out[base + c0:base + hi].copy_(self.x[c0:hi], non_blocking=True)
                 else:
                     for r in range(self.world):
                         g0, g1 = r * self.per + c0, min(self.total, r * self.per + c1)

@@ -2,8 +2,9 @@
 
 Skipped unless the box shows at least two GPUs.  Rank r owns the contiguous
 token block shard_bounds(M, 2, r); the gathered output of the device-resident
-forward and of the chunk-pipelined end-to-end forward (pinned host in, rank 0
-host out) must equal one GPU running every row, bit for bit.
+forward, of the chunk-pipelined end-to-end forward (pinned host in, rank 0
+host out) and of the same with a node-shared pinned output that every rank
+fills with its own rows must equal one GPU running every row, bit for bit.
 """
 import os
 import socket
@@ -49,11 +50,20 @@ def _worker(rank, world, port, m, result_path, chunks=3):
         for _ in range(2):
             stack.forward_host(host_in, host_out, chunks=chunks)
         torch.cuda.synchronize()
+        # node-shared pinned output: every rank writes its own rows, no gather
+        from h3_speedkit.stack import shared_host_output
+        shared = shared_host_output(m, D)
+        assert shared is not None
+        for _ in range(2):
+            stack.forward_host(host_in, shared, chunks=chunks, shared_out=True)
+        torch.cuda.synchronize()
+        dist.barrier()
         if rank == 0:
             ref = x_all.to(dev)
             LocalStack(blocks, ref, torch.zeros((m,), dtype=torch.int32, device=dev)).run()
             torch.cuda.synchronize()
-            ok = torch.equal(gathered, ref.cpu()) and torch.equal(host_out, ref.cpu())
+            ok = (torch.equal(gathered, ref.cpu()) and torch.equal(host_out, ref.cpu())
+                  and torch.equal(shared, ref.cpu()))
             Path(result_path).write_text("ok" if ok else "mismatch")
         dist.barrier()
     finally:

@@ -318,3 +318,23 @@ def test_cfg5_full_size_against_reference_kernels(device):
     print(f"\ncfg5 full size, 24 sampled rows: {same:.5f} bit-identical to the CPU chain, max deviation {err:.2e}")
     assert same > 0.85, f"only {same:.4f} of the sampled outputs are bit-identical"
     assert err < 2e-2, f"largest deviation {err:.2e} of the output magnitude"
+
+
+def test_shared_host_output_single_process(device):
+    """shared_host_output on one rank: a page-locked [M, D] mapping of a
+    shared-memory file; forward_host(shared_out=True) fills it with the rows."""
+    from h3_speedkit.stack import shared_host_output
+    m = 3000
+    blocks = _blocks(2, device)
+    x0 = synthetic.cfg5_tokens(m, D)
+    rows = torch.zeros((m,), dtype=torch.int32, device=device)
+    ref = x0.to(device)
+    LocalStack(blocks, ref, rows).run()
+    out = shared_host_output(m, D)
+    assert out is not None and out.shape == (m, D) and out.dtype == torch.bfloat16
+    stack = ShardedStack(blocks, rows, m, D, device)
+    stack.forward_host(x0.pin_memory(), out, shared_out=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref.cpu())
+    with pytest.raises(ValueError, match="shared_out"):
+        stack.forward_host(x0.pin_memory(), None, shared_out=True)

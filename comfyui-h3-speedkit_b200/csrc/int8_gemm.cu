@@ -14,9 +14,16 @@
 //               fused epilogue (bias, GELU, gate-residual, raw int32) and store.
 //               The second accumulator lets the epilogue of tile t overlap the
 //               mainloop of tile t+1.
-// Tiles are visited in grouped raster order (16 M-tiles per group) so that a
-// wave of CTAs shares B tiles in L2.  Every mbarrier wait is bounded; a wait that
-// runs out stops the CTA cleanly and records a status code (see
+// Tiles are visited weight-stationary: in groups of `group_n` N-tiles, whose
+// slice of B (group_n x 256 rows x K bytes, at most kBSliceBytes) stays in L2
+// while the group sweeps every M-tile, N-tile fastest.  A is then read from
+// DRAM once per N-group (once when all of B fits), B about once; a wave of
+// CTAs shares each A tile in L2.  Slices of 32 MB measured best (DRAM reads at
+// M=98304: QKV 1.05 GB, FC1 1.37 GB, FC2 8.0 GB); 64 MB slices do not stay
+// resident (FC1 7.1 GB).  Grouping 16 M-tiles with M fastest, the earlier
+// order, re-read B once per group and, at K = 16384, thrashed A (FC2 15.5 GB
+// for 2.5 GB of operands); the DRAM power that costs lowers the capped clock.  Every mbarrier wait is bounded; a wait
+// that runs out stops the CTA cleanly and records a status code (see
 // h3sk_pipeline_status).
 //
 // Epilogue arithmetic (non-fast-math TU, explicit round-to-nearest intrinsics):
@@ -57,7 +64,7 @@ constexpr int kEpilogueWarps = 8;    // two per TMEM lane quarter, one per colum
 constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
-constexpr int kGroupM = 16;
+constexpr int64_t kBSliceBytes = 32ll << 20;   // B bytes an N-group keeps in L2 (measured best)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
 enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
@@ -112,20 +119,21 @@ struct GemmParams {
   int64_t ldr;
   int m, n, k;
   int m_tiles, n_tiles, k_blocks, tiles;
+  int group_n;                    // N-tiles per weight-stationary group
   int* status;
   uint64_t timeout_ns;
 };
 
 __device__ int g_pipeline_status = 0;
 
-__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
-  const int per_group = kGroupM * n_tiles;
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int group_n, int& mt, int& nt) {
+  const int per_group = group_n * m_tiles;
   const int group = tile / per_group;
-  const int first_m = group * kGroupM;
-  const int gm = min(kGroupM, m_tiles - first_m);
+  const int first_n = group * group_n;
+  const int gn = min(group_n, n_tiles - first_n);
   const int local = tile - group * per_group;
-  mt = first_m + local % gm;
-  nt = local / gm;
+  mt = local / gn;
+  nt = first_n + local % gn;
 }
 
 // GELU-tanh, 0.5 v (1 + tanh(u)) with u = 0.7978845608028654 (v + 0.044715 v^3)
@@ -318,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = unit; ok && tile < p.tiles; tile += units) {
       int mt, nt;
-      tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      tile_coords(tile, p.m_tiles, p.n_tiles, p.group_n, mt, nt);
       const int a_row = mt * S::tile_m + int(rank) * kBM;
       const int b_row = nt * kBN + int(rank) * S::b_rows;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -437,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int tile = unit; tile < p.tiles; tile += units) {
       int mt, nt;
-      tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      tile_coords(tile, p.m_tiles, p.n_tiles, p.group_n, mt, nt);
       const int n0 = nt * kBN;
       // Stage this tile's per-column scales (and bias) in shared memory.
       epilogue_sync();   // the previous tile's readers are done
@@ -748,6 +756,11 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.tiles = p.m_tiles * p.n_tiles;
+  {
+    const int64_t slice = int64_t(kBN) * K;   // B bytes of one N-tile
+    const int64_t g = kBSliceBytes / (slice > 0 ? slice : 1);
+    p.group_n = int(g < 1 ? 1 : (g > p.n_tiles ? p.n_tiles : g));
+  }
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
   if (pair) {

@@ -134,23 +134,30 @@ def shared_host_output(rows: int, d: int, dtype=torch.bfloat16, group=None,
         path = box[0]
     if not path:
         return None
-    base = None
-    ok = 1
-    try:
-        if rank == 0:
-            base = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
-        if multi:
-            dist.barrier(group=group)
-        if rank != 0:
-            base = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
-        rc = torch.cuda.cudart().cudaHostRegister(base.data_ptr(), nbytes, 0)
-        if int(rc) != 0:
-            torch.cuda.cudart().cudaGetLastError()   # clear the failed call's error state
-            ok = 0
-    except (OSError, RuntimeError):
-        ok = 0
+    def mapping():
+        try:
+            return torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+        except Exception:   # e.g. no room in the file system
+            return None
+
+    # every rank takes the same collective steps on every path
+    base = mapping() if rank == 0 else None
     if multi:
-        flag = torch.tensor([ok], dtype=torch.int32, device=torch.cuda.current_device())
+        dist.barrier(group=group)   # the file exists (or rank 0 failed) before the others map it
+    if rank != 0:
+        base = mapping()
+    ok = 0
+    if base is not None:
+        try:
+            rc = torch.cuda.cudart().cudaHostRegister(base.data_ptr(), nbytes, 0)
+            ok = 1 if int(rc) == 0 else 0
+            if not ok:
+                torch.cuda.cudart().cudaGetLastError()   # clear the failed call's error state
+        except Exception:   # no CUDA runtime: the buffer cannot be page-locked
+            ok = 0
+    if multi:
+        on_gpu = dist.get_backend(group) == "nccl"
+        flag = torch.tensor([ok], dtype=torch.int32, device=torch.cuda.current_device() if on_gpu else "cpu")
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
         all_ok = bool(flag.item())
         dist.barrier(group=group)

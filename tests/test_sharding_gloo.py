@@ -115,3 +115,42 @@ def test_oracle_row_window_is_the_block_on_the_window():
     win = chain.block(x, b, rows, threads=1, skip=skip)
     assert np.array_equal(win[:skip], x[:skip])
     assert np.array_equal(win[skip:], full[skip:])
+
+
+def _shared_worker(rank, world, port, directory, result_dir):
+    import os as _os
+    _os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from h3_speedkit.stack import shared_host_output
+        out = shared_host_output(16, 32, group=None, directory=directory)
+        # on a host without a CUDA device the mapping cannot be page-locked: every
+        # rank agrees on None, and the file is gone
+        with open(f"{result_dir}/r{rank}", "w") as fh:
+            fh.write("none" if out is None else "tensor")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shared_host_output_agrees_across_ranks_without_a_gpu(tmp_path):
+    """shared_host_output on CPU ranks: every rank takes the same collective steps,
+    all return None when page-locking is impossible, and the shared file is removed."""
+    if torch.cuda.is_available():
+        pytest.skip("checks the fallback of a host without a CUDA device")
+    shm = tmp_path / "shm"
+    shm.mkdir()
+    mp.spawn(_shared_worker, args=(2, _free_port(), str(shm), str(tmp_path)), nprocs=2, join=True)
+    assert (tmp_path / "r0").read_text() == "none" and (tmp_path / "r1").read_text() == "none"
+    assert list(shm.iterdir()) == []
+
+
+def test_shared_host_output_without_room_returns_none(tmp_path, monkeypatch):
+    import os
+    from h3_speedkit.stack import shared_host_output
+
+    class Full:
+        f_bavail, f_frsize = 1, 4096
+    monkeypatch.setattr(os, "statvfs", lambda path: Full())
+    assert shared_host_output(1024, 1024, directory=str(tmp_path)) is None
+    assert list(tmp_path.iterdir()) == []

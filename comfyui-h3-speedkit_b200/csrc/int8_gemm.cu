@@ -64,6 +64,8 @@ constexpr int kEpilogueWarps = 8;    // two per TMEM lane quarter, one per colum
 constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
+constexpr int kDualMinK = 8192;     // K from which the dual (two N-tiles per unit) form is used
+constexpr int kDualMinWaves = 8;    // ... when its units fill at least this many waves of pairs
 constexpr int64_t kBSliceBytes = 32ll << 20;   // B bytes an N-group keeps in L2 (measured best)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
@@ -76,25 +78,30 @@ enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
 //   128 accumulator rows; the leader issues M=256 N=256 MMAs over both CTAs'
 //   shared memory, so every B byte crosses L2 -> SM once per 256 rows instead of
 //   once per 128.
-template <bool kPair>
+//   dual (CTA pair, long K): each work unit is two N-tiles of one M-tile; a
+//   stage holds the A tile and both B halves (48 KB, 4 stages), the leader
+//   issues the A stage against both and accumulates into both TMEM
+//   accumulators, so A is written into shared memory once per two tiles.
+template <bool kPair, bool kDual = false>
 struct Shape {
   static constexpr int pair = kPair ? 2 : 1;
+  static constexpr int dual_n = kDual ? 2 : 1;             // N-tiles per work unit
   static constexpr int tile_m = kBM * pair;               // rows per (pair) tile
   static constexpr int b_rows = kPair ? kBN / 2 : kBN;    // B rows loaded per CTA
   static constexpr int b_tile_bytes = b_rows * kBK;
-  static constexpr int stage_bytes = kATileBytes + b_tile_bytes;
-  static constexpr int stages = kPair ? 6 : 4;
+  static constexpr int stage_bytes = kATileBytes + dual_n * b_tile_bytes;
+  static constexpr int stages = kPair ? (kDual ? 4 : 6) : 4;
   static constexpr uint32_t idesc = idesc_i8(kBM * pair, kBN);
   static constexpr uint32_t tempty_count = kPair ? 2 * kEpilogueWarps : kEpilogueWarps;
 };
 
-template <bool kPair>
+template <bool kPair, bool kDual = false>
 struct SmemLayout {
-  using S = Shape<kPair>;
+  using S = Shape<kPair, kDual>;
   // offsets from the 1024-aligned base
   static constexpr int a = 0;
-  static constexpr int b = S::stages * kATileBytes;
-  static constexpr int bars = b + S::stages * S::b_tile_bytes;  // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int b = S::stages * kATileBytes;                 // stage s: dual_n B tiles
+  static constexpr int bars = b + S::stages * S::dual_n * S::b_tile_bytes;  // full[S], empty[S], tfull[2], tempty[2], drain
   static constexpr int nbars = 2 * S::stages + 5;
   static constexpr int misc = (bars + nbars * 8 + 15) / 16 * 16;  // tmem slot, abort flag, ready flag
   static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float (16-byte aligned)
@@ -105,6 +112,7 @@ struct SmemLayout {
 };
 static_assert(SmemLayout<true>::dynamic_bytes <= 227 * 1024, "pair layout exceeds shared memory");
 static_assert(SmemLayout<false>::dynamic_bytes <= 227 * 1024, "single layout exceeds shared memory");
+static_assert(SmemLayout<true, true>::dynamic_bytes <= 227 * 1024, "dual layout exceeds shared memory");
 
 struct GemmParams {
   const float* xs;
@@ -119,7 +127,9 @@ struct GemmParams {
   int64_t ldr;
   int m, n, k;
   int m_tiles, n_tiles, k_blocks, tiles;
-  int group_n;                    // N-tiles per weight-stationary group
+  int n_units;                    // work units along N (n_tiles / dual_n)
+  int work;                       // m_tiles * n_units
+  int group_n;                    // N units per weight-stationary group
   int* status;
   uint64_t timeout_ns;
 };
@@ -249,12 +259,12 @@ __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t
 // kPair: clusters of two CTAs share one 256 x 256 tile (see Shape); the leader
 // (rank 0) issues the MMAs, both CTAs produce their operand halves and run the
 // epilogue of their 128 accumulator rows.
-template <int kEpi, bool kPair>
+template <int kEpi, bool kPair, bool kDual = false>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
-  using S = Shape<kPair>;
-  using L = SmemLayout<kPair>;
+  using S = Shape<kPair, kDual>;
+  using L = SmemLayout<kPair, kDual>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem + L::a;
@@ -324,24 +334,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = unit; ok && tile < p.tiles; tile += units) {
-      int mt, nt;
-      tile_coords(tile, p.m_tiles, p.n_tiles, p.group_n, mt, nt);
+    for (int w = unit; ok && w < p.work; w += units) {
+      int mt, nu;
+      tile_coords(w, p.m_tiles, p.n_units, p.group_n, mt, nu);
       const int a_row = mt * S::tile_m + int(rank) * kBM;
-      const int b_row = nt * kBN + int(rank) * S::b_rows;
+      const int b_row = nu * S::dual_n * kBN + int(rank) * S::b_rows;   // B rows of the unit's first tile
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         int got = 0;
         if (lane == 0) {
           got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, status, 11, p.timeout_ns) ? 1 : 0;
           if (got) {
             uint8_t* da = smem_a + stage * kATileBytes;
-            uint8_t* db = smem_b + stage * S::b_tile_bytes;
+            uint8_t* db = smem_b + stage * S::dual_n * S::b_tile_bytes;
             if constexpr (kPair) {
               // The leader's full barrier counts both CTAs' bytes; only the leader arms it.
               if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::stage_bytes);
               const uint32_t bar = full_leader + uint32_t(stage) * 8u;
               tma_load_2d_pair(da, &map_a, bar, kb * kBK, a_row, policy_a);
-              tma_load_2d_pair(db, &map_b, bar, kb * kBK, b_row, policy_b);
+#pragma unroll
+              for (int j = 0; j < S::dual_n; ++j)
+                tma_load_2d_pair(db + j * S::b_tile_bytes, &map_b, bar, kb * kBK, b_row + j * kBN, policy_b);
             } else {
               mbar_arrive_expect_tx(&full[stage], S::stage_bytes);
               tma_load_2d(da, &map_a, &full[stage], kb * kBK, a_row, policy_a);
@@ -376,10 +388,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = unit; ok && tile < p.tiles; tile += units) {
+      for (int w = unit; ok && w < p.work; w += units) {
+        // the unit's accumulators: acc (one tile) or both (dual)
         int got = 0;
         if (lane == 0) {
           got = mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort, status, 21, p.timeout_ns) ? 1 : 0;
+          if (kDual && got)
+            got = mbar_wait_bounded(&tempty[1], acc_phase ^ 1u, abort, status, 21, p.timeout_ns) ? 1 : 0;
           if (got) tc_fence_after();
         }
         if (!__shfl_sync(0xffffffffu, got, 0)) break;
@@ -391,15 +406,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (got) {
               tc_fence_after();
               const uint64_t a_desc = smem_desc_k_sw128(smem_a + stage * kATileBytes);
-              const uint64_t b_desc = smem_desc_k_sw128(smem_b + stage * S::b_tile_bytes);
 #pragma unroll
-              for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                // +32 bytes along K inside the swizzle atom = +2 in the 16-byte address field
-                const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
-                if constexpr (kPair)
-                  mma_i8_pair(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
-                else
-                  mma_i8(d_tmem, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
+              for (int j = 0; j < S::dual_n; ++j) {
+                const uint64_t b_desc = smem_desc_k_sw128(smem_b + (stage * S::dual_n + j) * S::b_tile_bytes);
+                const uint32_t d = d_tmem + uint32_t(j * kBN);
+#pragma unroll
+                for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                  // +32 bytes along K inside the swizzle atom = +2 in the 16-byte address field
+                  const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+                  if constexpr (kPair)
+                    mma_i8_pair(d, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
+                  else
+                    mma_i8(d, a_desc + uint64_t(2 * kk), b_desc + uint64_t(2 * kk), S::idesc, accum);
+                }
               }
               if constexpr (kPair) mma_commit_pair(&empty[stage], 0x3);   // frees the stage in both CTAs
               else mma_commit(&empty[stage]);
@@ -417,11 +436,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         if (lane == 0) {
-          if constexpr (kPair) mma_commit_pair(&tfull[acc], 0x3);   // both CTAs' epilogues
-          else mma_commit(&tfull[acc]);
+          if constexpr (kPair) {
+            mma_commit_pair(&tfull[acc], 0x3);   // both CTAs' epilogues
+            if constexpr (kDual) mma_commit_pair(&tfull[1], 0x3);
+          } else {
+            mma_commit(&tfull[acc]);
+          }
         }
         __syncwarp();
-        if (++acc == 2) {
+        if (kDual) {
+          acc_phase ^= 1u;   // acc stays 0: the unit used accumulators 0 and 1
+        } else if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -443,9 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader = kPair ? map_to_rank(smem_addr(tempty), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = unit; tile < p.tiles; tile += units) {
-      int mt, nt;
-      tile_coords(tile, p.m_tiles, p.n_tiles, p.group_n, mt, nt);
+    // Tiles in the MMA's order: the dual_n tiles of each work unit in turn, so
+    // the accumulators alternate 0, 1, 0, 1 as in the single-tile form.
+    for (int it = 0;; ++it) {
+      const int w = unit + (it / S::dual_n) * units;
+      if (w >= p.work) break;
+      int mt, nu;
+      tile_coords(w, p.m_tiles, p.n_units, p.group_n, mt, nu);
+      const int nt = nu * S::dual_n + it % S::dual_n;
       const int n0 = nt * kBN;
       // Stage this tile's per-column scales (and bias) in shared memory.
       epilogue_sync();   // the previous tile's readers are done
@@ -647,8 +677,8 @@ bool make_output_map(CUtensorMap* map, const void* base, int rows, int cols, int
 
 struct DeviceInfo {
   int sms = 0;
-  bool attrs_set[2][4] = {};
-  int max_pairs[4] = {};     // co-resident clusters of two CTAs, per epilogue kind
+  bool attrs_set[2][2][4] = {};   // [pair][dual][epilogue]
+  int max_pairs[2][4] = {};       // co-resident clusters of two CTAs, per [dual][epilogue]
 };
 
 DeviceInfo& device_info(int device) {
@@ -666,24 +696,24 @@ int* status_ptr() {
   return ptr;
 }
 
-template <int kEpi, bool kPair>
+template <int kEpi, bool kPair, bool kDual = false>
 cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, GemmParams p,
                         cudaStream_t stream) {
-  using L = SmemLayout<kPair>;
+  using L = SmemLayout<kPair, kDual>;
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
   DeviceInfo& info = device_info(device);
-  auto kernel = int8_gemm_persistent<kEpi, kPair>;
-  if (!info.attrs_set[kPair][kEpi]) {
+  auto kernel = int8_gemm_persistent<kEpi, kPair, kDual>;
+  if (!info.attrs_set[kPair][kDual][kEpi]) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::dynamic_bytes);
     if (e != cudaSuccess) return e;
-    info.attrs_set[kPair][kEpi] = true;
+    info.attrs_set[kPair][kDual][kEpi] = true;
   }
   p.status = status_ptr();
   if (!p.status) return cudaErrorInvalidSymbol;
   if constexpr (!kPair) {
-    const int grid = p.tiles < info.sms ? p.tiles : info.sms;
+    const int grid = p.work < info.sms ? p.work : info.sms;
     kernel<<<grid, kThreads, L::dynamic_bytes, stream>>>(ma, mb, md, p);
     return cudaGetLastError();
   } else {
@@ -700,15 +730,15 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (info.max_pairs[kEpi] == 0) {
+    if (info.max_pairs[kDual][kEpi] == 0) {
       cfg.gridDim = dim3(unsigned(info.sms & ~1));
       int clusters = 0;
       e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
       if (e != cudaSuccess) return e;
       if (clusters < 1) return cudaErrorInvalidConfiguration;
-      info.max_pairs[kEpi] = clusters;
+      info.max_pairs[kDual][kEpi] = clusters;
     }
-    const int pairs = p.tiles < info.max_pairs[kEpi] ? p.tiles : info.max_pairs[kEpi];
+    const int pairs = p.work < info.max_pairs[kDual][kEpi] ? p.work : info.max_pairs[kDual][kEpi];
     cfg.gridDim = dim3(unsigned(2 * pairs));
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, md, p);
   }
@@ -756,14 +786,33 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.tiles = p.m_tiles * p.n_tiles;
+  // The dual form (two N-tiles per work unit, one A stage for both) where K is
+  // long enough for its unoverlapped epilogue to be small against the mainloop
+  // and there are enough units (>= kDualMinWaves per co-resident pair) for the
+  // larger units not to lose a partial last wave.
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(cudaErrorInvalidDevice, "h3_int8: no device");
+  const int approx_pairs = device_info(device).sms / 2;
+  const bool dual = pair && K >= kDualMinK && p.n_tiles % 2 == 0 &&
+                    int64_t(p.m_tiles) * (p.n_tiles / 2) >= int64_t(kDualMinWaves) * approx_pairs;
+  const int dual_n = dual ? 2 : 1;
+  p.n_units = p.n_tiles / dual_n;
+  p.work = p.m_tiles * p.n_units;
   {
-    const int64_t slice = int64_t(kBN) * K;   // B bytes of one N-tile
+    const int64_t slice = int64_t(kBN) * dual_n * K;   // B bytes of one work unit's N-tiles
     const int64_t g = kBSliceBytes / (slice > 0 ? slice : 1);
-    p.group_n = int(g < 1 ? 1 : (g > p.n_tiles ? p.n_tiles : g));
+    p.group_n = int(g < 1 ? 1 : (g > p.n_units ? p.n_units : g));
   }
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
-  if (pair) {
+  if (dual) {
+    switch (epi) {
+      case kEpiDequant: e = launch_gemm<kEpiDequant, true, true>(ma, mb, md, p, stream); break;
+      case kEpiGelu: e = launch_gemm<kEpiGelu, true, true>(ma, mb, md, p, stream); break;
+      case kEpiGate: e = launch_gemm<kEpiGate, true, true>(ma, mb, md, p, stream); break;
+      default: e = launch_gemm<kEpiAcc, true, true>(ma, mb, md, p, stream); break;
+    }
+  } else if (pair) {
     switch (epi) {
       case kEpiDequant: e = launch_gemm<kEpiDequant, true>(ma, mb, md, p, stream); break;
       case kEpiGelu: e = launch_gemm<kEpiGelu, true>(ma, mb, md, p, stream); break;

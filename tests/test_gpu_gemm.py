@@ -46,11 +46,14 @@ def test_accumulators_exact(device, m, n, k):
     assert _lib.pipeline_status() == 0
 
 
-@pytest.mark.parametrize("m,n,k", [(4096, 4096, 1024), (5000, 1032, 512)])
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 1024), (5000, 1032, 512), (4096, 4096, 8192), (19000, 3848, 8192)])
 def test_accumulators_exact_many_tiles(device, m, n, k):
     """Many tiles per CTA pair (every pair walks several tiles, both accumulators
     and every pipeline stage wrap), checked against torch._int_mm (cuBLAS) as the
-    reference for int32 accumulators."""
+    reference for int32 accumulators.  (19000, 3848, 8192) takes the dual form
+    (two N-tiles per work unit: K >= 8192, an even number of N-tiles -- sixteen,
+    the last 8 columns wide -- and at least eight waves of units; 19000 rows
+    leave a ragged last M-tile)."""
     a, w, *_ = _operands(m, n, k, m + n + k, device)
     acc = gemm.int8_accumulators(a, w)
     ref = torch._int_mm(a, w.t())
@@ -133,6 +136,24 @@ def test_gate_residual_in_place_bitexact(device, m, n, k, tables, with_bias):
     assert out.data_ptr() == residual.data_ptr()
     ref = ocpu.gate_residual(ocpu.gemm_s32(np_(a), np_(w)), np_(xs), np_(ws), bf16_bits(gate), np_(rows), before,
                              bf16_bits(bias) if with_bias else None)
+    assert np.array_equal(bf16_bits(residual), ref)
+
+
+def test_gate_residual_dual_form_bitexact(device):
+    """The gate epilogue through the dual form (see test_accumulators_exact_many_tiles),
+    with int32 accumulators from torch._int_mm and the epilogue from the C restatement."""
+    m, n, k, tables = 19000, 3848, 8192, 2
+    a, w, xs, ws, bias = _operands(m, n, k, 4242, device)
+    g = torch.Generator().manual_seed(9)
+    residual = torch.randn((m, n), generator=g).to(torch.bfloat16).to(device)
+    gate = (torch.randn((tables, n), generator=g) * 0.3).to(torch.bfloat16).to(device)
+    rows = torch.randint(0, tables, (m,), generator=g, dtype=torch.int32).to(device)
+    before = bf16_bits(residual)
+    acc = torch._int_mm(a, w.t())
+    gemm.int8_gate_residual(a, w, xs, ws, residual, gate, rows, bias=bias)
+    torch.cuda.synchronize()
+    assert _lib.pipeline_status() == 0
+    ref = ocpu.gate_residual(np_(acc), np_(xs), np_(ws), bf16_bits(gate), np_(rows), before, bf16_bits(bias))
     assert np.array_equal(bf16_bits(residual), ref)
 
 

@@ -126,7 +126,7 @@ struct GemmParams {
   int64_t gate_ld;
   int64_t ldr;
   int m, n, k;
-  int m_tiles, n_tiles, k_blocks, tiles;
+  int m_tiles, n_tiles, k_blocks;
   int n_units;                    // work units along N (n_tiles / dual_n)
   int work;                       // m_tiles * n_units
   int group_n;                    // N units per weight-stationary group
@@ -785,7 +785,6 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
-  p.tiles = p.m_tiles * p.n_tiles;
   // The dual form (two N-tiles per work unit, one A stage for both) where K is
   // long enough for its unoverlapped epilogue to be small against the mainloop
   // and there are enough units (>= kDualMinWaves per co-resident pair) for the

@@ -12,6 +12,8 @@ and ragged row counts that leave CTAs and row teams idle.
 """
 import ctypes as ct
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -146,3 +148,21 @@ def test_invalid_arguments_rejected_before_launch(device):
     assert lib.h3_residual_quant_run_k(*ptrs, m, k + 8, k + 8, k + 8, k + 8, ct.c_float(1e-6), 1, 1, 0, st) != 0
     torch.cuda.synchronize()
     assert torch.equal(x, before)
+
+
+@pytest.mark.parametrize("k,m,tables", [(256, 2001, 1), (2048, 3001, 2), (16384, 501, 1)])
+def test_streaming_equals_row_kernel_at_other_widths(device, k, m, tables):
+    """Widths the reference build does not cover (its K is a compile-time 4096 or
+    5376 here): the streaming form (staged tables where they fit; at K=16384 the
+    doubled slot leaves room for one row team) against the one-CTA-per-row form
+    (debug outputs), and the updated rows against the CPU restatement."""
+    from helpers import bf16_bits
+    from oracle import cpu as ocpu
+    args = _inputs(m, k, tables, torch.bfloat16, torch.bfloat16, 31 * k + m, device)
+    stream = _ours("run_t", *args)
+    rows_k = _ours("run_k", *args, debug=True)
+    torch.cuda.synchronize()
+    _assert_same(stream, rows_k[:3])
+    x, branch, w, gate, shift, scale, rows = args
+    x_new = ocpu.residual_update(bf16_bits(x), bf16_bits(branch), bf16_bits(gate), rows.cpu().numpy())
+    assert np.array_equal(bf16_bits(stream[0]), x_new)

@@ -13,7 +13,6 @@ and ragged row counts that leave CTAs and row teams idle.
 import ctypes as ct
 
 import numpy as np
-
 import pytest
 import torch
 

@@ -1,19 +1,20 @@
 // INT8 GEMM for B200 (sm_100a): D = epilogue(A[M,K] . B[N,K]^T) with int32
 // accumulation in tensor memory.
 //
-// Design (one persistent CTA per SM, 6 warps):
-//   warp 0      TMA producer: 128x128-byte A tiles and 256x128-byte B tiles,
-//               128-byte swizzle, into a 4-stage shared-memory ring guarded by
-//               full/empty mbarriers.  No multicast.
+// Design (one persistent CTA per SM, 10 warps; M > 128 runs CTA pairs, see Shape):
+//   warp 0      TMA producer: 128x128-byte A tiles and B tiles (256 rows, or the
+//               CTA's 128-row half in a pair), 128-byte swizzle, into a shared-
+//               memory ring guarded by full/empty mbarriers.  No multicast.
 //   warp 1      allocates 512 TMEM columns (two 128x256 int32 accumulators) and
-//               issues tcgen05.mma.kind::i8 (M=128, N=256, K=32; four per
-//               stage) from one thread; tcgen05.commit frees each smem stage and
-//               publishes each finished accumulator.
+//               issues tcgen05.mma.kind::i8 (N=256, K=32; four per stage; M=256
+//               over both CTAs of a pair) from one thread; tcgen05.commit frees
+//               each smem stage and publishes each finished accumulator.
 //   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column half
 //               (w - 2) / 4, 32 columns per tcgen05.ld; dequantise, apply the
 //               fused epilogue (bias, GELU, gate-residual, raw int32) and store.
 //               The second accumulator lets the epilogue of tile t overlap the
-//               mainloop of tile t+1.
+//               mainloop of tile t+1 (in the dual form a unit's two tiles use
+//               both accumulators and the epilogue does not overlap).
 // Tiles are visited weight-stationary: in groups of `group_n` N-tiles, whose
 // slice of B (group_n x 256 rows x K bytes, at most kBSliceBytes) stays in L2
 // while the group sweeps every M-tile, N-tile fastest.  A is then read from

@@ -1,14 +1,17 @@
 """Build the sm_100a kernel library in-tree and write its manifest.
 
 Output: ``h3_speedkit/_native/libh3sk_b200.so`` plus one symlink per library
-name the reference loads (``norm.so``, ``residual.so``, ``convrot.so``, ``fc1.so``, ``gate.so``)
+name the reference loads (``norm.so``, ``residual.so``, ``convrot.so``, ``fc1.so``, ``gate.so``, ``qkv.so``,
+``sample.so``, ``anchor.so``)
 and ``build.json`` in the reference's manifest schema
 (tools/build_kernels.py:41-63 of H3 SpeedKit: schema, kernels[name].sha256 ...).
 
 The quantiser translation units are compiled with ``--use_fast_math`` exactly
 as the reference compiles its norm/convrot kernels (tools/build_kernels.py:32-34),
 because the quantiser's division must be the same operation; the GEMM unit is
-compiled without it and spells every epilogue rounding explicitly.
+compiled without it and spells every epilogue rounding explicitly.  The QKV head
+epilogue is compiled without it and the K anchor detector with it, as the
+reference compiles its qkv/sample and anchor units (tools/build_kernels.py:35-37).
 """
 from __future__ import annotations
 
@@ -26,7 +29,7 @@ PKG = CSRC.parent
 NATIVE = PKG / "h3_speedkit" / "_native"
 BUILD = PKG / "_build"
 LIB_NAME = "libh3sk_b200.so"
-ALIASES = ("norm", "residual", "convrot", "fc1", "gate")
+ALIASES = ("norm", "residual", "convrot", "fc1", "gate", "qkv", "sample", "anchor")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-std=c++17", "-O3", "-DNDEBUG", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
           "--expt-relaxed-constexpr"]
@@ -34,6 +37,8 @@ UNITS = (
     ("norm_quant.cu", ["--use_fast_math", "-DH3SK_QUANT_FAST_MATH"]),
     ("convrot_quant.cu", ["--use_fast_math", "-DH3SK_QUANT_FAST_MATH"]),
     ("int8_gemm.cu", []),
+    ("qkv_quant.cu", []),
+    ("anchor.cu", ["--use_fast_math"]),
 )
 
 
@@ -88,7 +93,8 @@ def build(nvcc: str | None = None, force: bool = False, quiet: bool = True) -> P
     os.replace(tmp, lib)
     digest = sha256(lib)
     sources = {"norm": "norm_quant.cu", "residual": "norm_quant.cu", "convrot": "convrot_quant.cu",
-               "fc1": "int8_gemm.cu", "gate": "int8_gemm.cu"}
+               "fc1": "int8_gemm.cu", "gate": "int8_gemm.cu", "qkv": "qkv_quant.cu", "sample": "qkv_quant.cu",
+               "anchor": "anchor.cu"}
     for name in ALIASES:
         alias = NATIVE / (name + ".so")
         if alias.is_symlink() or alias.exists():

@@ -15,6 +15,16 @@ namespace h3sk {
 // (defined with the GEMM); bounded waits that run out record their code there.
 int* status_device_ptr();
 
+// The INT8 GEMM with the dequant epilogue bf(((acc*xs)*ws)+0) written head-major:
+// D is [N/128, M, 128] BF16 (plane h holds product columns 128h..128h+127).
+// Returns 1 on success, 0 on failure (reason in h3_int8_error).
+int gemm_dequant_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int N,
+                       int K, cudaStream_t stream);
+int last_gemm_error();
+// Set the thread's h3_int8_last_error / h3_int8_error record (returns 0), or clear it.
+int record_failure(int code, const char* what);
+void record_success();
+
 // Driver entry point of cuTensorMapEncodeTiled, resolved once through the
 // runtime (no libcuda link dependency); null if the driver lacks it.
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

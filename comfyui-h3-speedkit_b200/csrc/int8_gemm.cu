@@ -131,6 +131,7 @@ struct GemmParams {
   int n_units;                    // work units along N (n_tiles / dual_n)
   int work;                       // m_tiles * n_units
   int group_n;                    // N units per weight-stationary group
+  int head_major;                 // 1: D is [N/128, M, 128] (one plane per 128 columns)
   int* status;
   uint64_t timeout_ns;
 };
@@ -534,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_shared();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&map_d, stage, col0, row_base);
+            if (p.head_major) tma_store_3d(&map_d, stage, col0 & 127, row_base, col0 >> 7);
+            else tma_store_2d(&map_d, stage, col0, row_base);
             bulk_commit();
           }
         }
@@ -676,6 +678,21 @@ bool make_output_map(CUtensorMap* map, const void* base, int rows, int cols, int
   return r == CUDA_SUCCESS;
 }
 
+// Head-major BF16 output: plane h = columns [128h, 128h + 128) of the product,
+// stored as [heads, rows, 128] (plane stride rows * 128 elements), 32 x 32 boxes.
+bool make_output_map_heads(CUtensorMap* map, const void* base, int rows, int heads) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {128, cuuint64_t(rows), cuuint64_t(heads)};
+  const cuuint64_t strides[2] = {256, cuuint64_t(rows) * 256};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                        elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   int sms = 0;
   bool attrs_set[2][2][4] = {};   // [pair][dual][epilogue]
@@ -747,9 +764,11 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 
 int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
              void* D, int64_t ldd, const void* gate, const int32_t* rows, const void* residual, int M, int N,
-             int K, cudaStream_t stream) {
+             int K, cudaStream_t stream, bool heads = false) {
   if (!A || !B || !D || M < 1 || N < 1 || K < 16 || K % 16 || N % 8 || ldd < N || ldd % 8)
     return fail(cudaErrorInvalidValue, "h3_int8: invalid shape or null operand");
+  if (heads && (epi != kEpiDequant || N % 128))
+    return fail(cudaErrorInvalidValue, "h3_int8: head-major output needs the dequant epilogue and N % 128 == 0");
   if ((uintptr_t(A) & 15u) || (uintptr_t(B) & 15u) || (uintptr_t(D) & 15u))
     return fail(cudaErrorInvalidValue, "h3_int8: A, B and D must be 16-byte aligned");
   if (epi != kEpiAcc && (!xs || !ws || (uintptr_t(xs) & 3u) || (uintptr_t(ws) & 3u)))
@@ -767,7 +786,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       !make_operand_map(&mb, B, N, K, pair ? Shape<true>::b_rows : Shape<false>::b_rows))
     return fail(cudaErrorInvalidValue, "h3_int8: tensor map encoding failed");
   std::memset(&md, 0, sizeof(md));
-  if (epi != kEpiAcc && !make_output_map(&md, D, M, N, ldd))
+  if (epi != kEpiAcc && !(heads ? make_output_map_heads(&md, D, M, N / 128) : make_output_map(&md, D, M, N, ldd)))
     return fail(cudaErrorInvalidValue, "h3_int8: output tensor map encoding failed");
   GemmParams p{};
   p.xs = xs;
@@ -783,6 +802,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.m = M;
   p.n = N;
   p.k = K;
+  p.head_major = heads ? 1 : 0;
   p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
@@ -836,6 +856,18 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
 }  // namespace
 
 int* status_device_ptr() { return status_ptr(); }
+
+int gemm_dequant_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int N,
+                       int K, cudaStream_t stream) {
+  return run_gemm(kEpiDequant, A, B, xs, ws, nullptr, D, N, nullptr, nullptr, nullptr, M, N, K, stream, true);
+}
+
+int last_gemm_error() { return t_last_error; }
+int record_failure(int code, const char* what) { return fail(code, what); }
+void record_success() {
+  t_last_error = 0;
+  std::snprintf(t_last_message, sizeof(t_last_message), "ok");
+}
 
 }  // namespace h3sk
 

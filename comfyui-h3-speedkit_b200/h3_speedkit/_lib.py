@@ -46,6 +46,15 @@ EXPORTS = {
     "h3_int8_gate_ex": ([_P] * 11 + [_I] * 3 + [_SZ], _I),
     "h3_int8_last_error": ([], _I),
     "h3_int8_error": ([], ct.c_char_p),
+    "h3_qkv_quant_kv": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _SZ], _I),
+    "h3_qkv_quant_kv_ex": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _I, _I, _P, _SZ], _I),
+    "h3_sample_konly": ([_P] * 8 + [_F] + [_P] * 3 + [_I, _SZ], _I),
+    "h3_sample_konly_ex": ([_P] * 8 + [_F] + [_I, _I, _I, _P, _SZ], _I),
+    "h3_sample_gather": ([_P] * 6 + [_I, _SZ], _I),
+    "h3_sample_gather_ex": ([_P] * 6 + [_I, _I, _SZ], _I),
+    "h3_sample_anchor": ([_P, _P, _SZ], _I),
+    "h3_sample_anchor_ex": ([_P, _P, _I, _SZ], _I),
+    "h3_quant_v": ([_P] * 5 + [_I, _I, _SZ], _I),
     "h3sk_pipeline_status": ([_P, _I, _SZ], _I),
     "h3sk_wait_selftest": ([_I, _P, _SZ], _I),
     "h3sk_int8_mma_peak": ([_I, _P, _SZ], _I),

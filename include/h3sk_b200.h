@@ -230,6 +230,79 @@ int h3_int8_last_error(void);
 const char* h3_int8_error(void);
 
 /* ------------------------------------------------------------------------ */
+/* QKV projection -> pre-quantised attention operands (H3 geometry)          */
+/* ------------------------------------------------------------------------ */
+
+/* The H3 geometry the reference's QKV entry points are built for
+ * (h3_speedkit/ops/qkv.py:25-28): 56 heads of 128, hidden 5376, N = 21504. */
+enum { H3_QKV_HEADS = 56, H3_QKV_HIDDEN = 5376, H3_QKV_SAMPLES = 9 };
+
+/*
+ * Replaces h3_qkv_quant_kv (kernels/gemm/r84_kfourwarp.cu:385-388).  Returns 1 on
+ * success, 0 on failure (reason in h3_int8_error).
+ *   A [M, 5376] INT8, B [21504, 5376] INT8, xs [M] FP32, ws [21504] FP32
+ *   D      BF16 [3, 56, M, 128] (16-byte aligned): Q and K RMS-normalised with
+ *          qw / kw (BF16 [128]) and roped with freqs (BF16 [M, 48, 2, 2]); V raw
+ *   QI     INT8 [56, M, 128], QS FP32 [56, ceil(M/128)*32]  (rotated Q codes/scales)
+ *   KI     INT8 [56, M, 128], KS FP32 [56, ceil(M/128)*4]   (K minus its anchor row)
+ *   VP     FP32 [56, ceil(M/128), 128] per-tile maxima of |V|
+ *   SK     BF16 [56, 9, 128] sampled keys, anchors int32 [56] (row of SK or -1);
+ *          both NULL = no centring
+ *   1 <= M <= 200000.
+ */
+int h3_qkv_quant_kv(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                    const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI, float* QS,
+                    float* VP, int8_t* KI, float* KS, const void* SK, const int* anchors, int M,
+                    uintptr_t stream);
+/* Same contract for any head count and hidden size (N = 3 * heads * 128, hidden % 16
+ * == 0), with an optional rrms [2, heads, M] FP32 debug output (NULL = none).  No
+ * reference counterpart (the reference fixes the H3 geometry). */
+int h3_qkv_quant_kv_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                       const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI,
+                       float* QS, float* VP, int8_t* KI, float* KS, const void* SK, const int* anchors,
+                       int M, int heads, int hidden, float* rrms, uintptr_t stream);
+/*
+ * Replaces h3_sample_konly (kernels/gemm/r82_sample_konly.cu:337-341): the K plane of
+ * the QKV projection for the nine sample rows, normalised and roped, into plane 1 of
+ * D [3, 56, 9, 128] (planes 0 and 2 are not written).  M must be 9; QI, QS and VP are
+ * unused, as in the reference.  Returns 1 / 0.
+ */
+int h3_sample_konly(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                    const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI, float* QS,
+                    float* VP, int M, uintptr_t stream);
+/* Same for any head count, hidden size and row count (no reference counterpart). */
+int h3_sample_konly_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                       const void* freqs, const void* qw, const void* kw, float eps, int M, int heads,
+                       int hidden, float* rrms, uintptr_t stream);
+/*
+ * Replaces h3_sample_gather (kernels/gemm/r82_sample_konly.cu:352-356): rows
+ * s*(M-1)/8, s = 0..8, of Q [M, 5376] INT8, XS [M] FP32 and ROPE [M, 192] BF16 into
+ * SQ [9, 5376], SX [9], SR [9, 192].  Returns 1 / 0.
+ */
+int h3_sample_gather(const void* Q, const void* XS, const void* ROPE, void* SQ, void* SX, void* SR, int M,
+                     uintptr_t stream);
+/* Same for any hidden size (no reference counterpart). */
+int h3_sample_gather_ex(const void* Q, const void* XS, const void* ROPE, void* SQ, void* SX, void* SR,
+                        int M, int hidden, uintptr_t stream);
+/*
+ * Replaces h3_sample_anchor (kernels/gemm/r79_sample_anchor.cu:700-702): K [56, 9, 128]
+ * BF16 sampled keys -> anchors int32 [56].  Returns 1 / 0.
+ */
+int h3_sample_anchor(const void* K, void* anchors, uintptr_t stream);
+/* Same for any head count (no reference counterpart). */
+int h3_sample_anchor_ex(const void* K, void* anchors, int heads, uintptr_t stream);
+/*
+ * V quantiser of the QKV op.  No reference C counterpart: it replaces the two Triton
+ * kernels the reference launches on the V plane (h3_speedkit/ops/quant_v.py:57-104,
+ * launched at ops/qkv.py:70-79).  VP FP32 [heads, ceil(M/128), 128] tile maxima and
+ * V BF16 [heads, M, 128] (plane 2 of D) -> VS FP32 [heads*128] scales, VINV FP32
+ * [heads*128] their approximate reciprocals, VI INT8 [heads*128, ceil(M/128)*128]
+ * (channel-major, tokens permuted inside each run of 16).  Returns 1 / 0.
+ */
+int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, float* VINV, int M, int heads,
+               uintptr_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Pipeline health and diagnostics                                           */
 /* ------------------------------------------------------------------------ */
 

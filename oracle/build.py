@@ -18,7 +18,13 @@
      * ``ref_residual_k{K}.so`` kernels/residual_quant/residual_quant.cu (the
        reference's residual update fused with the prologue; K fixed the same way
        as norm_quant.cu, rewritten the same way for K = 4096);
-   The reference's INT8 GEMMs (kernels/gemm/fc1.cu, gate.cu) need the external
+     * ``ref_anchor.so``     kernels/gemm/r79_sample_anchor.cu, unmodified (the K
+       anchor detector ``h3_sample_anchor``; plain CUDA, --use_fast_math);
+     * ``ref_gather.so``     kernels/gemm/r82_sample_konly.cu, unmodified, built
+       without ``COMFY_HAVE_CUTLASS``: that leaves exactly its sample-row gather
+       ``h3_sample_gather`` (the CUTLASS K-only GEMM is compiled out);
+   The reference's INT8 GEMMs (kernels/gemm/fc1.cu, gate.cu, and the fused QKV
+   kernel r84_kfourwarp.cu with its K-only sample form) need the external
    CUTLASS library and are therefore not built; the GEMM oracle is the exact C
    restatement (int32 accumulation + IEEE epilogue, reproducible bit for bit).
    Step 2 runs only where the reference checkout exists (the build host); the
@@ -125,6 +131,13 @@ def build_ref(force: bool = False) -> list[Path]:
     if force or not _newer(target, conv_src):
         _compile(nvcc, conv_src, target, [conv_src.parent, conv_src.parent / "vendor"], ["--use_fast_math"])
     built.append(target)
+    gemm_dir = kernels / "gemm"
+    for name, source, extra in (("ref_anchor.so", "r79_sample_anchor.cu", ["--use_fast_math"]),
+                                ("ref_gather.so", "r82_sample_konly.cu", [])):
+        target = REF_OUT / name
+        if force or not _newer(target, gemm_dir / source):
+            _compile(nvcc, gemm_dir / source, target, [gemm_dir], extra)
+        built.append(target)
     launcher = HERE / "ref_kitchen_launch.cu"
     target = REF_OUT / "ref_kitchen.so"
     vendor = kernels / "convrot" / "vendor"

@@ -332,3 +332,290 @@ H3O_EXPORT void h3o_gate(const int32_t* acc, const float* xs, const float* ws, c
 }
 
 H3O_EXPORT int h3o_max_threads(void) { return set_threads(0); }
+
+/* ---- QKV head epilogue -------------------------------------------------------------
+ * The epilogue of the reference's fused QKV kernel after its int32 mainloop
+ * (kernels/gemm/r84_kfourwarp.cu:228-375; the K-plane-only sample form is
+ * r82_sample_konly.cu:230-330).  Input: the dequantised BF16 rows y [m, 3*H*128]
+ * (plane g = Q, K, V; head h; 128 channels), i.e. bf(((acc*xs)*ws)+0).
+ * The reference TU is built without fast-math, so nothing flushes here.
+ *   - per (row, Q/K head): sum = 32 lane chains fmaf(v, v, s) over d = l + 32i,
+ *     then the shfl_down tree; rrms = rsqrtf(sum/128 + eps) (hardware
+ *     approximation: 1/sqrt in double here, or the caller's injected value);
+ *     x = bf((t*rrms)*w); RoPE on d < 48 with partner d + 48:
+ *     y0 = bf(a*x0 + b*x1), y1 = bf(c*x0 + e*x1) (every product of two BF16 values
+ *     is exact in FP32, so contraction cannot change the sum); tail d >= 96 is x.
+ *   - Q codes: per 128-row tile, 32 groups of 4 rows {base + 8j}, base =
+ *     (sub/8)*32 + sub%8; K codes: 4 groups of 32 rows {tr : tr%8 in {2kg, 2kg+1}}
+ *     after subtracting the anchor row of sk; each row is rotated by the signed
+ *     128-point Hadamard (m > 256) or by 4-point blocks only (m <= 256);
+ *     scale = fmaf(max|v|, 1/127, 1e-7); code = cvt.rni.sat.s8(v * rcp(scale))
+ *     (rcp.approx.ftz on the GPU: IEEE 1/scale here).
+ *   - V: vp = max over each tile's rows of the |BF16| bit patterns.           */
+static const uint32_t kQkvSigns[4] = {0x1035997bu, 0x8087f5eeu, 0xee2e4e1au, 0x71132418u};
+
+static void qkv_convrot4(float* v) {
+  const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+  v[0] = (a0 + a2) * 0.5f;
+  v[1] = (a1 + a3) * 0.5f;
+  v[2] = (a0 - a2) * 0.5f;
+  v[3] = (a1 - a3) * 0.5f;
+}
+
+/* One 128-channel row as the reference's warp holds it: lane l owns channels 4l..4l+3. */
+static void qkv_rotate(float* v, int full) {
+  if (full) {
+    for (int ch = 0; ch < 128; ++ch) {
+      const int lane = ch >> 2, c = ch & 3;
+      const uint32_t flip = ((kQkvSigns[lane >> 3] >> ((lane & 7) * 4 + c)) & 1u) ^ 1u;
+      v[ch] = f_from_u(u_from_f(v[ch]) ^ (flip << 31));
+    }
+  }
+  for (int lane = 0; lane < 32; ++lane) qkv_convrot4(v + 4 * lane);
+  if (!full) return;
+  for (int bit = 1; bit < 32; bit <<= 1)
+    for (int lane = 0; lane < 32; ++lane) {
+      if (lane & bit) continue;
+      for (int c = 0; c < 4; ++c) {
+        const float lo = v[4 * lane + c], hi = v[4 * (lane | bit) + c];
+        v[4 * lane + c] = lo + hi;
+        v[4 * (lane | bit) + c] = lo - hi;
+      }
+    }
+  for (int ch = 0; ch < 128; ++ch) v[ch] *= 0.1767766952966369f;
+}
+
+/* cvt.rni.sat.s8.f32: round half to even, saturate, NaN -> 0. */
+static inline int8_t qkv_code(float x) {
+  if (x != x) return 0;
+  const float r = nearbyintf(x);
+  return (int8_t)(r > 127.0f ? 127 : (r < -128.0f ? -128 : (int)r));
+}
+
+static float qkv_rrms(const uint16_t* t, float eps) {
+  float p[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+      const float v = bf_to_f(t[l + 32 * i]);
+      s = fmaf(v, v, s);
+    }
+    p[l] = s;
+  }
+  for (int off = 16; off > 0; off >>= 1)
+    for (int l = 0; l < off; ++l) p[l] = p[l] + p[l + off];
+  return (float)(1.0 / sqrt((double)(p[0] / 128.0f + eps)));
+}
+
+/* Normalise + RoPE one Q/K head row t -> u (both BF16 bits). */
+static void qkv_norm_rope(const uint16_t* t, const uint16_t* w, const uint16_t* f, float rrms, uint16_t* u) {
+  for (int d = 0; d < 48; ++d) {
+    const float x0 = bf_round((bf_to_f(t[d]) * rrms) * bf_to_f(w[d]));
+    const float x1 = bf_round((bf_to_f(t[d + 48]) * rrms) * bf_to_f(w[d + 48]));
+    const float a = bf_to_f(f[4 * d]), b = bf_to_f(f[4 * d + 1]), c = bf_to_f(f[4 * d + 2]), e = bf_to_f(f[4 * d + 3]);
+    u[d] = f_to_bf(fmaf(a, x0, b * x1));
+    u[d + 48] = f_to_bf(fmaf(c, x0, e * x1));
+  }
+  for (int d = 96; d < 128; ++d) u[d] = f_to_bf((bf_to_f(t[d]) * rrms) * bf_to_f(w[d]));
+}
+
+/* planes: bit g set => produce plane g (Q=1, K=2, V=4).  d: [3, H, m, 128] (only the
+ * requested planes are written).  qi/ki: [H, m, 128]; qs: [H, parts*32];
+ * ks: [H, parts*4]; vp: [H, parts, 128]; any may be NULL to skip it.
+ * rrms_in / rrms_out: optional [2, H, m].  sk: [H, 9, 128]; anchors: [H].     */
+H3O_EXPORT void h3o_qkv_heads(const uint16_t* y, int64_t m, int64_t heads, const uint16_t* freqs,
+                              const uint16_t* qw, const uint16_t* kw, float eps, const uint16_t* sk,
+                              const int32_t* anchors, const float* rrms_in, int planes, uint16_t* d,
+                              int8_t* qi, float* qs, int8_t* ki, float* ks, float* vp, float* rrms_out,
+                              int threads) {
+  set_threads(threads);
+  const int64_t n = 3 * heads * 128, parts = (m + 127) / 128;
+  const int full = m > 256;
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+  for (int64_t tm = 0; tm < parts; ++tm)
+    for (int64_t h = 0; h < heads; ++h) {
+      const int64_t r0 = tm * 128, rows = (m - r0) < 128 ? (m - r0) : 128;
+      uint16_t u[2][128][128];
+      for (int g = 0; g < 2; ++g) {
+        if (!(planes & (1 << g))) continue;
+        const uint16_t* w = g == 0 ? qw : kw;
+        for (int64_t tr = 0; tr < rows; ++tr) {
+          const int64_t row = r0 + tr;
+          const uint16_t* t = y + row * n + (g * heads + h) * 128;
+          const float rrms = rrms_in ? rrms_in[(g * heads + h) * m + row] : qkv_rrms(t, eps);
+          if (rrms_out) rrms_out[(g * heads + h) * m + row] = rrms;
+          qkv_norm_rope(t, w, freqs + row * 192, rrms, u[g][tr]);
+          if (d) memcpy(d + ((g * heads + h) * m + row) * 128, u[g][tr], 256);
+        }
+      }
+      if ((planes & 1) && qi && qs) {
+        for (int sub = 0; sub < 32; ++sub) {
+          const int base = (sub / 8) * 32 + sub % 8;
+          float v[4][128], mx = 0.0f;
+          for (int j = 0; j < 4; ++j) {
+            const int64_t tr = base + 8 * j;
+            for (int ch = 0; ch < 128; ++ch) v[j][ch] = tr < rows ? bf_to_f(u[0][tr][ch]) : 0.0f;
+            qkv_rotate(v[j], full);
+            for (int ch = 0; ch < 128; ++ch) mx = fmaxf(mx, fabsf(v[j][ch]));
+          }
+          const float sc = fmaf(mx, 1.0f / 127.0f, 1e-7f), inv = 1.0f / sc;
+          qs[h * parts * 32 + tm * 32 + sub] = sc;
+          for (int j = 0; j < 4; ++j) {
+            const int64_t tr = base + 8 * j;
+            if (tr >= rows) continue;
+            for (int ch = 0; ch < 128; ++ch) qi[(h * m + r0 + tr) * 128 + ch] = qkv_code(v[j][ch] * inv);
+          }
+        }
+      }
+      if ((planes & 2) && ki && ks) {
+        float bias[128];
+        const int a = anchors ? anchors[h] : -1;
+        for (int ch = 0; ch < 128; ++ch) bias[ch] = a >= 0 ? bf_to_f(sk[(h * 9 + a) * 128 + ch]) : 0.0f;
+        for (int kg = 0; kg < 4; ++kg) {
+          float v[32][128], mx = 0.0f;
+          for (int i = 0; i < 32; ++i) {
+            const int64_t tr = (i / 2) * 8 + kg * 2 + (i & 1);
+            for (int ch = 0; ch < 128; ++ch) v[i][ch] = tr < rows ? bf_to_f(u[1][tr][ch]) - bias[ch] : 0.0f;
+            qkv_rotate(v[i], full);
+            for (int ch = 0; ch < 128; ++ch) mx = fmaxf(mx, fabsf(v[i][ch]));
+          }
+          const float sc = fmaf(mx, 1.0f / 127.0f, 1e-7f), inv = 1.0f / sc;
+          ks[(h * parts + tm) * 4 + kg] = sc;
+          for (int i = 0; i < 32; ++i) {
+            const int64_t tr = (i / 2) * 8 + kg * 2 + (i & 1);
+            if (tr >= rows) continue;
+            for (int ch = 0; ch < 128; ++ch) ki[(h * m + r0 + tr) * 128 + ch] = qkv_code(v[i][ch] * inv);
+          }
+        }
+      }
+      if (planes & 4) {
+        for (int ch = 0; ch < 128; ++ch) {
+          uint32_t mx = 0;
+          for (int64_t tr = 0; tr < rows; ++tr) {
+            const uint16_t b = y[(r0 + tr) * n + (2 * heads + h) * 128 + ch];
+            if (d) d[((2 * heads + h) * m + r0 + tr) * 128 + ch] = b;
+            const uint32_t mag = b & 0x7fffu;
+            mx = mag > mx ? mag : mx;
+          }
+          if (vp) vp[(h * parts + tm) * 128 + ch] = bf_to_f((uint16_t)mx);
+        }
+      }
+    }
+}
+
+/* ---- K anchor detector -----------------------------------------------------------
+ * kernels/gemm/r79_sample_anchor.cu:467-605 as launched by h3_sample_anchor
+ * (:700-702): per head, nine sampled keys k[s][c] (c < 128), one channel per
+ * thread of 4 warps, shfl_down trees, warp totals added in warp order.  The TU
+ * uses --use_fast_math: FTZ on every operation; 9*x - sum contracts to one
+ * fma, exact here because 9*x is exact for a BF16 x.                          */
+static float warp_tree_sum(float* p) {
+  for (int off = 16; off > 0; off >>= 1)
+    for (int l = 0; l < off; ++l) p[l] = ftz_add(p[l], p[l + off]);
+  return p[0];
+}
+static float warp_tree_max(float* p) {
+  for (int off = 16; off > 0; off >>= 1)
+    for (int l = 0; l < off; ++l) p[l] = fmaxf(p[l], p[l + off]);
+  return p[0];
+}
+
+H3O_EXPORT void h3o_sample_anchor(const uint16_t* k, int64_t heads, int32_t* anchors) {
+  for (int64_t h = 0; h < heads; ++h) {
+    const uint16_t* kh = k + h * 9 * 128;
+    float e[128], mxv[128], dist[9][128], sum[128];
+    for (int c = 0; c < 128; ++c) {
+      float en = 0.0f, mx = 0.0f, cs = 0.0f;
+      for (int s = 0; s < 9; ++s) {
+        const float v = ftz(bf_to_f(kh[s * 128 + c]));
+        en = ftz(fmaf(v, v, en));
+        mx = fmaxf(mx, fabsf(v));
+        cs = ftz_add(cs, v);
+      }
+      e[c] = en;
+      mxv[c] = mx;
+      sum[c] = cs;
+      for (int s = 0; s < 9; ++s) {
+        const float dd = ftz(fmaf(9.0f, ftz(bf_to_f(kh[s * 128 + c])), -cs));
+        dist[s][c] = ftz(fmaf(dd, dd, 0.0f));
+      }
+    }
+    (void)sum;
+    float we[4], wm[4], wd[9][4];
+    for (int w = 0; w < 4; ++w) {
+      float p[32];
+      memcpy(p, e + 32 * w, sizeof p);
+      we[w] = warp_tree_sum(p);
+      memcpy(p, mxv + 32 * w, sizeof p);
+      wm[w] = warp_tree_max(p);
+      for (int s = 0; s < 9; ++s) {
+        memcpy(p, dist[s] + 32 * w, sizeof p);
+        wd[s][w] = warp_tree_sum(p);
+      }
+    }
+    int best = 0;
+    float best_d = 3.402823466e+38f;
+    for (int s = 0; s < 9; ++s) {
+      float dsum = 0.0f;
+      for (int w = 0; w < 4; ++w) dsum = ftz_add(dsum, wd[s][w]);
+      if (dsum < best_d) {
+        best = s;
+        best_d = dsum;
+      }
+    }
+    float be[128], bm[128];
+    for (int c = 0; c < 128; ++c) {
+      const float a = ftz(bf_to_f(kh[best * 128 + c]));
+      float en = 0.0f, mx = 0.0f;
+      for (int s = 0; s < 9; ++s) {
+        const float r = ftz_sub(bf_to_f(kh[s * 128 + c]), a);
+        en = ftz(fmaf(r, r, en));
+        mx = fmaxf(mx, fabsf(r));
+      }
+      be[c] = en;
+      bm[c] = mx;
+    }
+    float toe = 0.0f, tom = 0.0f, tbe = 0.0f, tbm = 0.0f;
+    for (int w = 0; w < 4; ++w) {
+      float p[32];
+      memcpy(p, be + 32 * w, sizeof p);
+      const float wbe = warp_tree_sum(p);
+      memcpy(p, bm + 32 * w, sizeof p);
+      const float wbm = warp_tree_max(p);
+      toe = ftz_add(toe, we[w]);
+      tom = fmaxf(tom, wm[w]);
+      tbe = ftz_add(tbe, wbe);
+      tbm = fmaxf(tbm, wbm);
+    }
+    const int improves = tbe < toe && tbm <= ftz_mul(tom, 1.125f);
+    anchors[h] = improves ? best : -1;
+  }
+}
+
+/* ---- V quantiser -------------------------------------------------------------------
+ * The Triton kernels the reference's QKV op runs on the V plane
+ * (h3_speedkit/ops/quant_v.py:57-110, launched at ops/qkv.py:70-79):
+ *   scale[h,c] = max(RN_ftz(max_p vp[h,p,c] * (1/127)), 1e-12); inv = rcp(scale)
+ *   (rcp.approx.ftz on the GPU: IEEE 1/scale here);
+ *   vi[h*128 + c, dst] = cvt.rni.sat.s8(RN_ftz(v[h, src(dst), c] * inv)) for
+ *   dst < padded = parts*128, src = dst with bits (b3 b2 b1 b0) -> (b1 b3 b2 b0)
+ *   inside each run of 16 tokens, and 0 for src >= m.                           */
+H3O_EXPORT void h3o_quant_v(const uint16_t* v, int64_t m, int64_t heads, const float* vp, int8_t* vi,
+                            float* scale, int threads) {
+  set_threads(threads);
+  const int64_t parts = (m + 127) / 128, padded = parts * 128;
+  const float k127 = f_from_u(0x3C010204u), floor_ = f_from_u(0x2B8CBCCCu);
+#pragma omp parallel for schedule(static)
+  for (int64_t hc = 0; hc < heads * 128; ++hc) {
+    const int64_t h = hc / 128, c = hc % 128;
+    float mx = 0.0f;
+    for (int64_t p = 0; p < parts; ++p) mx = fmaxf(mx, vp[(h * parts + p) * 128 + c]);
+    const float sc = fmaxf(ftz_mul(mx, k127), floor_), inv = ftz(1.0f / sc);
+    scale[hc] = sc;
+    for (int64_t dst = 0; dst < padded; ++dst) {
+      const int64_t src = (dst & ~(int64_t)15) | (dst & 1) | ((dst & 2) << 2) | ((dst & 4) >> 1) | ((dst & 8) >> 1);
+      const float x = src < m ? bf_to_f(v[(h * m + src) * 128 + c]) : 0.0f;
+      vi[hc * padded + dst] = qkv_code(ftz_mul(x, inv));
+    }
+  }
+}

@@ -1,8 +1,9 @@
 """The reference's own CUDA kernels as the GPU oracle.  TEST INFRASTRUCTURE ONLY.
 
 Loads the libraries ``oracle/build.py`` compiled into ``oracle/_ref`` from the
-reference sources (norm_quant.cu, convrot_register_v2.cu and the vendored
-Kitchen quantiser) and runs them on torch CUDA tensors.  Output buffers are
+reference sources (norm_quant.cu, residual_quant.cu, convrot_register_v2.cu, the
+vendored Kitchen quantiser, the K anchor detector and the sample-row gather) and
+runs them on torch CUDA tensors.  Output buffers are
 allocated by the caller-side helpers here with torch; nothing in the product
 path uses this module.
 """
@@ -122,3 +123,36 @@ def residual_quant(x, branch, w, gate, shift, scale, rows, eps, *, debug=False):
     if rc:
         raise RuntimeError(f"reference residual_quant failed with CUDA error {rc}")
     return (xn, q, qs, dn, dr, drs) if debug else (xn, q, qs)
+
+
+def sample_anchor(k):
+    """Reference h3_sample_anchor (r79_sample_anchor.cu:467-605, 700-702): the nine
+    sampled keys k [56, 9, 128] BF16 -> int32 [56] anchor row (0..8) or -1."""
+    import torch
+    fn = _load("ref_anchor.so").h3_sample_anchor
+    fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
+    fn.restype = ct.c_int
+    if tuple(k.shape) != (56, 9, 128) or not k.is_contiguous():
+        raise ValueError("the reference detector is launched for 56 heads x 9 samples x 128")
+    anchors = torch.empty((56,), dtype=torch.int32, device=k.device)
+    if fn(k.data_ptr(), anchors.data_ptr(), _stream(k)) != 1:
+        raise RuntimeError("reference h3_sample_anchor launch failed")
+    return anchors
+
+
+def sample_gather(q, xs, rope):
+    """Reference h3_sample_gather (r82_sample_konly.cu:345-357): rows s*(m-1)//8 of
+    q [m, 5376] INT8, xs [m, 1] FP32 and the RoPE table [m, 192] BF16."""
+    import torch
+    fn = _load("ref_gather.so").h3_sample_gather
+    fn.argtypes = [ct.c_void_p] * 6 + [ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    m = q.shape[0]
+    dev = q.device
+    sq = torch.empty((9, 5376), dtype=torch.int8, device=dev)
+    sx = torch.empty((9, 1), dtype=torch.float32, device=dev)
+    sr = torch.empty((9, 192), dtype=torch.bfloat16, device=dev)
+    if fn(q.data_ptr(), xs.data_ptr(), rope.data_ptr(), sq.data_ptr(), sx.data_ptr(), sr.data_ptr(), m,
+          _stream(q)) != 1:
+        raise RuntimeError("reference h3_sample_gather launch failed")
+    return sq, sx, sr

@@ -36,7 +36,7 @@ def test_manifest_and_aliases():
     native = _lib.NATIVE
     manifest = json.loads((native / "build.json").read_text())
     assert manifest["schema"] == 1
-    for name in ("norm", "residual", "convrot", "fc1", "gate"):
+    for name in ("norm", "residual", "convrot", "fc1", "gate", "qkv", "sample", "anchor"):
         alias = native / f"{name}.so"
         assert alias.exists() and alias.resolve() == (native / _lib.LIB_NAME).resolve()
         assert manifest["kernels"][name]["sha256"]
@@ -126,3 +126,38 @@ def test_diagnostics_reject_bad_arguments():
     tops = ct.c_double(0)
     assert lib.h3sk_int8_mma_peak(1, ct.byref(tops), 0) == INVALID
     assert lib.h3sk_pipeline_status(None, 0, 0) == INVALID
+
+
+def _qkv(lib, **kw):
+    args = dict(A=16, B=16, xs=16, ws=16, D=16, freqs=16, qw=16, kw=16, eps=1e-6, QI=16, QS=16, VP=16, KI=16,
+                KS=16, SK=16, anchors=16, M=4)
+    args.update(kw)
+    return lib.h3_qkv_quant_kv(*(args[k] for k in ("A", "B", "xs", "ws", "D", "freqs", "qw", "kw")),
+                               ct.c_float(args["eps"]),
+                               *(args[k] for k in ("QI", "QS", "VP", "KI", "KS", "SK", "anchors", "M")), 0)
+
+
+@pytest.mark.parametrize("bad", [dict(A=None), dict(D=None), dict(M=0), dict(M=200001), dict(D=8),
+                                 dict(QI=None), dict(KS=None), dict(QI=18), dict(SK=None),
+                                 dict(eps=float("nan")), dict(eps=-1.0)])
+def test_qkv_rejects_before_launch(bad):
+    """h3_qkv_quant_kv keeps the reference's 1 / 0 convention (r84_kfourwarp.cu:385-388)
+    and rejects on the host: null operands, M outside [1, 200000] (the reference's
+    bound), a D that a TMA store cannot address, SK without anchors."""
+    lib = _lib.load()
+    assert _qkv(lib, **bad) == 0
+    assert lib.h3_int8_last_error() == INVALID and lib.h3_int8_error()
+
+
+def test_qkv_sample_entry_points_reject_before_launch():
+    lib = _lib.load()
+    eps = ct.c_float(1e-6)
+    # the reference's h3_sample_konly accepts M == 9 only (r82_sample_konly.cu:339)
+    assert lib.h3_sample_konly(16, 16, 16, 16, 16, 16, 16, 16, eps, None, None, None, 8, 0) == 0
+    assert lib.h3_sample_konly_ex(16, 16, 16, 16, 16, 16, 16, 16, eps, 9, 56, 5370, None, 0) == 0
+    assert lib.h3_sample_gather(16, 16, 16, 16, 16, 16, 0, 0) == 0
+    assert lib.h3_sample_gather(16, 18, 16, 16, 16, 16, 9, 0) == 0
+    assert lib.h3_sample_anchor_ex(16, 16, 0, 0) == 0
+    assert lib.h3_sample_anchor_ex(17, 16, 56, 0) == 0
+    assert lib.h3_quant_v(16, 16, 16, 16, 16, 0, 56, 0) == 0
+    assert lib.h3_quant_v(16, 8, 16, 16, 16, 9, 56, 0) == 0

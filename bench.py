@@ -62,6 +62,9 @@ def parse_args():
                     help="block geometry of the stack: cfg5 (default) or the H3 model's own (SwiGLU)")
     ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
                     help="5 (default): the 8-block stack; 1-4: the single-op BASELINE configs on one GPU")
+    ap.add_argument("--op", choices=("qkv",), default=None,
+                    help="qkv: the QKV op (projection -> pre-quantised attention operands) at the H3 "
+                         "geometry on one GPU, --tokens rows")
     return ap.parse_args()
 
 
@@ -540,10 +543,146 @@ def run_config(args):
     return 0
 
 
+def run_qkv(args):
+    """The QKV op at the H3 geometry (56 heads x 128, hidden 5376, N 21504) on one
+    GPU: the five launches of ``QKV.run`` (gather, K-only sample GEMM, anchor
+    detector, QKV GEMM + head epilogue, V quantiser), median over `--steps`
+    calls after `--warmup`, inputs larger than L2.  The GEMM alone (same kernel,
+    row-major output) is timed beside it for the tensor roofline."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import ctypes as ct
+    import numpy as np
+    import torch
+
+    from h3_speedkit import _lib
+    from h3_speedkit.ops import gemm
+    from h3_speedkit.ops.qkv import QKV
+    heads, hidden, m = 56, 5376, args.tokens
+    n = 3 * heads * 128
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM))
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1234)
+    q_cpu = torch.randint(-127, 128, (m, hidden), generator=g, dtype=torch.int8)
+    w_cpu = torch.randint(-127, 128, (n, hidden), generator=g, dtype=torch.int8)
+    xs_cpu = torch.rand((m, 1), generator=g) * 0.009 + 0.001
+    ws_cpu = torch.rand((n, 1), generator=g) * 0.0045 + 0.0005
+    ang = torch.rand((m, 48), generator=g) * 6.283
+    rope_cpu = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).reshape(1, m, 1, 48, 2, 2)
+    rope_cpu = rope_cpu.to(torch.bfloat16)
+    qw_cpu = (torch.rand((128,), generator=g) + 0.5).to(torch.bfloat16)
+    kw_cpu = (torch.rand((128,), generator=g) + 0.5).to(torch.bfloat16)
+    ops = 2.0 * m * n * hidden
+    workload = f"QKV op, H3 geometry: q INT8 [{m},{hidden}] x W [{n},{hidden}]^T, 56 heads x 128"
+    cfg = {"workload": workload, "tokens": m, "heads": heads, "hidden": hidden,
+           "l2": "inputs larger than L2 (D alone is 3*56*M*256 bytes)", "timing": f"median of {args.steps} calls"}
+    if args.impl == "reference":
+        from oracle import qkv as oqkv
+        sample = 256
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+        times = []
+        for _ in range(max(1, args.steps)):
+            t0 = time.perf_counter()
+            oqkv.qkv(q_cpu[:sample].numpy(), w_cpu.numpy(), xs_cpu[:sample].numpy(), ws_cpu.numpy(),
+                     bits(rope_cpu[:, :sample]).reshape(-1, 192), bits(qw_cpu), bits(kw_cpu), 1e-6, threads=threads)
+            times.append(time.perf_counter() - t0)
+        cpu_s = statistics.median(times) * m / sample
+        value = m / cpu_s
+        line = {"metric": "QKV op tokens/s (H3 geometry)", "value": value, "unit": "tokens/s", "n_gpus": 1,
+                "steps": args.steps, "warmup": 0, "ms_per_step": cpu_s * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg,
+                "impl": "reference",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": f"{sample} of the {m} rows through the CPU restatement, scaled"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    args_dev = tuple(t.to(dev) for t in (q_cpu, w_cpu, xs_cpu, ws_cpu, rope_cpu, qw_cpu, kw_cpu))
+    op = QKV()
+    clocks = ClockSampler()
+    ms = _median_ms(lambda _: op.run(*args_dev, 1e-6), warmup=max(3, args.warmup), iters=max(3, args.steps))
+    q, w, xs, ws = args_dev[:4]
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    clocks.start()
+    gemm_ms = _median_ms(lambda _: gemm.int8_linear(q, w, xs.view(-1), ws.view(-1), out=y),
+                         warmup=max(3, args.warmup), iters=max(3, args.steps))
+    ms = _median_ms(lambda _: op.run(*args_dev, 1e-6), warmup=1, iters=max(3, args.steps))
+    clock = clocks.stop()
+    del y
+    out = op.run(*args_dev, 1e-6)
+    v = out["d"][2]
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    vq_ms = _median_ms(lambda _: lib.h3_quant_v(out["vp"].data_ptr(), v.data_ptr(), out["vi"].data_ptr(),
+                                                out["vs"].data_ptr(), out["vinv"].data_ptr(), m, heads, st),
+                       warmup=3, iters=max(3, args.steps))
+    # bytes the head epilogue must move: Q/K planes read + written, codes and
+    # scales written, V plane read (its maxima written)
+    parts = (m + 127) // 128
+    epi_bytes = 2 * (2 * m * heads * 128 * 2) + 2 * m * heads * 128 + heads * parts * 36 * 4 + m * heads * 128 * 2
+    # end to end: q and the RoPE rows from pinned host memory, the three code
+    # tensors and their scales back to pinned host memory, inside the timed region
+    pin = lambda t: t.pin_memory()
+    q_h, xs_h, rope_h = pin(q_cpu), pin(xs_cpu.float()), pin(rope_cpu)
+    res_h = [torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in ("qi", "ki", "vi", "qs", "ks", "vs")]
+    q_d, xs_d, rope_d = torch.empty_like(args_dev[0]), torch.empty_like(args_dev[2]), torch.empty_like(args_dev[4])
+
+    def e2e(_):
+        q_d.copy_(q_h, non_blocking=True)
+        xs_d.copy_(xs_h, non_blocking=True)
+        rope_d.copy_(rope_h, non_blocking=True)
+        r = op.run(q_d, w, xs_d, ws, rope_d, args_dev[5], args_dev[6], 1e-6)
+        for h_t, k in zip(res_h, ("qi", "ki", "vi", "qs", "ks", "vs")):
+            h_t.copy_(r[k], non_blocking=True)
+    e2e_ms = _median_ms(e2e, warmup=2, iters=max(3, args.steps))
+    h2d = q_cpu.numel() + xs_cpu.numel() * 4 + rope_cpu.numel() * 2
+    d2h = sum(t.numel() * t.element_size() for t in res_h)
+    # CPU baseline: the restatement on a bounded sample
+    from oracle import qkv as oqkv
+    sample = 256
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    if not args.no_cpu_baseline:
+        oqkv.qkv(q_cpu[:sample].numpy(), w_cpu.numpy(), xs_cpu[:sample].numpy(), ws_cpu.numpy(),
+                 bits(rope_cpu[:, :sample]).reshape(-1, 192), bits(qw_cpu), bits(kw_cpu), 1e-6, threads=threads)
+    cpu_s = (time.perf_counter() - t0) * m / sample
+    gemm_tops = ops / (gemm_ms / 1e3) / 1e12
+    line = {
+        "metric": "QKV op tokens/s (H3 geometry)", "value": m / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg,
+        "tops": ops / (ms / 1e3) / 1e12,
+        "kernels_ms": {"op": ms, "gemm_alone": gemm_ms, "v_quant": vq_ms,
+                       "head_epilogue_and_samples": ms - gemm_ms - vq_ms},
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
+                     "frac": gemm_tops / int8_peak, "traffic": None,
+                     "peak_source": f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json"},
+        "roofline_epilogue": {"bound": "hbm", "bytes": epi_bytes,
+                              "achieved": epi_bytes / max(1e-9, (ms - gemm_ms - vq_ms) / 1e3) / 1e9,
+                              "peak": hbm_peak, "unit": "GB/s",
+                              "frac": epi_bytes / max(1e-9, (ms - gemm_ms - vq_ms) / 1e3) / 1e9 / hbm_peak},
+        "e2e": {"value": m / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "cpu_baseline": None if args.no_cpu_baseline else {
+            "value": m / cpu_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} of the {m} rows through the CPU restatement, scaled"},
+        "clocks": clock, "gpu_launches": 6,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     global D, ATTN, FFN, SWIGLU
     args = parse_args()
     D, ATTN, FFN, SWIGLU = GEOMETRIES[args.geometry]
+    if args.op == "qkv":
+        return run_qkv(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.config != 5:

@@ -75,206 +75,328 @@ __device__ __forceinline__ float rcp_approx_ftz(float x) {
   return y;
 }
 
-__device__ __forceinline__ uint32_t code_s8(float x) {
-  int c;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(x));
-  return uint32_t(c) & 0xffu;
-}
-
-// The 4-point block of one lane's channels.
-__device__ __forceinline__ void block4(float (&v)[4]) {
-  const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
-  v[0] = (a0 + a2) * 0.5f;
-  v[1] = (a1 + a3) * 0.5f;
-  v[2] = (a0 - a2) * 0.5f;
-  v[3] = (a1 - a3) * 0.5f;
-}
-
-// Rotate one 128-channel row held 4 channels per lane (lane l: channels 4l..4l+3).
-// Every lane of the warp must call it (shuffles).
-__device__ __forceinline__ void rotate(float (&v)[4], int lane, bool full) {
-  if (full) {
-    const uint32_t word = lane < 8 ? 0x1035997bu : lane < 16 ? 0x8087f5eeu : lane < 24 ? 0xee2e4e1au : 0x71132418u;
-    const int shift = (lane & 7) * 4;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t flip = ((word >> (shift + c)) & 1u) ^ 1u;
-      v[c] = __uint_as_float(__float_as_uint(v[c]) ^ (flip << 31));
-    }
-  }
-  block4(v);
-  if (!full) return;
-#pragma unroll
-  for (int bit = 1; bit < 32; bit <<= 1) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[c], bit);
-      v[c] = (lane & bit) ? other - v[c] : v[c] + other;
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < 4; ++c) v[c] *= 0.1767766952966369f;
-}
-
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
   return x;
 }
 
-__device__ __forceinline__ void load4(const __nv_bfloat16* row, int lane, float (&v)[4]) {
-  const uint2 u = *reinterpret_cast<const uint2*>(row + 4 * lane);
-  v[0] = __uint_as_float(u.x << 16);
-  v[1] = __uint_as_float(u.x & 0xffff0000u);
-  v[2] = __uint_as_float(u.y << 16);
-  v[3] = __uint_as_float(u.y & 0xffff0000u);
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// Two floats -> one BF16 pair word, round to nearest even (low half = lo).
+__device__ __forceinline__ uint32_t bf2(float lo, float hi) {
+  uint32_t w;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
+  return w;
+}
+__device__ __forceinline__ void unpack8(const uint4 u, float* v) {
+  v[0] = lo_f(u.x); v[1] = hi_f(u.x); v[2] = lo_f(u.y); v[3] = hi_f(u.y);
+  v[4] = lo_f(u.z); v[5] = hi_f(u.z); v[6] = lo_f(u.w); v[7] = hi_f(u.w);
+}
+// Codes of four values: cvt.rni.s32 then a saturating pack is cvt.rni.sat.s8
+// (round half to even, clamp to [-128, 127], NaN -> 0) four at a time.
+__device__ __forceinline__ uint32_t codes4(float a, float b, float c, float d, float inv) {
+  int ia, ib, ic, id;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ia) : "f"(a * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ib) : "f"(b * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ic) : "f"(c * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(id) : "f"(d * inv));
+  uint32_t hi, word;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(id), "r"(ic), "r"(0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(word) : "r"(ib), "r"(ia), "r"(hi));
+  return word;
 }
 
-__device__ __forceinline__ uint32_t pack_codes(const float (&v)[4], float inv) {
-  return code_s8(v[0] * inv) | (code_s8(v[1] * inv) << 8) | (code_s8(v[2] * inv) << 16) | (code_s8(v[3] * inv) << 24);
+// Rotation of one 128-channel row held by two threads, 64 channels each (thread
+// `half` owns channels 64*half + j, j = 0..63); the partner is lane ^ 1.  The
+// stages run in the reference's order -- sign flips, the 4-point block on channel
+// bits 0-1 ((a0 + a2) * 0.5 ...), butterflies on channel bits 2, 3, 4, 5 in
+// registers and bit 6 across the pair, each lo' = lo + hi, hi' = lo - hi, then the
+// factor 0.1767766952966369f -- so every value meets the same IEEE operations
+// with the same operands as in the reference's 4-channels-per-lane form.
+__device__ __forceinline__ void rotate64(float (&v)[64], int half, bool full) {
+  if (full) {
+    // flip channel ch when bit (ch & 31) of word ch >> 5 is clear
+    const uint32_t m0 = ~(half ? 0xee2e4e1au : 0x1035997bu), m1 = ~(half ? 0x71132418u : 0x8087f5eeu);
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const uint32_t m = j < 32 ? m0 : m1;
+      v[j] = __uint_as_float(__float_as_uint(v[j]) ^ ((m << (31 - (j & 31))) & 0x80000000u));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 64; j += 4) {
+    const float a0 = v[j] + v[j + 1], a1 = v[j] - v[j + 1], a2 = v[j + 2] + v[j + 3], a3 = v[j + 2] - v[j + 3];
+    v[j] = (a0 + a2) * 0.5f;
+    v[j + 1] = (a1 + a3) * 0.5f;
+    v[j + 2] = (a0 - a2) * 0.5f;
+    v[j + 3] = (a1 - a3) * 0.5f;
+  }
+  if (!full) return;
+#pragma unroll
+  for (int bit = 4; bit < 64; bit <<= 1) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      if (j & bit) continue;
+      const float lo = v[j], hi = v[j | bit];
+      v[j] = lo + hi;
+      v[j | bit] = lo - hi;
+    }
+  }
+  // bit 6: the partner holds the other half; lo + hi on half 0, lo - hi on half 1
+  // (fmaf(v, -1, other) = RN(other - v): the product is exact).
+  const float sgn = half ? -1.f : 1.f;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) {
+    const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    v[j] = fmaf(v[j], sgn, other) * 0.1767766952966369f;
+  }
 }
 
-// One CTA per (128-row tile, head, plane).
-__global__ void __launch_bounds__(kThreads) heads_kernel(const HeadParams p) {
-  __shared__ __align__(16) __nv_bfloat16 tile[kTileRows * kHead];
-  __shared__ float group_max[kThreads / 32];
-  __shared__ uint32_t v_half[kHead];
-  const int tm = blockIdx.x, h = blockIdx.y, g = p.plane0 + int(blockIdx.z);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// uint4 slot of 16-byte chunk c (0..15) of tile row r.  The chunk's low three bits
+// are XORed with r ^ (r >> 1) ^ (r >> 2): every access pattern below (pairs of
+// threads per row, the Q and K row groups of phase 2, the row-linear copies)
+// then spreads a warp's 16-byte accesses evenly over the eight bank groups.
+__device__ __forceinline__ int slot(int r, int c) { return r * 16 + (c ^ ((r ^ (r >> 1) ^ (r >> 2)) & 7)); }
+
+constexpr int kSlabChunks = kTileRows * kHead / 8;   // 16-byte chunks of one slab (32 KB)
+constexpr int kHeadsSmem = 2 * kSlabChunks * 16;      // two slabs in flight per CTA
+
+// Work item idx: plane-major, then head, then 128-row tile.
+struct Item {
+  int g, h, tm;
+};
+__device__ __forceinline__ Item item_of(const HeadParams& p, int idx) {
+  const int per_plane = p.heads * p.parts;
+  const int rem = idx % per_plane;
+  return Item{p.plane0 + idx / per_plane, rem / p.parts, rem % p.parts};
+}
+__device__ __forceinline__ __nv_bfloat16* slab_of(const HeadParams& p, const Item& it) {
+  return p.d + ((int64_t(it.g) * p.heads + it.h) * p.m + int64_t(it.tm) * kTileRows) * kHead;
+}
+
+// Asynchronous copy of item idx's slab into `buf` (16-byte cp.async per chunk,
+// swizzled slots); the caller commits the group.
+__device__ __forceinline__ void prefetch(const HeadParams& p, int idx, uint4* buf) {
+  const Item it = item_of(p, idx);
+  const int rows = min(kTileRows, p.m - it.tm * kTileRows);
+  const uint4* src = reinterpret_cast<const uint4*>(slab_of(p, it));
+  const uint32_t base = uint32_t(__cvta_generic_to_shared(buf));
+  for (int i = threadIdx.x; i < rows * (kHead / 8); i += kThreads)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(base + uint32_t(slot(i >> 4, i & 15)) * 16u),
+                 "l"(src + i)
+                 : "memory");
+}
+
+// Finish one slab already in shared memory.  Every early return is uniform
+// across the CTA (it depends on the item and the parameters only).
+__device__ __forceinline__ void process(const HeadParams& p, const Item& it, uint4* tile4, float* group_max,
+                                        uint4* v_part) {
+  const int tm = it.tm, h = it.h, g = it.g;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane & 1;
   const int r0 = tm * kTileRows;
   const int rows = min(kTileRows, p.m - r0);
-  __nv_bfloat16* slab = p.d + ((int64_t(g) * p.heads + h) * p.m + r0) * kHead;
-  for (int i = threadIdx.x; i < rows * (kHead / 8); i += kThreads)
-    reinterpret_cast<uint4*>(tile)[i] = reinterpret_cast<const uint4*>(slab)[i];
-  __syncthreads();
+  __nv_bfloat16* slab = slab_of(p, it);
 
   if (g == 2) {
-    // V: column maxima of |BF16| bit patterns; two row halves per channel.
+    // V: column maxima of the |BF16| bit patterns.  Thread (chunk c, row group
+    // rg) folds 8 rows of 8 channels with packed 16-bit maxima; lanes c and
+    // c + 16 of a warp, then the 8 warps through shared memory, are combined.
     if (p.vp == nullptr) return;
-    const int ch = threadIdx.x & (kHead - 1), half = threadIdx.x >> 7;
-    uint32_t mx = 0;
-    const int end = min(rows, (half + 1) * 64);
-    for (int tr = half * 64; tr < end; ++tr) {
-      const uint32_t mag = uint32_t(__bfloat16_as_ushort(tile[tr * kHead + ch])) & 0x7fffu;
-      mx = mag > mx ? mag : mx;
+    const int c = threadIdx.x & 15, rg = threadIdx.x >> 4;
+    uint32_t m4[4] = {0u, 0u, 0u, 0u};
+    const int end = min(rows, rg * 8 + 8);
+    for (int tr = rg * 8; tr < end; ++tr) {
+      const uint4 u = tile4[slot(tr, c)];
+      m4[0] = __vmaxu2(m4[0], u.x & 0x7fff7fffu);
+      m4[1] = __vmaxu2(m4[1], u.y & 0x7fff7fffu);
+      m4[2] = __vmaxu2(m4[2], u.z & 0x7fff7fffu);
+      m4[3] = __vmaxu2(m4[3], u.w & 0x7fff7fffu);
     }
-    if (half) v_half[ch] = mx;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m4[k] = __vmaxu2(m4[k], __shfl_xor_sync(0xffffffffu, m4[k], 16));
+    if (lane < 16) v_part[warp * 16 + c] = make_uint4(m4[0], m4[1], m4[2], m4[3]);
     __syncthreads();
-    if (!half) {
-      const uint32_t other = v_half[ch];
-      mx = other > mx ? other : mx;
+    if (threadIdx.x < kHead) {
+      const int ch = threadIdx.x;
+      uint32_t mx = 0;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) {
+        const uint32_t* part = reinterpret_cast<const uint32_t*>(&v_part[w * 16 + (ch >> 3)]);
+        const uint32_t word = part[(ch & 7) >> 1];
+        const uint32_t mag = (ch & 1) ? (word >> 16) : (word & 0xffffu);
+        mx = mag > mx ? mag : mx;
+      }
       p.vp[(int64_t(h) * p.parts + tm) * kHead + ch] = __uint_as_float(mx << 16);
     }
     return;
   }
 
-  // Q / K: RMS over the head, weight, RoPE; one warp per row.
+  // ---- phase 1: RMS over the head, weight, RoPE (row tr, thread half `half`) ----
   const __nv_bfloat16* w = g == 0 ? p.qw : p.kw;
-  for (int tr = warp; tr < rows; tr += kThreads / 32) {
-    __nv_bfloat16* t = tile + tr * kHead;
-    float sum = 0.f;
+  {
+    const int tr = threadIdx.x >> 1;
+    const bool live = tr < rows;                       // whole pairs: the pair stays converged
+    // chains l = 16*half + j over channels l, l + 32, l + 64, l + 96 in that order
+    float ch[16];
 #pragma unroll
-    for (int d = lane; d < kHead; d += 32) {
-      const float v = __bfloat162float(t[d]);
-      sum = fmaf(v, v, sum);
-    }
+    for (int j = 0; j < 16; ++j) ch[j] = 0.f;
+    if (live) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_down_sync(0xffffffffu, sum, off);
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-    const float rrms = rsqrtf(sum / 128.f + p.eps);
-    const int row = r0 + tr;
-    if (p.rrms != nullptr && lane == 0) p.rrms[(int64_t(g) * p.heads + h) * p.m + row] = rrms;
-    // Each lane reads and writes only its own channels (2l, 2l+1, +48; 96 + l).
-    if (lane < kPairs / 2) {
+      for (int c = 0; c < 4; ++c) {
+        float x[16];
+        unpack8(tile4[slot(tr, 4 * c + 2 * half)], x);
+        unpack8(tile4[slot(tr, 4 * c + 2 * half + 1)], x + 8);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int d = lane * 2 + i;
-        float x0 = __bfloat162float(t[d]), x1 = __bfloat162float(t[d + kPairs]);
-        x0 = __bfloat162float(__float2bfloat16_rn(x0 * rrms * __bfloat162float(w[d])));
-        x1 = __bfloat162float(__float2bfloat16_rn(x1 * rrms * __bfloat162float(w[d + kPairs])));
-        const __nv_bfloat16* f = p.freqs + int64_t(row) * kRopeRow + d * 4;
-        const float a = __bfloat162float(f[0]), b = __bfloat162float(f[1]);
-        const float c = __bfloat162float(f[2]), e = __bfloat162float(f[3]);
-        t[d] = __float2bfloat16_rn(a * x0 + b * x1);
-        t[d + kPairs] = __float2bfloat16_rn(c * x0 + e * x1);
+        for (int j = 0; j < 16; ++j) ch[j] = fmaf(x[j], x[j], ch[j]);
       }
     }
-    const int d = 2 * kPairs + lane;
-    t[d] = __float2bfloat16_rn(__bfloat162float(t[d]) * rrms * __bfloat162float(w[d]));
+    __syncwarp();   // every RMS read of the row precedes the partner's writes below
+    // the shfl_down tree of the reference: off 16 across the pair, 8..1 in registers
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ch[j] += __shfl_xor_sync(0xffffffffu, ch[j], 1);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < off; ++j) ch[j] += ch[j + off];
+    const float sum = __shfl_sync(0xffffffffu, ch[0], lane & ~1);
+    const float rrms = rsqrtf(sum / 128.f + p.eps);
+    if (live) {
+      const int row = r0 + tr;
+      if (p.rrms != nullptr && half == 0) p.rrms[(int64_t(g) * p.heads + h) * p.m + row] = rrms;
+      const uint4* w4 = reinterpret_cast<const uint4*>(w);
+      const uint4* f4 = reinterpret_cast<const uint4*>(p.freqs + int64_t(row) * kRopeRow) + 12 * half;
+      // pairs d = 24*half + 8q + i, partner d + 48: one uint4 of x0, x1, w0, w1 and
+      // four uint4 of RoPE coefficients (a, b, c, e per pair) per q
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int v0 = 3 * half + q, v1 = 6 + 3 * half + q;       // uint4 index of d and d + 48
+        float x0[8], x1[8], w0[8], w1[8];
+        unpack8(tile4[slot(tr, v0)], x0);
+        unpack8(tile4[slot(tr, v1)], x1);
+        unpack8(w4[v0], w0);
+        unpack8(w4[v1], w1);
+        uint32_t y0[4], y1[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const uint4 f = f4[4 * q + i / 2];
+          float a[2], b[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            a[k] = __bfloat162float(__float2bfloat16_rn(x0[i + k] * rrms * w0[i + k]));
+            b[k] = __bfloat162float(__float2bfloat16_rn(x1[i + k] * rrms * w1[i + k]));
+          }
+          // pair i: (f.x, f.y) = (a_c, b_c | c_c, e_c); pair i + 1: (f.z, f.w)
+          y0[i / 2] = bf2(lo_f(f.x) * a[0] + hi_f(f.x) * b[0], lo_f(f.z) * a[1] + hi_f(f.z) * b[1]);
+          y1[i / 2] = bf2(lo_f(f.y) * a[0] + hi_f(f.y) * b[0], lo_f(f.w) * a[1] + hi_f(f.w) * b[1]);
+        }
+        tile4[slot(tr, v0)] = make_uint4(y0[0], y0[1], y0[2], y0[3]);
+        tile4[slot(tr, v1)] = make_uint4(y1[0], y1[1], y1[2], y1[3]);
+      }
+      // tail channels 96 + 16*half .. +16: normalised and weighted only
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int vi = 12 + 2 * half + q;
+        float x[8], wt[8];
+        unpack8(tile4[slot(tr, vi)], x);
+        unpack8(w4[vi], wt);
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) o[i / 2] = bf2(x[i] * rrms * wt[i], x[i + 1] * rrms * wt[i + 1]);
+        tile4[slot(tr, vi)] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < rows * (kHead / 8); i += kThreads)
-    reinterpret_cast<uint4*>(slab)[i] = reinterpret_cast<const uint4*>(tile)[i];
+    reinterpret_cast<uint4*>(slab)[i] = tile4[slot(i >> 4, i & 15)];
   if (!p.quant) return;
+  if (g == 0 ? (p.qi == nullptr || p.qs == nullptr) : (p.ki == nullptr || p.ks == nullptr)) return;
 
-  const bool full = p.m > 256;
+  // ---- phase 2: rotation and codes; row tr, channels 64*half .. +64 ----
+  // Q: lanes 8s..8s+7 of warp w hold the 4 rows {base + 8j} of group 4w + s;
+  // K: warps 2kg, 2kg+1 hold the 32 rows {tr : tr % 8 in {2kg, 2kg+1}} of group kg.
+  int tr, group;
   if (g == 0) {
-    if (p.qi == nullptr || p.qs == nullptr) return;
-    for (int sub = warp; sub < 32; sub += kThreads / 32) {
-      const int base = (sub >> 3) * 32 + (sub & 7);
-      float v[4][4];
-      float mx = 0.f;
+    group = 4 * warp + (lane >> 3);
+    tr = (group >> 3) * 32 + (group & 7) + 8 * ((lane >> 1) & 3);
+  } else {
+    group = warp >> 1;
+    const int r_in = (warp & 1) * 16 + (lane >> 1);
+    tr = (r_in >> 1) * 8 + group * 2 + (r_in & 1);
+  }
+  const bool live = tr < rows;
+  float v[64];
+  if (live) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int tr = base + 8 * j;
-        if (tr < rows) load4(tile + tr * kHead, lane, v[j]);
-        else v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
-        rotate(v[j], lane, full);
+    for (int q = 0; q < 8; ++q) unpack8(tile4[slot(tr, 8 * half + q)], v + 8 * q);
+    if (g == 1 && p.anchors != nullptr && p.sk != nullptr) {
+      const int anchor = p.anchors[h];
+      if (anchor >= 0 && anchor < kSamples) {   // an out-of-range anchor reads nothing
+        const uint4* s4 = reinterpret_cast<const uint4*>(p.sk + (int64_t(h) * kSamples + anchor) * kHead) + 8 * half;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) mx = fmaxf(mx, fabsf(v[j][c]));
-      }
-      mx = warp_max(mx);
-      const float sc = fmaf(mx, 1.f / 127.f, 1e-7f), inv = rcp_approx_ftz(sc);
-      if (lane == 0) p.qs[int64_t(h) * p.parts * 32 + tm * 32 + sub] = sc;
+        for (int q = 0; q < 8; ++q) {
+          float b[8];
+          unpack8(s4[q], b);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int tr = base + 8 * j;
-        if (tr < rows)
-          *reinterpret_cast<uint32_t*>(p.qi + (int64_t(h) * p.m + r0 + tr) * kHead + 4 * lane) = pack_codes(v[j], inv);
+          for (int i = 0; i < 8; ++i) v[8 * q + i] = v[8 * q + i] - b[i];
+        }
       }
     }
-    return;
-  }
-
-  // K: centre on the anchor row, rotate, one scale per 32-row group; two warps
-  // per group (16 rows each), their maxima combined through shared memory.
-  if (p.ki == nullptr || p.ks == nullptr) return;
-  float bias[4] = {0.f, 0.f, 0.f, 0.f};
-  const int anchor = (p.anchors != nullptr && p.sk != nullptr) ? p.anchors[h] : -1;
-  if (anchor >= 0 && anchor < kSamples) {   // an out-of-range anchor reads nothing
+  } else {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) bias[c] = __bfloat162float(p.sk[(int64_t(h) * kSamples + anchor) * kHead + 4 * lane + c]);
+    for (int j = 0; j < 64; ++j) v[j] = 0.f;
   }
-  const int kg = warp >> 1, half = warp & 1;
-  float v[16][4];
+  rotate64(v, half, p.m > 256);
   float mx = 0.f;
 #pragma unroll
-  for (int ii = 0; ii < 16; ++ii) {
-    const int i = half * 16 + ii;
-    const int tr = (i >> 1) * 8 + kg * 2 + (i & 1);
-    if (tr < rows) {
-      load4(tile + tr * kHead, lane, v[ii]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) v[ii][c] = v[ii][c] - bias[c];
-    } else {
-      v[ii][0] = v[ii][1] = v[ii][2] = v[ii][3] = 0.f;
-    }
-    rotate(v[ii], lane, full);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) mx = fmaxf(mx, fabsf(v[ii][c]));
+  for (int j = 0; j < 64; ++j) mx = fmaxf(mx, fabsf(v[j]));
+  float sc, inv;
+  if (g == 0) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    sc = fmaf(mx, 1.f / 127.f, 1e-7f);
+    inv = rcp_approx_ftz(sc);
+    if ((lane & 7) == 0) p.qs[int64_t(h) * p.parts * 32 + tm * 32 + group] = sc;
+  } else {
+    mx = warp_max(mx);
+    if (lane == 0) group_max[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(group_max[warp & ~1], group_max[warp | 1]);
+    sc = fmaf(mx, 1.f / 127.f, 1e-7f);
+    inv = rcp_approx_ftz(sc);
+    if (threadIdx.x == 64 * group) p.ks[(int64_t(h) * p.parts + tm) * 4 + group] = sc;
   }
-  mx = warp_max(mx);
-  if (lane == 0) group_max[warp] = mx;
-  __syncthreads();
-  mx = fmaxf(group_max[warp & ~1], group_max[warp | 1]);
-  const float sc = fmaf(mx, 1.f / 127.f, 1e-7f), inv = rcp_approx_ftz(sc);
-  if (lane == 0 && half == 0) p.ks[(int64_t(h) * p.parts + tm) * 4 + kg] = sc;
+  if (live) {
+    int8_t* out = (g == 0 ? p.qi : p.ki) + (int64_t(h) * p.m + r0 + tr) * kHead + 64 * half;
 #pragma unroll
-  for (int ii = 0; ii < 16; ++ii) {
-    const int i = half * 16 + ii;
-    const int tr = (i >> 1) * 8 + kg * 2 + (i & 1);
-    if (tr < rows)
-      *reinterpret_cast<uint32_t*>(p.ki + (int64_t(h) * p.m + r0 + tr) * kHead + 4 * lane) = pack_codes(v[ii], inv);
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<uint4*>(out)[q] =
+          make_uint4(codes4(v[16 * q], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3], inv),
+                     codes4(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7], inv),
+                     codes4(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11], inv),
+                     codes4(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15], inv));
+  }
+}
+
+// Persistent: CTA b takes items b, b + grid, ...; the slab of the next item is
+// copied into the other buffer while this one is finished.
+__global__ void __launch_bounds__(kThreads, 2) heads_kernel(const HeadParams p, int items) {
+  extern __shared__ __align__(16) uint4 heads_smem[];
+  __shared__ float group_max[kThreads / 32];
+  __shared__ uint4 v_part[(kThreads / 32) * 16];
+  int idx = blockIdx.x;
+  if (idx < items) prefetch(p, idx, heads_smem);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int k = 0; idx < items; ++k, idx += gridDim.x) {
+    const int next = idx + int(gridDim.x);
+    if (next < items) prefetch(p, next, heads_smem + ((k + 1) & 1) * kSlabChunks);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");   // this item's slab has landed
+    __syncthreads();
+    process(p, item_of(p, idx), heads_smem + (k & 1) * kSlabChunks, group_max, v_part);
+    __syncthreads();   // the buffer is free before the next prefetch refills it
   }
 }
 
@@ -355,9 +477,12 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 // Head epilogue launch over planes [plane0, plane0 + planes).
 int launch_heads(const HeadParams& p, int planes, cudaStream_t stream) {
-  dim3 grid(p.parts, p.heads, planes);
-  heads_kernel<<<grid, kThreads, 0, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  const int64_t items = int64_t(planes) * p.heads * p.parts;
+  int grid = 0;
+  cudaError_t e = rq_persistent_grid(reinterpret_cast<const void*>(heads_kernel), kThreads, kHeadsSmem, items, &grid);
+  if (e != cudaSuccess) return record_failure(e, "h3_qkv: head epilogue occupancy query failed");
+  heads_kernel<<<grid, kThreads, kHeadsSmem, stream>>>(p, int(items));
+  e = cudaGetLastError();
   return e == cudaSuccess ? 1 : record_failure(e, "h3_qkv: head epilogue launch failed");
 }
 

@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "host_util.h"
 #include "../../include/h3sk_b200.h"
@@ -621,4 +622,74 @@ H3SK_EXPORT int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, 
   if (e != cudaSuccess) return h3sk::record_failure(e, "h3_quant_v: launch failed");
   h3sk::record_success();
   return 1;
+}
+
+// ---- allocation-free whole-op entry point ------------------------------------------
+// The op's intermediates (sample rows, their K plane, anchors, V reciprocal scales)
+// live in one file-scope device array instead of caller buffers.  Its size bounds
+// the geometry: heads <= 64, hidden <= 8192 (the H3 geometry is 56 x 5376).
+namespace h3sk {
+namespace qkv {
+
+constexpr int kNoAllocMaxHeads = 64;
+constexpr int kNoAllocMaxHidden = 8192;
+constexpr size_t pad256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr size_t kSqOff = 0;
+constexpr size_t kSxOff = kSqOff + pad256(size_t(kSamples) * kNoAllocMaxHidden);
+constexpr size_t kSrOff = kSxOff + pad256(kSamples * 4);
+constexpr size_t kSdOff = kSrOff + pad256(size_t(kSamples) * kRopeRow * 2);
+constexpr size_t kAnchorOff = kSdOff + pad256(size_t(3) * kNoAllocMaxHeads * kSamples * kHead * 2);
+constexpr size_t kVinvOff = kAnchorOff + pad256(size_t(kNoAllocMaxHeads) * 4);
+constexpr size_t kScratchBytes = kVinvOff + pad256(size_t(kNoAllocMaxHeads) * kHead * 4);   // 552,960 B
+
+__device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+
+// Device address of g_scratch on the current device, resolved once per device.
+unsigned char* scratch_base() {
+  static std::mutex mu;
+  static unsigned char* base[64] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (base[device] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_scratch) != cudaSuccess) return nullptr;
+    base[device] = static_cast<unsigned char*>(ptr);
+  }
+  return base[device];
+}
+
+}  // namespace qkv
+}  // namespace h3sk
+
+H3SK_EXPORT int h3_qkv_noalloc(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                               const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI, float* QS,
+                               float* VP, int8_t* KI, float* KS, void* VI, float* VS, int M, int heads, int hidden,
+                               uintptr_t stream) {
+  using namespace h3sk::qkv;
+  if (heads < 1 || heads > kNoAllocMaxHeads || hidden < 16 || hidden > kNoAllocMaxHidden || hidden % 16)
+    return h3sk::record_failure(cudaErrorInvalidValue, "h3_qkv_noalloc: heads <= 64 and hidden <= 8192 (hidden % 16 == 0)");
+  if (!A || !xs || !freqs || !VI || !VS || M < 1 || M > kMaxRows)
+    return h3sk::record_failure(cudaErrorInvalidValue, "h3_qkv_noalloc: null operand or M out of range");
+  unsigned char* base = scratch_base();
+  if (base == nullptr) return h3sk::record_failure(cudaErrorInvalidSymbol, "h3_qkv_noalloc: scratch address");
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int8_t* sq = reinterpret_cast<int8_t*>(base + kSqOff);
+  float* sx = reinterpret_cast<float*>(base + kSxOff);
+  __nv_bfloat16* sr = reinterpret_cast<__nv_bfloat16*>(base + kSrOff);
+  __nv_bfloat16* sd = reinterpret_cast<__nv_bfloat16*>(base + kSdOff);
+  const __nv_bfloat16* sk = sd + size_t(heads) * kSamples * kHead;   // plane 1 of [3, heads, 9, 128]
+  int* anchors = reinterpret_cast<int*>(base + kAnchorOff);
+  float* vinv = reinterpret_cast<float*>(base + kVinvOff);
+  // Every scratch word is written before it is read, so nothing is cleared.
+  if (!gather_run(A, xs, freqs, sq, sx, sr, M, hidden, s)) return 0;
+  if (!qkv_run(sq, B, sx, ws, sd, sr, qw, kw, eps, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+               kSamples, heads, hidden, nullptr, s, true))
+    return 0;
+  if (!h3_sample_anchor_ex(sk, anchors, heads, stream)) return 0;
+  if (!qkv_run(A, B, xs, ws, D, freqs, qw, kw, eps, QI, QS, VP, KI, KS, sk, anchors, M, heads, hidden, nullptr, s,
+               false))
+    return 0;
+  const void* v_plane = static_cast<const __nv_bfloat16*>(D) + size_t(2) * heads * M * kHead;
+  return h3_quant_v(VP, v_plane, VI, VS, vinv, M, heads, stream);
 }

@@ -55,6 +55,7 @@ EXPORTS = {
     "h3_sample_anchor": ([_P, _P, _SZ], _I),
     "h3_sample_anchor_ex": ([_P, _P, _I, _SZ], _I),
     "h3_quant_v": ([_P] * 5 + [_I, _I, _SZ], _I),
+    "h3_qkv_noalloc": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _I, _I, _SZ], _I),
     "h3sk_pipeline_status": ([_P, _I, _SZ], _I),
     "h3sk_wait_selftest": ([_I, _P, _SZ], _I),
     "h3sk_int8_mma_peak": ([_I, _P, _SZ], _I),

@@ -301,6 +301,20 @@ int h3_sample_anchor_ex(const void* K, void* anchors, int heads, uintptr_t strea
  */
 int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, float* VINV, int M, int heads,
                uintptr_t stream);
+/*
+ * The whole QKV op in one call, allocating nothing.  No reference counterpart (the
+ * reference runs the five steps from Python with torch-allocated intermediates,
+ * h3_speedkit/ops/qkv.py:46-79).  Same operands and outputs as h3_qkv_quant_kv_ex
+ * plus the V quantiser's VI / VS; the intermediates (nine sample rows, their K plane,
+ * the anchors, the V reciprocal scales) live in a 552,960-byte file-scope device
+ * array, which bounds heads <= 64 and hidden <= 8192 (larger shapes are rejected).
+ * Calls that share a device share that array: they must not overlap (issue them on
+ * one stream, or order them with events).  Returns 1 / 0.
+ */
+int h3_qkv_noalloc(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
+                   const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI, float* QS,
+                   float* VP, int8_t* KI, float* KS, void* VI, float* VS, int M, int heads, int hidden,
+                   uintptr_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Pipeline health and diagnostics                                           */

@@ -107,6 +107,9 @@ class QKV:
         if qw.numel() != HEAD or kw.numel() != HEAD or qw.dtype != torch.bfloat16 or kw.dtype != torch.bfloat16:
             raise ValueError("qw / kw must be BF16 [128]")
         device = q.device
+        inputs = (q, w, xs, ws, rope, qw, kw)
+        if any(not x.is_cuda or x.device != device or not x.is_contiguous() for x in inputs):
+            raise ValueError("QKV operands must be contiguous and on one CUDA device")
         stream = torch.cuda.current_stream(device)
         st = stream.cuda_stream
         parts = (m + 127) // 128
@@ -130,9 +133,7 @@ class QKV:
         if debug:
             t["rrms"] = torch.empty((2, heads, m), device=device, dtype=f32)
             t["sample_rrms"] = torch.empty((2, heads, SAMPLES), device=device, dtype=f32)
-        owners = (q, w, xs, ws, rope, qw, kw, *t.values())
-        if any(not x.is_cuda or x.device != device or not x.is_contiguous() for x in owners):
-            raise ValueError("QKV operands must be contiguous and on one CUDA device")
+        owners = (*inputs, *t.values())
         for x in owners:
             x.record_stream(stream)
         p = {k: v.data_ptr() for k, v in t.items()}

@@ -2,8 +2,8 @@
 
 Run on a B200 box from the repository root after ``oracle/build.py`` has built
 ``oracle/_ref`` (the reference's norm_quant.cu, residual_quant.cu,
-convrot_register_v2.cu and the vendored Kitchen quantiser, compiled from the
-reference sources):
+convrot_register_v2.cu, the vendored Kitchen quantiser, r79_sample_anchor.cu and
+the gather of r82_sample_konly.cu, compiled from the reference sources):
 
     python tests/golden/make_golden.py [name-prefix ...]
 
@@ -95,6 +95,31 @@ def residual_case(name, k, m, tables, gate_dtype, table_dtype, seed):
                         norm=bits(dn), rstd=drs.cpu().numpy())
 
 
+def anchor_case(name, seed):
+    """The K anchor detector (r79_sample_anchor.cu:467-605) on three sets of 56 x 9
+    sampled keys: plain, with a shared per-head offset, and with one outlier sample."""
+    g = torch.Generator().manual_seed(seed)
+    k = torch.randn((3, 56, 9, 128), generator=g)
+    k[1] += torch.randn((56, 1, 128), generator=g) * 4
+    k[2, :, 4] *= 30
+    k = k.to(torch.bfloat16)
+    anchors = torch.stack([ref_gpu.sample_anchor(k[i].cuda()) for i in range(3)])
+    torch.cuda.synchronize()
+    np.savez_compressed(HERE / f"{name}.npz", kind="sample_anchor", k=bits(k), anchors=anchors.cpu().numpy())
+
+
+def gather_case(name, m, seed):
+    """The sample-row gather (r82_sample_konly.cu:345-357), hidden 5376."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randint(-127, 128, (m, 5376), generator=g, dtype=torch.int8)
+    xs = torch.rand((m, 1), generator=g)
+    rope = torch.randn((m, 192), generator=g).to(torch.bfloat16)
+    sq, sx, sr = ref_gpu.sample_gather(q.cuda(), xs.cuda(), rope.cuda())
+    torch.cuda.synchronize()
+    np.savez_compressed(HERE / f"{name}.npz", kind="sample_gather", q=q.numpy(), xs=xs.numpy(), rope=bits(rope),
+                        sq=sq.cpu().numpy(), sx=sx.cpu().numpy(), sr=bits(sr))
+
+
 CASES = [
     ("norm_k4096_bf16", lambda n: norm_case(n, 4096, 8, 2, torch.bfloat16, 101)),
     ("norm_k5376_f32", lambda n: norm_case(n, 5376, 6, 3, torch.float32, 102)),
@@ -106,6 +131,8 @@ CASES = [
     ("kitchen_k2048_swiglu", lambda n: kitchen_case(n, 2048, 8, 2, 108)),
     ("residual_k5376_bf16", lambda n: residual_case(n, 5376, 6, 2, torch.bfloat16, torch.bfloat16, 109)),
     ("residual_k4096_f32", lambda n: residual_case(n, 4096, 8, 3, torch.float32, torch.float32, 110)),
+    ("anchor_k56x9", lambda n: anchor_case(n, 111)),
+    ("gather_m20", lambda n: gather_case(n, 20, 112)),
 ]
 
 

@@ -66,3 +66,21 @@ def test_oracle_residual_prologue_matches_reference_kernel(name):
     assert np.array_equal(norm, g["norm"]), "normalised/modulated BF16 values"
     assert np.array_equal(qs, g["qscale"]), "row scales"
     assert_codes_close(q, g["q"], 1e-3, name)
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c.startswith("anchor_")])
+def test_oracle_anchor_detector_matches_reference_kernel(name):
+    """r79_sample_anchor.cu fixtures: the anchor row of each head, exactly."""
+    from oracle import qkv as oqkv
+    g = load(name)
+    for i in range(g["k"].shape[0]):
+        assert np.array_equal(oqkv.sample_anchor(g["k"][i]), g["anchors"][i]), f"key set {i}"
+    assert (g["anchors"][1] >= 0).all() and (g["anchors"][0] == -1).all()
+
+
+@pytest.mark.parametrize("name", [c for c in CASES if c.startswith("gather_")])
+def test_oracle_sample_rows_match_reference_kernel(name):
+    from oracle import qkv as oqkv
+    g = load(name)
+    sq, sx, sr = oqkv.gather(g["q"], g["xs"], g["rope"])
+    assert np.array_equal(sq, g["sq"]) and np.array_equal(sx, g["sx"]) and np.array_equal(sr, g["sr"])

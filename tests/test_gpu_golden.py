@@ -73,3 +73,31 @@ def test_residual_prologue_reproduces_golden(device, name, debug):
     if debug:
         assert np.array_equal(dbg["debug_rstd"].cpu().numpy(), g["rstd"])
         assert np.array_equal(dbg["debug_norm"].cpu().view(torch.int16).numpy().view(np.uint16), g["norm"])
+
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in GOLDEN.glob("anchor_*.npz")))
+def test_anchor_detector_reproduces_golden(device, name):
+    from h3_speedkit import _lib
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    lib = _lib.load()
+    for i in range(g["k"].shape[0]):
+        k = _tensor(g["k"][i], device)
+        out = torch.empty((56,), dtype=torch.int32, device=device)
+        assert lib.h3_sample_anchor(k.data_ptr(), out.data_ptr(), torch.cuda.current_stream().cuda_stream) == 1
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), g["anchors"][i])
+
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in GOLDEN.glob("gather_*.npz")))
+def test_sample_gather_reproduces_golden(device, name):
+    from h3_speedkit import _lib
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    q, xs, rope = _tensor(g["q"], device), _tensor(g["xs"], device), _tensor(g["rope"], device)
+    sq = torch.empty((9, 5376), dtype=torch.int8, device=device)
+    sx = torch.empty((9, 1), dtype=torch.float32, device=device)
+    sr = torch.empty((9, 192), dtype=torch.bfloat16, device=device)
+    assert _lib.load().h3_sample_gather(q.data_ptr(), xs.data_ptr(), rope.data_ptr(), sq.data_ptr(), sx.data_ptr(),
+                                        sr.data_ptr(), q.shape[0], torch.cuda.current_stream().cuda_stream) == 1
+    torch.cuda.synchronize()
+    assert np.array_equal(sq.cpu().numpy(), g["sq"]) and np.array_equal(sx.cpu().numpy(), g["sx"])
+    assert np.array_equal(sr.cpu().view(torch.int16).numpy().view(np.uint16), g["sr"])

@@ -275,3 +275,25 @@ def test_last_block_window_from_the_prepared_layout():
     assert runtime.last_block_window({"layout": gap}, 5000) == 0          # spans not contiguous
     one = SimpleNamespace(seq_len=5000, segments=[(0, 700, "text"), (700, 5000, "video")])
     assert runtime.last_block_window({"layout": one}, 5000) == 0          # the reference needs two spans
+
+
+def test_qkv_op_rejects_wrong_geometry_before_any_launch():
+    """ops/qkv.py:24-40 of the reference: the H3 geometry, the RoPE layout and the
+    operand dtypes are checked first, with the reference's messages."""
+    import torch
+    from h3_speedkit.ops.qkv import QKV
+    op = QKV()
+    m = 4
+    q = torch.zeros((m, 5376), dtype=torch.int8)
+    w = torch.zeros((21504, 5376), dtype=torch.int8)
+    xs, ws = torch.zeros((m, 1)), torch.zeros((21504, 1))
+    rope = torch.zeros((1, m, 1, 48, 2, 2), dtype=torch.bfloat16)
+    qw = kw = torch.zeros((128,), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="H3 56 x 128, hidden=5376"):
+        op(q[:, :5120], w, xs, ws, rope, qw, kw, 1e-6)
+    with pytest.raises(ValueError, match="pinned partial split-half RoPE layout"):
+        op(q, w, xs, ws, rope.view(1, m, 1, 96, 2), qw, kw, 1e-6)
+    with pytest.raises(ValueError, match="does not match the CUDA ABI"):
+        op(q, w, xs.double(), ws, rope, qw, kw, 1e-6)
+    with pytest.raises(ValueError, match="contiguous and on one CUDA device"):
+        op(q, w, xs, ws, rope, qw, kw, 1e-6)

@@ -117,12 +117,20 @@ __device__ __forceinline__ uint32_t codes4(float a, float b, float c, float d, f
 // with the same operands as in the reference's 4-channels-per-lane form.
 __device__ __forceinline__ void rotate64(float (&v)[64], int half, bool full) {
   if (full) {
-    // flip channel ch when bit (ch & 31) of word ch >> 5 is clear
-    const uint32_t m0 = ~(half ? 0xee2e4e1au : 0x1035997bu), m1 = ~(half ? 0x71132418u : 0x8087f5eeu);
+    // flip channel ch when bit (ch & 31) of word ch >> 5 is clear.  Per register j
+    // both halves' flips are compile-time constants: equal ones become a negation
+    // (folded into the adds below), differing ones an XOR with the half's mask.
+    const uint32_t hmask = half ? 0x80000000u : 0u;
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
-      const uint32_t m = j < 32 ? m0 : m1;
-      v[j] = __uint_as_float(__float_as_uint(v[j]) ^ ((m << (31 - (j & 31))) & 0x80000000u));
+      const uint32_t w0 = j < 32 ? 0x1035997bu : 0x8087f5eeu;   // channels j (half 0)
+      const uint32_t w1 = j < 32 ? 0xee2e4e1au : 0x71132418u;   // channels 64 + j (half 1)
+      const bool f0 = ((w0 >> (j & 31)) & 1u) == 0u, f1 = ((w1 >> (j & 31)) & 1u) == 0u;
+      if (f0 && f1) {
+        v[j] = -v[j];
+      } else if (f0 != f1) {
+        v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (f1 ? hmask : (hmask ^ 0x80000000u)));
+      }
     }
   }
 #pragma unroll
@@ -154,11 +162,17 @@ __device__ __forceinline__ void rotate64(float (&v)[64], int half, bool full) {
   }
 }
 
-// uint4 slot of 16-byte chunk c (0..15) of tile row r.  The chunk's low three bits
-// are XORed with r ^ (r >> 1) ^ (r >> 2): every access pattern below (pairs of
-// threads per row, the Q and K row groups of phase 2, the row-linear copies)
-// then spreads a warp's 16-byte accesses evenly over the eight bank groups.
-__device__ __forceinline__ int slot(int r, int c) { return r * 16 + (c ^ ((r ^ (r >> 1) ^ (r >> 2)) & 7)); }
+// uint4 slot of 16-byte chunk c (0..15) of tile row r: the chunk's low three bits
+// are XORed with (r ^ (r >> 1) ^ (r >> 2) ^ 3h) & 7, h = c >> 3 the chunk's half.
+// A 16-byte shared access is served eight lanes at a time; counted over every
+// access pattern below (pairs of threads per row in phase 1, the Q and K row
+// groups of phase 2, the V column scan, the row-linear copies) this key needs
+// 1920 such wavefronts against a conflict-free floor of 1536 (no swizzle: 6656;
+// the key without the 3h term: 2432, as both threads of a row then meet in one
+// bank group).
+__device__ __forceinline__ int slot(int r, int c) {
+  return r * 16 + (c ^ ((r ^ (r >> 1) ^ (r >> 2) ^ (3 * (c >> 3))) & 7));
+}
 
 constexpr int kSlabChunks = kTileRows * kHead / 8;   // 16-byte chunks of one slab (32 KB)
 constexpr int kHeadsSmem = 2 * kSlabChunks * 16;      // two slabs in flight per CTA

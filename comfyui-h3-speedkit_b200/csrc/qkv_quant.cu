@@ -639,9 +639,15 @@ H3SK_EXPORT int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, 
 }
 
 // ---- allocation-free whole-op entry point ------------------------------------------
-// The op's intermediates (sample rows, their K plane, anchors, V reciprocal scales)
-// live in one file-scope device array instead of caller buffers.  Its size bounds
-// the geometry: heads <= 64, hidden <= 8192 (the H3 geometry is 56 x 5376).
+// For callers that may not allocate device memory at run time: a serving loop
+// that must not call cudaMalloc after warm-up (the call can synchronise the
+// device and stall every other stream), or a host framework that owns all device
+// memory through its own pool and hands this library only the operands and
+// outputs.  The op's intermediates (sample rows, their K plane, anchors, V
+// reciprocal scales) live in one file-scope device array instead of allocated
+// buffers.  Its size bounds the geometry: heads <= 64, hidden <= 8192 (the H3
+// geometry is 56 x 5376); every GPU that loads the library holds the array
+// until the process exits.
 namespace h3sk {
 namespace qkv {
 
@@ -656,9 +662,12 @@ constexpr size_t kAnchorOff = kSdOff + pad256(size_t(3) * kNoAllocMaxHeads * kSa
 constexpr size_t kVinvOff = kAnchorOff + pad256(size_t(kNoAllocMaxHeads) * 4);
 constexpr size_t kScratchBytes = kVinvOff + pad256(size_t(kNoAllocMaxHeads) * kHead * 4);   // 552,960 B
 
-__device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-// Device address of g_scratch on the current device, resolved once per device.
+// Device address of g_scratch on the current device.  In host code the name
+// g_scratch is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress, once per device, on the first call made with that
+// device current, and cached.
 unsigned char* scratch_base() {
   static std::mutex mu;
   static unsigned char* base[64] = {};

@@ -302,14 +302,22 @@ int h3_sample_anchor_ex(const void* K, void* anchors, int heads, uintptr_t strea
 int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, float* VINV, int M, int heads,
                uintptr_t stream);
 /*
- * The whole QKV op in one call, allocating nothing.  No reference counterpart (the
- * reference runs the five steps from Python with torch-allocated intermediates,
- * h3_speedkit/ops/qkv.py:46-79).  Same operands and outputs as h3_qkv_quant_kv_ex
- * plus the V quantiser's VI / VS; the intermediates (nine sample rows, their K plane,
- * the anchors, the V reciprocal scales) live in a 552,960-byte file-scope device
- * array, which bounds heads <= 64 and hidden <= 8192 (larger shapes are rejected).
- * Calls that share a device share that array: they must not overlap (issue them on
- * one stream, or order them with events).  Returns 1 / 0.
+ * The whole QKV op in one call, allocating nothing.  It has no counterpart in the
+ * reference (which runs the five steps from Python with torch-allocated
+ * intermediates).  It is for callers that cannot allocate device memory while
+ * they run: a serving loop that must not call cudaMalloc after warm-up (the call
+ * can synchronise the device and stall other streams), or a framework that owns
+ * all device memory through its own pool.  Same operands and outputs as
+ * h3_qkv_quant_kv_ex plus the V quantiser's VI / VS.  The intermediates (nine
+ * sample rows, their K plane, the anchors, the V reciprocal scales) live in a
+ * 552,960-byte file-scope device array that every GPU loading the library holds
+ * until exit; it bounds heads <= 64 and hidden <= 8192, and larger shapes are
+ * rejected with an error (h3_int8_error).  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  Every call writes each
+ * intermediate before reading it, so nothing needs clearing, but all calls on a
+ * device share the array: calls that overlap on the GPU race (issue them on one
+ * stream, or order them with events).  Returns 1 / 0.
  */
 int h3_qkv_noalloc(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D,
                    const void* freqs, const void* qw, const void* kw, float eps, int8_t* QI, float* QS,

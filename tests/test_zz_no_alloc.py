@@ -1,7 +1,9 @@
 """The allocation-free QKV entry point ``h3_qkv_noalloc``.
 
-It runs the same five steps as the QKV op with its intermediates in a file-scope
-device array, so its outputs must equal, bit for bit, those of the op built
+It is for callers that cannot allocate device memory while they run (a serving
+loop that forbids cudaMalloc after warm-up, a framework that owns all device
+memory).  It runs the same five steps as the QKV op with its intermediates in a
+file-scope device array, so its outputs must equal, bit for bit, those of the op built
 from the individual entry points with torch-allocated intermediates
 (``QKV.run``) -- on two calls in a row, so that stale scratch from the first
 call cannot leak into the second.  Collected last so that it also runs after

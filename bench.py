@@ -41,7 +41,7 @@ METRIC = "INT8 DiT-block TOPS and tokens/s at 1/2/4/8 B200; % INT8/HBM roofline"
 D, FFN, BLOCKS, TOKENS = 4096, 16384, 8, 98304
 ATTN, SWIGLU = 4096, False          # cfg5: attention width = D, GELU MLP
 # --geometry h3: the H3 model's block (hidden 5376, attention 7168, SwiGLU MLP of
-# width 14336), the row SURVEY ranks next after config 5
+# width 14336), the real model's geometry beside config 5's generic one
 GEOMETRIES = {"cfg5": (4096, 4096, 16384, False), "h3": (5376, 7168, 14336, True)}
 CPU_SAMPLE_TOKENS = 1024
 FALLBACK_BF16_SUSTAINED = 1400.0   # TFLOP/s, used only if MEASURED_PEAKS.json is absent
@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--blocks", type=int, default=BLOCKS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-single-ops", action="store_true",
+                    help="N=1: leave out the BASELINE config 1-4 single-op lines nested in the stack line")
     ap.add_argument("--geometry", choices=tuple(GEOMETRIES), default="cfg5",
                     help="block geometry of the stack: cfg5 (default) or the H3 model's own (SwiGLU)")
     ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
@@ -74,6 +76,34 @@ def measured_peaks():
         data = json.loads(path.read_text())
         return data, "measured"
     return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": FALLBACK_BF16_SUSTAINED, "hbm_gbs": FALLBACK_HBM}, "fallback"
+
+
+def int8_peaks(lib, stream) -> dict:
+    """Dense INT8 tensor peak of this GPU, the roofline denominator of the GEMMs.
+
+    burst: the live tcgen05 kind::i8 issue-rate probe (every SM issues back-to-back
+    128x256x32 MMAs from shared memory into TMEM; no operand traffic), measured on
+    this GPU at the start of the run -- the figure for an op timed alone.
+    sustained: burst x (bf16_tflops_sustained / bf16_tflops) of MEASURED_PEAKS.json,
+    i.e. scaled by the clock loss the same pool's cuBLAS GEMM shows between a burst
+    and a seconds-long loop under the 1 kW power cap -- the figure for a GEMM timed
+    inside the long block-stack step.  Without a probe result the burst falls back
+    to 2 x bf16_tflops (INT8 dense = 2 x BF16 dense on B200)."""
+    import ctypes as ct
+    peaks, kind = measured_peaks()
+    bf16_burst = float(peaks.get("bf16_tflops", 1590.0))
+    bf16_sust = float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
+    tops = ct.c_double(0.0)
+    probe = None
+    for _ in range(2):   # the first call warms the clocks up; keep the better one
+        if lib.h3sk_int8_mma_peak(1 << 16, ct.byref(tops), stream) == 0 and tops.value > 0:
+            probe = max(probe or 0.0, tops.value)
+    burst = probe if probe else 2.0 * bf16_burst
+    src = ("live tcgen05 kind::i8 probe" if probe else f"2 x bf16_tflops of {kind} MEASURED_PEAKS.json")
+    return {"burst": burst, "sustained": burst * bf16_sust / bf16_burst, "probe_tops": probe,
+            "burst_source": src,
+            "sustained_source": f"burst x bf16_tflops_sustained/bf16_tflops ({bf16_sust:.1f}/{bf16_burst:.1f}) "
+                                f"of {kind} MEASURED_PEAKS.json"}
 
 
 class ClockSampler:
@@ -265,12 +295,7 @@ def run_ours(args):
         stack.load(x_src)
         stack.forward(events)
 
-    probe = None
-    if rank == 0:
-        import ctypes as ct
-        tops = ct.c_double(0.0)
-        if lib.h3sk_int8_mma_peak(1 << 16, ct.byref(tops), stream.cuda_stream) == 0:
-            probe = tops.value
+    i8 = int8_peaks(lib, stream.cuda_stream) if rank == 0 else None
 
     for _ in range(args.warmup):
         step()
@@ -340,6 +365,15 @@ def run_ours(args):
                "h2d_bytes_per_step": args.tokens * D * 2, "d2h_bytes_per_step": args.tokens * D * 2,
                "ms_per_step": e_elapsed * 1e3 / args.steps, "output": out_desc}
 
+    # ---- BASELINE single-op configs 1-4 (rank 0, N=1 only) -------------------------
+    singles = None
+    if rank == 0 and world == 1 and not args.no_single_ops:
+        singles = {}
+        for c in (1, 2, 3, 4):
+            singles[f"cfg{c}"] = single_op(c, lib, i8, warmup=10, iters=50, e2e_iters=5,
+                                           cpu_baseline=not args.no_cpu_baseline)
+            torch.cuda.empty_cache()
+
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -357,7 +391,7 @@ def run_ours(args):
         return 0
 
     peaks, peak_kind = measured_peaks()
-    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
+    int8_peak = i8["sustained"]
     m_local = stop - start
     gemm_ops = {"qkv": 2 * m_local * 3 * ATTN * D, "outproj": 2 * m_local * D * ATTN,
                 "fc1": 2 * m_local * fc1_n() * D, "fc2": 2 * m_local * D * FFN}
@@ -395,13 +429,16 @@ def run_ours(args):
         "tops": total_ops * args.steps / elapsed / 1e12,
         "roofline": {"bound": "tensor", "kernel": f"int8_gemm_persistent ({dominant})", "achieved": achieved,
                      "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
-                     "peak_source": f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json",
-                     "int8_mma_probe_tops": probe},
+                     "peak_source": "sustained INT8: " + i8["sustained_source"],
+                     "int8_mma_probe_tops": i8["probe_tops"], "frac_of_burst": achieved / i8["burst"],
+                     "per_gemm": {k: {"tops": round(gemm_ops[k] / (v["avg_ms"] / 1e3) / 1e12, 1),
+                                      "frac": round(gemm_ops[k] / (v["avg_ms"] / 1e3) / 1e12 / int8_peak, 4)}
+                                  for k, v in gemms.items()}},
         "roofline_prologue": prologue_line,
         "kernels": {k: {"launches": v["launches"], "avg_ms": round(v["avg_ms"], 4),
                         "share": round(v["total_ms"] / step_total, 4)} for k, v in per_kernel.items()},
         "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps * world,
-        "e2e": e2e, "cpu_baseline": cpu,
+        "e2e": e2e, "cpu_baseline": cpu, "single_ops": singles,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -428,27 +465,30 @@ def _median_ms(fn, warmup=20, iters=100, rotate=1):
     return statistics.median(a.elapsed_time(b) for a, b in times)
 
 
-def run_config(args):
-    """BASELINE configs 1-4 as single-op lines (SURVEY-style measurement: 20 warm-up
-    and 100 timed launches, median, buffers rotated beyond L2)."""
-    if int(os.environ.get("RANK", "0")) != 0:
-        return 0
+def single_op(cfg: int, lib, i8: dict, *, warmup: int = 20, iters: int = 100, e2e_iters: int = 10,
+              cpu_baseline: bool = True) -> dict:
+    """One BASELINE single-op config (1-4) on the current GPU: the device-timed
+    median with inputs resident in HBM (buffers rotated beyond L2), the same op end
+    to end through its Python API with the step's activations copied in from pinned
+    host memory and its outputs copied back (weights stay resident, as a model's
+    do), the roofline against the burst INT8 peak (an op timed alone) or the
+    measured HBM copy bandwidth, and a bounded CPU-restatement baseline."""
+    import ctypes as ct
     import numpy as np
     import torch
 
-    from h3_speedkit import _lib, synthetic
+    from h3_speedkit import synthetic
     from h3_speedkit.ops import gemm
     from h3_speedkit.ops.convrot import quantize_int8_rowwise_convrot64
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
     peaks, peak_kind = measured_peaks()
-    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM))
     threads = host_threads()
     torch.set_num_threads(threads)
     st = lambda: torch.cuda.current_stream().cuda_stream
-    cfg = args.config
+    pin = lambda t: t.contiguous().pin_memory()
+    nb = lambda *ts: sum(t.numel() * t.element_size() for t in ts)
+    cpu = None
     if cfg == 1:
         inp = synthetic.cfg1()
         x, w, bias = inp["x"].to(dev), inp["w"].to(dev), inp["bias"].to(dev)
@@ -456,23 +496,32 @@ def run_config(args):
         ws = wsc.reshape(-1).contiguous()
         out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=dev)
 
-        def op(_):
-            q, qs = quantize_int8_rowwise_convrot64(x)
-            gemm.int8_linear(q, wq, qs.reshape(-1), ws, bias=bias, out=out)
-        ms = _median_ms(op)
+        def run(xd, o):
+            q, qs = quantize_int8_rowwise_convrot64(xd)
+            gemm.int8_linear(q, wq, qs.reshape(-1), ws, bias=bias, out=o)
+        ms = _median_ms(lambda _: run(x, out), warmup=warmup, iters=iters)
         ops = 2.0 * 1024 * 2048 * 2048
-        value, unit, bound, ach, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", None, int8_peak
-        ach = value
-        from oracle import cpu as ocpu
-        xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
-        t0 = time.perf_counter()
-        qc, sc = ocpu.convrot_quant(xb)
-        acc = ocpu.gemm_s32(qc, wq.cpu().numpy())
-        ocpu.dequant(acc, sc.reshape(-1), ws.cpu().numpy(), bias.cpu().view(torch.int16).numpy().view(np.uint16))
-        cpu_s = time.perf_counter() - t0
-        cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
-               "sample": "the full config-1 linear (activation quant, int32 GEMM, dequant)"}
+        value, unit, bound, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", i8["burst"]
+        x_h, out_h = pin(inp["x"]), torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        x_d = torch.empty_like(x)
+
+        def e2e(_):
+            x_d.copy_(x_h, non_blocking=True)
+            run(x_d, out)
+            out_h.copy_(out, non_blocking=True)
+        io = (nb(x_h), nb(out_h))
+        if cpu_baseline:
+            from oracle import cpu as ocpu
+            xb = inp["x"].view(torch.int16).numpy().view(np.uint16)
+            t0 = time.perf_counter()
+            qc, sc = ocpu.convrot_quant(xb)
+            acc = ocpu.gemm_s32(qc, wq.cpu().numpy())
+            ocpu.dequant(acc, sc.reshape(-1), ws.cpu().numpy(), bias.cpu().view(torch.int16).numpy().view(np.uint16))
+            cpu_s = time.perf_counter() - t0
+            cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+                   "sample": "the full config-1 linear (activation quant, int32 GEMM, dequant)"}
         workload = "cfg1: W8A8 linear, X BF16 [1024,2048] quantised per token (ConvRot256), W [2048,2048] per channel"
+        per_step = ops
     elif cfg == 2:
         inp = synthetic.cfg2()
         m, k = inp["x"].shape
@@ -481,64 +530,116 @@ def run_config(args):
         qs_ = [torch.empty((m, k), dtype=torch.int8, device=dev) for _ in range(sets)]
         ss_ = [torch.empty((m, 1), dtype=torch.float32, device=dev) for _ in range(sets)]
         w, sh, sc, rows = (inp[n].to(dev) for n in ("weight", "shift", "scale", "rows"))
-        import ctypes as ct
 
-        def op(i):
-            rc = lib.h3_norm_quant_run_t(xs[i].data_ptr(), w.data_ptr(), sh.data_ptr(), sc.data_ptr(), rows.data_ptr(),
-                                         qs_[i].data_ptr(), ss_[i].data_ptr(), None, None, None, m, k, 1, k, k, k,
+        def run(xd, q, qs):
+            rc = lib.h3_norm_quant_run_t(xd.data_ptr(), w.data_ptr(), sh.data_ptr(), sc.data_ptr(), rows.data_ptr(),
+                                         q.data_ptr(), qs.data_ptr(), None, None, None, m, k, 1, k, k, k,
                                          ct.c_float(1e-6), 1, 0, st())
             if rc:
                 raise RuntimeError(f"prologue failed: {rc}")
-        ms = _median_ms(op, rotate=sets)
+        ms = _median_ms(lambda i: run(xs[i], qs_[i], ss_[i]), warmup=warmup, iters=iters, rotate=sets)
         nbytes = m * k * 2 + m * k + m * 4 + m * 4 + 3 * k * 2
         value, unit, bound, peak = nbytes / (ms / 1e3) / 1e9, "GB/s", "hbm", hbm_peak
-        ach = value
-        from oracle import cpu as ocpu
-        sample = 512
-        xb = inp["x"][:sample].view(torch.int16).numpy().view(np.uint16)
-        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)
-        t0 = time.perf_counter()
-        ocpu.norm_quant(xb, bits(inp["weight"]), bits(inp["shift"]), bits(inp["scale"]), inp["rows"][:sample].numpy(),
-                        1e-6, threads=threads)
-        cpu_s = (time.perf_counter() - t0) * m / sample
-        cpu = {"value": nbytes / cpu_s / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{sample} of the 6144 rows, scaled to the full shape"}
+        x_h = pin(inp["x"])
+        q_h = torch.empty((m, k), dtype=torch.int8).pin_memory()
+        s_h = torch.empty((m, 1), dtype=torch.float32).pin_memory()
+
+        def e2e(_):
+            xs[0].copy_(x_h, non_blocking=True)
+            run(xs[0], qs_[0], ss_[0])
+            q_h.copy_(qs_[0], non_blocking=True)
+            s_h.copy_(ss_[0], non_blocking=True)
+        io = (nb(x_h), nb(q_h, s_h))
+        if cpu_baseline:
+            from oracle import cpu as ocpu
+            sample = 512
+            xb = inp["x"][:sample].view(torch.int16).numpy().view(np.uint16)
+            bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)
+            t0 = time.perf_counter()
+            ocpu.norm_quant(xb, bits(inp["weight"]), bits(inp["shift"]), bits(inp["scale"]),
+                            inp["rows"][:sample].numpy(), 1e-6, threads=threads)
+            cpu_s = (time.perf_counter() - t0) * m / sample
+            cpu = {"value": nbytes / cpu_s / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": f"{sample} of the 6144 rows, scaled to the full shape"}
         workload = "cfg2: fused prologue, x BF16 [6144,4096], one BF16 table"
+        per_step = nbytes
     else:
         inp = synthetic.cfg3() if cfg == 3 else synthetic.cfg4()
         a, w, xs, ws, bias = (inp[n].to(dev) for n in ("a", "w", "xs", "ws", "bias"))
         m, k = a.shape
         n = w.shape[0]
+        a_h, xs_h = pin(inp["a"]), pin(inp["xs"])
         if cfg == 3:
             out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
             op = lambda _: gemm.int8_linear(a, w, xs, ws, bias=bias, gelu=True, out=out)
+            out_h = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+
+            def e2e(_):
+                a.copy_(a_h, non_blocking=True)
+                xs.copy_(xs_h, non_blocking=True)
+                gemm.int8_linear(a, w, xs, ws, bias=bias, gelu=True, out=out)
+                out_h.copy_(out, non_blocking=True)
+            io = (nb(a_h, xs_h), nb(out_h))
             workload = "cfg3: FC1 INT8 GEMM + GELU-tanh epilogue, [24576,4096] x [16384,4096]^T"
         else:
             res, gate, rows = inp["residual"].to(dev), inp["gate"].to(dev), inp["rows"].to(dev)
             op = lambda _: gemm.int8_gate_residual(a, w, xs, ws, res, gate, rows, bias=bias, requant=True)
+            res_h = pin(inp["residual"])
+            back = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory(),
+                    torch.empty((m, n), dtype=torch.int8).pin_memory(),
+                    torch.empty((m, 1), dtype=torch.float32).pin_memory()]
+
+            def e2e(_):
+                a.copy_(a_h, non_blocking=True)
+                xs.copy_(xs_h, non_blocking=True)
+                res.copy_(res_h, non_blocking=True)
+                r, q, s_ = gemm.int8_gate_residual(a, w, xs, ws, res, gate, rows, bias=bias, requant=True)
+                for h_t, d_t in zip(back, (r, q, s_)):
+                    h_t.copy_(d_t, non_blocking=True)
+            io = (nb(a_h, xs_h, res_h), nb(*back))
             workload = ("cfg4: FC2 INT8 GEMM + in-place gate-residual + ConvRot256/INT8 requant, "
                         "[24576,16384] x [4096,16384]^T")
-        ms = _median_ms(op)
+        ms = _median_ms(op, warmup=warmup, iters=iters)
         ops = 2.0 * m * n * k
-        value, unit, bound, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", int8_peak
-        ach = value
-        sample = 1024
-        t0 = time.perf_counter()
-        torch._int_mm(inp["a"][:sample], inp["w"].t())
-        cpu_s = (time.perf_counter() - t0) * m / sample
-        cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
-               "sample": f"torch._int_mm on {sample} of the {m} rows (int32 GEMM only), scaled to the full shape"}
-    line = {
-        "metric": f"BASELINE config {cfg} ({unit})", "value": value, "unit": unit, "n_gpus": 1, "steps": 100,
-        "warmup": 20, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8", "data": "synthetic", "config": {"workload": workload, "timing": "median of 100 launches",
+        value, unit, bound, peak = ops / (ms / 1e3) / 1e12, "TOPS", "tensor", i8["burst"]
+        if cpu_baseline:
+            sample = 1024
+            t0 = time.perf_counter()
+            torch._int_mm(inp["a"][:sample], inp["w"].t())
+            cpu_s = (time.perf_counter() - t0) * m / sample
+            cpu = {"value": ops / cpu_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+                   "sample": f"torch._int_mm on {sample} of the {m} rows (int32 GEMM only), scaled to the full shape"}
+        per_step = ops
+    e2e_ms = _median_ms(e2e, warmup=2, iters=e2e_iters)
+    scale_unit = 1e12 if unit == "TOPS" else 1e9
+    return {
+        "metric": f"BASELINE config {cfg} ({unit})", "value": value, "unit": unit, "n_gpus": 1, "steps": iters,
+        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic", "config": {"workload": workload, "timing": f"median of {iters} launches",
                                                        "l2": "buffers rotated beyond L2 or larger than L2"},
-        "roofline": {"bound": bound, "achieved": ach, "peak": peak, "unit": "TOPS" if bound == "tensor" else "GB/s",
-                     "frac": ach / peak, "traffic": None,
-                     "peak_source": (f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json" if bound == "tensor"
+        "roofline": {"bound": bound, "achieved": value, "peak": peak, "unit": unit, "frac": value / peak,
+                     "traffic": None,
+                     "peak_source": ("burst INT8: " + i8["burst_source"] if bound == "tensor"
                                      else f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json")},
+        "e2e": {"value": per_step / (e2e_ms / 1e3) / scale_unit, "unit": unit, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": io[0], "d2h_bytes_per_step": io[1],
+                "timing": f"median of {e2e_iters} calls through the op API, copies inside"},
         "cpu_baseline": cpu, "gpu_launches": 2 if cfg in (1, 4) else 1,
     }
+
+
+def run_config(args):
+    """BASELINE configs 1-4 as their own lines (20 warm-up and 100 timed launches,
+    median, buffers rotated beyond L2)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import torch
+
+    from h3_speedkit import _lib
+    torch.cuda.set_device(torch.device("cuda", 0))
+    lib = _lib.load()
+    i8 = int8_peaks(lib, torch.cuda.current_stream().cuda_stream)
+    line = single_op(args.config, lib, i8, cpu_baseline=not args.no_cpu_baseline)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -562,7 +663,6 @@ def run_qkv(args):
     heads, hidden, m = 56, 5376, args.tokens
     n = 3 * heads * 128
     peaks, peak_kind = measured_peaks()
-    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED))
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM))
     threads = host_threads()
     torch.set_num_threads(threads)
@@ -603,6 +703,8 @@ def run_qkv(args):
         return 0
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    i8 = int8_peaks(_lib.load(), torch.cuda.current_stream().cuda_stream)
+    int8_peak = i8["burst"]
     args_dev = tuple(t.to(dev) for t in (q_cpu, w_cpu, xs_cpu, ws_cpu, rope_cpu, qw_cpu, kw_cpu))
     op = QKV()
     clocks = ClockSampler()
@@ -662,7 +764,7 @@ def run_qkv(args):
                        "head_epilogue_and_samples": ms - gemm_ms - vq_ms},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": gemm_tops / int8_peak, "traffic": None,
-                     "peak_source": f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json"},
+                     "peak_source": "burst INT8: " + i8["burst_source"]},
         "roofline_epilogue": {"bound": "hbm", "bytes": epi_bytes,
                               "achieved": epi_bytes / max(1e-9, (ms - gemm_ms - vq_ms) / 1e3) / 1e9,
                               "peak": hbm_peak, "unit": "GB/s",

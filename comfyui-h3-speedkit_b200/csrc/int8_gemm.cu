@@ -32,7 +32,7 @@
 //         kernels/gemm/fc1.cu:83-90 (EVT multiplies, plus 0) and the explicit form
 //         of kernels/gemm/r84_kfourwarp.cu:240-241;
 //   gate: out = bf(__fmaf_rn(y, gate[rows[m]][n], residual[m][n]))
-//         kernels/gemm/gate.cu:172-180, 239-242 and indexed_gate.cuh:85-87;
+//         kernels/gemm/gate.cu:33-41, 100-104 and indexed_gate.cuh:85-87;
 //   GELU: out = bf(gelu_tanh(y)), the formula of convrot64_exact.cuh:913-923.
 #include <cuda.h>
 #include <cuda_bf16.h>

@@ -501,16 +501,22 @@ int launch_heads(const HeadParams& p, int planes, cudaStream_t stream) {
   return e == cudaSuccess ? 1 : record_failure(e, "h3_qkv: head epilogue launch failed");
 }
 
-int qkv_run(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, const void* freqs,
-            const void* qw, const void* kw, float eps, int8_t* QI, float* QS, float* VP, int8_t* KI, float* KS,
-            const void* SK, const int* anchors, int M, int heads, int hidden, float* rrms, cudaStream_t stream,
-            bool sample) {
+// Every host-side check of one QKV call, the GEMM's operand rules included
+// (A, B, D 16-byte aligned; scales 4-byte aligned), so that a caller running
+// several launches can validate all of them before it enqueues the first.
+// Returns 1, or 0 after recording the reason.
+int qkv_check(const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* D, const void* freqs,
+              const void* qw, const void* kw, float eps, const int8_t* QI, const float* QS, const float* VP,
+              const int8_t* KI, const float* KS, const void* SK, const int* anchors, int M, int heads, int hidden,
+              bool sample) {
   if (!A || !B || !xs || !ws || !D || !freqs || !qw || !kw || M < 1 || M > kMaxRows || heads < 1 || hidden < 16 ||
       hidden % 16)
     return record_failure(cudaErrorInvalidValue, "h3_qkv: null operand or shape out of range");
   if (!(eps >= 0.f) || eps > 3.0e38f) return record_failure(cudaErrorInvalidValue, "h3_qkv: eps must be finite and >= 0");
   if (!aligned(D, 16) || !aligned(freqs, 2) || !aligned(qw, 2) || !aligned(kw, 2))
     return record_failure(cudaErrorInvalidValue, "h3_qkv: D must be 16-byte aligned");
+  if (!aligned(A, 16) || !aligned(B, 16) || !aligned(xs, 4) || !aligned(ws, 4))
+    return record_failure(cudaErrorInvalidValue, "h3_qkv: A and B must be 16-byte aligned, xs and ws FP32");
   if (!sample) {
     if (!QI || !QS || !VP || !KI || !KS)
       return record_failure(cudaErrorInvalidValue, "h3_qkv: QI, QS, VP, KI and KS are required");
@@ -519,6 +525,15 @@ int qkv_run(const int8_t* A, const int8_t* B, const float* xs, const float* ws, 
     if ((SK == nullptr) != (anchors == nullptr))
       return record_failure(cudaErrorInvalidValue, "h3_qkv: SK and anchors go together");
   }
+  return 1;
+}
+
+int qkv_run(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, const void* freqs,
+            const void* qw, const void* kw, float eps, int8_t* QI, float* QS, float* VP, int8_t* KI, float* KS,
+            const void* SK, const int* anchors, int M, int heads, int hidden, float* rrms, cudaStream_t stream,
+            bool sample) {
+  if (!qkv_check(A, B, xs, ws, D, freqs, qw, kw, eps, QI, QS, VP, KI, KS, SK, anchors, M, heads, hidden, sample))
+    return 0;
   const int64_t plane = int64_t(heads) * kHead;
   HeadParams p{};
   p.d = static_cast<__nv_bfloat16*>(D);
@@ -667,7 +682,10 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 // Device address of g_scratch on the current device.  In host code the name
 // g_scratch is only a host-side stand-in, so the address is looked up with
 // cudaGetSymbolAddress, once per device, on the first call made with that
-// device current, and cached.
+// device current, and cached for the life of the process.  The cache is not
+// refreshed: after cudaDeviceReset (which destroys the context holding the
+// array) the cached address is stale, so this entry point must not be used
+// after a reset in the same process.
 unsigned char* scratch_base() {
   static std::mutex mu;
   static unsigned char* base[64] = {};
@@ -692,8 +710,13 @@ H3SK_EXPORT int h3_qkv_noalloc(const int8_t* A, const int8_t* B, const float* xs
   using namespace h3sk::qkv;
   if (heads < 1 || heads > kNoAllocMaxHeads || hidden < 16 || hidden > kNoAllocMaxHidden || hidden % 16)
     return h3sk::record_failure(cudaErrorInvalidValue, "h3_qkv_noalloc: heads <= 64 and hidden <= 8192 (hidden % 16 == 0)");
-  if (!A || !xs || !freqs || !VI || !VS || M < 1 || M > kMaxRows)
-    return h3sk::record_failure(cudaErrorInvalidValue, "h3_qkv_noalloc: null operand or M out of range");
+  // All checks of the five steps run here, before the first launch, so that a
+  // rejected call leaves every output untouched.  The sample steps read only
+  // caller operands checked below and the aligned scratch array.
+  if (!qkv_check(A, B, xs, ws, D, freqs, qw, kw, eps, QI, QS, VP, KI, KS, nullptr, nullptr, M, heads, hidden, false))
+    return 0;
+  if (!VI || !VS || !aligned(VI, 4) || !aligned(VS, 4))
+    return h3sk::record_failure(cudaErrorInvalidValue, "h3_qkv_noalloc: VI and VS must be non-null and 4-byte aligned");
   unsigned char* base = scratch_base();
   if (base == nullptr) return h3sk::record_failure(cudaErrorInvalidSymbol, "h3_qkv_noalloc: scratch address");
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

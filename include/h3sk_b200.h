@@ -194,7 +194,7 @@ enum {
 int h3_int8(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M,
             int N, int K, int config, uintptr_t stream);
 /*
- * Replaces h3_int8_gate (kernels/gemm/gate.cu:275-282):
+ * Replaces h3_int8_gate (kernels/gemm/gate.cu:136-143):
  *   D[m, n] = bf16( fmaf( bf16(((acc*xs[m])*ws[n])+0), gate[rows[m]*N + n], residual[m, n] ) )
  *   gate BF16 table [G, N], rows int32 [M], residual BF16 [M, N].  D may equal
  *   residual (in-place update, h3_speedkit/runtime.py:120).  Returns 1 / 0.
@@ -314,7 +314,11 @@ int h3_quant_v(const float* VP, const void* V, void* VI, float* VS, float* VINV,
  * until exit; it bounds heads <= 64 and hidden <= 8192, and larger shapes are
  * rejected with an error (h3_int8_error).  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  Every call writes each
+ * make that first call before any stream capture.  The address is cached for
+ * the life of the process, so the entry point must not be called after a
+ * cudaDeviceReset in the same process (the reset frees the array's context and
+ * leaves the cached address stale).  Every operand is checked before the first
+ * of the five launches, so a rejected call writes no output.  Every call writes each
  * intermediate before reading it, so nothing needs clearing, but all calls on a
  * device share the array: calls that overlap on the GPU race (issue them on one
  * stream, or order them with events).  Returns 1 / 0.

@@ -23,12 +23,22 @@
      * ``ref_gather.so``     kernels/gemm/r82_sample_konly.cu, unmodified, built
        without ``COMFY_HAVE_CUTLASS``: that leaves exactly its sample-row gather
        ``h3_sample_gather`` (the CUTLASS K-only GEMM is compiled out);
-   The reference's INT8 GEMMs (kernels/gemm/fc1.cu, gate.cu, and the fused QKV
-   kernel r84_kfourwarp.cu with its K-only sample form) need the external
-   CUTLASS library and are therefore not built; the GEMM oracle is the exact C
-   restatement (int32 accumulation + IEEE epilogue, reproducible bit for bit).
+     * ``ref_fc1.so``        kernels/gemm/fc1.cu, unmodified (``h3_int8``, the
+       CUTLASS 2.x Sm80 INT8 GEMM with the dequant EVT epilogue), flags
+       ``-DCOMFY_HAVE_CUTLASS -DH3_EVT_STAGES=2``;
+     * ``ref_gate.so``       kernels/gemm/gate.cu, unmodified (``h3_int8_gate``,
+       the gate-residual EVT epilogue, configs 0 and 13), ``-DH3_EVT_STAGES=1``;
+     * ``ref_qkv.so``        kernels/gemm/r84_kfourwarp.cu, unmodified
+       (``h3_qkv_quant_kv``, the QKV GEMM fused with the per-head RMS / RoPE /
+       rotation / quantisation epilogue), ``-DH3_EVT_STAGES=2``.
+   The three GEMM units need CUTLASS headers.  The reference pins CUTLASS 4.5.0
+   (configs/compatibility.json:19); the recipe takes them from ``H3SK_CUTLASS``
+   (a directory holding ``cutlass/cutlass.h``) or else from the copy that the
+   flashinfer wheel ships (``flashinfer/data/cutlass/include``, also 4.5.0), and
+   skips those three libraries with a notice when neither exists.
    Step 2 runs only where the reference checkout exists (the build host); the
-   GPU box uses the prebuilt files.
+   GPU box uses the prebuilt files.  The checkout is ``H3SK_REFERENCE`` or, when
+   that is unset, a directory named ``reference`` beside this repository.
 """
 from __future__ import annotations
 
@@ -41,7 +51,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("H3SK_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("H3SK_REFERENCE") or HERE.parent.parent / "reference")
 C_LIB = HERE / "libh3_oracle.so"
 NORM_WIDTHS = (2048, 4096, 5376)
 RESIDUAL_WIDTHS = (4096, 5376)
@@ -144,7 +154,61 @@ def build_ref(force: bool = False) -> list[Path]:
     if force or not _newer(target, launcher, vendor / "convrot64_exact.cuh"):
         _compile(nvcc, launcher, target, [vendor], ["--use_fast_math"])
     built.append(target)
+    built += _build_ref_gemms(nvcc, gemm_dir, force)
     return built
+
+
+# (library, source in kernels/gemm, the reference's flags for it: tools/build_kernels.py:35-39)
+REF_GEMMS = (("ref_fc1.so", "fc1.cu", ["-DCOMFY_HAVE_CUTLASS", "-DH3_EVT_STAGES=2"]),
+             ("ref_gate.so", "gate.cu", ["-DCOMFY_HAVE_CUTLASS", "-DH3_EVT_STAGES=1"]),
+             ("ref_qkv.so", "r84_kfourwarp.cu", ["-DCOMFY_HAVE_CUTLASS", "-DH3_EVT_STAGES=2"]))
+
+
+def cutlass_include() -> Path | None:
+    """CUTLASS headers for the reference GEMM units: ``H3SK_CUTLASS`` or flashinfer's copy."""
+    env = os.environ.get("H3SK_CUTLASS")
+    candidates = [Path(env)] if env else []
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("flashinfer")
+        if spec and spec.submodule_search_locations:
+            candidates += [Path(p) / "data" / "cutlass" / "include" for p in spec.submodule_search_locations]
+    except (ImportError, ValueError):
+        pass
+    for c in candidates:
+        if (c / "cutlass" / "cutlass.h").is_file():
+            return c
+    return None
+
+
+def _build_ref_gemms(nvcc: str, gemm_dir: Path, force: bool) -> list[Path]:
+    """Compile fc1.cu, gate.cu and r84_kfourwarp.cu in parallel (each takes about a minute)."""
+    todo = [(REF_OUT / name, gemm_dir / src, extra) for name, src, extra in REF_GEMMS
+            if force or not _newer(REF_OUT / name, gemm_dir / src, gemm_dir / "cutlass_gemm_common.cuh")]
+    done = [REF_OUT / name for name, _, _ in REF_GEMMS if (REF_OUT / name).exists()]
+    if not todo:
+        return done
+    include = cutlass_include()
+    if include is None:
+        print("oracle: CUTLASS headers not found (set H3SK_CUTLASS); reference GEMM oracles not built",
+              file=sys.stderr)
+        return [p for p in done if p not in {t for t, _, _ in todo}]
+    procs = []
+    for target, source, extra in todo:
+        tmp = target.with_suffix(".so.tmp")
+        cmd = [nvcc, *REF_FLAGS, *extra, f"-I{include}", f"-I{gemm_dir}", str(source), "-o", str(tmp)]
+        procs.append((target, tmp, source, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                                                            text=True)))
+    failures = []
+    for target, tmp, source, proc in procs:
+        _, err = proc.communicate()
+        if proc.returncode:
+            failures.append(f"{source.name}:\n{err[-4000:]}")
+        else:
+            os.replace(tmp, target)
+    if failures:
+        raise RuntimeError("reference GEMM oracle build failed for " + "\n".join(failures))
+    return [REF_OUT / name for name, _, _ in REF_GEMMS]
 
 
 def build(force: bool = False) -> None:

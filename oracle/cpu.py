@@ -207,7 +207,7 @@ def dequant(acc, xs, ws, bias=None, *, gelu=False, threads=None) -> np.ndarray:
 
 
 def gate_residual(acc, xs, ws, gate, rows, residual, bias=None, threads=None) -> np.ndarray:
-    """bf(fmaf(bf(dequant), gate[rows[m]], residual)) -> BF16 bits (gate.cu:172-180, 239-242)."""
+    """bf(fmaf(bf(dequant), gate[rows[m]], residual)) -> BF16 bits (gate.cu:33-41, 100-104)."""
     acc = _c(acc, np.int32)
     m, n = acc.shape
     gate = _c(gate, np.uint16)

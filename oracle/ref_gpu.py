@@ -2,8 +2,9 @@
 
 Loads the libraries ``oracle/build.py`` compiled into ``oracle/_ref`` from the
 reference sources (norm_quant.cu, residual_quant.cu, convrot_register_v2.cu, the
-vendored Kitchen quantiser, the K anchor detector and the sample-row gather) and
-runs them on torch CUDA tensors.  Output buffers are
+vendored Kitchen quantiser, the K anchor detector, the sample-row gather, and the
+CUTLASS GEMMs fc1.cu, gate.cu and r84_kfourwarp.cu) and runs them on torch CUDA
+tensors.  Output buffers are
 allocated by the caller-side helpers here with torch; nothing in the product
 path uses this module.
 """
@@ -156,3 +157,61 @@ def sample_gather(q, xs, rope):
           _stream(q)) != 1:
         raise RuntimeError("reference h3_sample_gather launch failed")
     return sq, sx, sr
+
+
+def int8(a, b, xs, ws, *, config=3):
+    """Reference h3_int8 (fc1.cu:119-138): D = bf(((acc * xs[m]) * ws[n]) + 0), the
+    CUTLASS Sm80 INT8 GEMM; config 3 is the one the runtime uses (runtime.py:155-156)."""
+    import torch
+    fn = _load("ref_fc1.so").h3_int8
+    fn.argtypes = [ct.c_void_p] * 5 + [ct.c_int] * 4 + [ct.c_size_t]
+    fn.restype = ct.c_int
+    m, k = a.shape
+    n = b.shape[0]
+    d = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    if fn(a.data_ptr(), b.data_ptr(), xs.data_ptr(), ws.data_ptr(), d.data_ptr(), m, n, k, config,
+          _stream(a)) != 1:
+        raise RuntimeError(f"reference h3_int8 (config {config}) refused or failed")
+    return d
+
+
+def int8_gate(a, b, xs, ws, gate, rows, residual, *, config=13, out=None):
+    """Reference h3_int8_gate (gate.cu:136-143): D = bf(fmaf(bf(acc*xs*ws + 0),
+    gate[rows[m], n], residual[m, n])).  ``out`` may be ``residual`` itself (the
+    runtime's in-place call, runtime.py:117-124); by default D is a new tensor."""
+    import torch
+    fn = _load("ref_gate.so").h3_int8_gate
+    fn.argtypes = [ct.c_void_p] * 8 + [ct.c_int] * 4 + [ct.c_size_t]
+    fn.restype = ct.c_int
+    m, k = a.shape
+    n = b.shape[0]
+    d = torch.empty((m, n), dtype=torch.bfloat16, device=a.device) if out is None else out
+    if fn(a.data_ptr(), b.data_ptr(), xs.data_ptr(), ws.data_ptr(), d.data_ptr(), gate.data_ptr(),
+          rows.data_ptr(), residual.data_ptr(), m, n, k, config, _stream(a)) != 1:
+        raise RuntimeError(f"reference h3_int8_gate (config {config}) refused or failed")
+    return d
+
+
+def qkv_quant_kv(a, b, xs, ws, freqs, qw, kw, eps, sk, anchors):
+    """Reference h3_qkv_quant_kv (r84_kfourwarp.cu:213-388): the H3 QKV GEMM
+    (56 heads x 128, hidden 5376) fused with per-head RMS, RoPE, the Q/K rotation
+    and quantisation and the V tile maxima.  Returns dict d, qi, qs, ki, ks, vp
+    in the layouts of the reference's own call (ops/qkv.py:63-69)."""
+    import torch
+    fn = _load("ref_qkv.so").h3_qkv_quant_kv
+    fn.argtypes = [ct.c_void_p] * 8 + [ct.c_float] + [ct.c_void_p] * 7 + [ct.c_int, ct.c_size_t]
+    fn.restype = ct.c_int
+    m = a.shape[0]
+    heads, dev = 56, a.device
+    parts = (m + 127) // 128
+    t = {"d": torch.empty((3, heads, m, 128), dtype=torch.bfloat16, device=dev),
+         "qi": torch.empty((heads, m, 128), dtype=torch.int8, device=dev),
+         "ki": torch.empty((heads, m, 128), dtype=torch.int8, device=dev),
+         "qs": torch.empty((heads, parts * 32), dtype=torch.float32, device=dev),
+         "ks": torch.empty((heads, parts * 4), dtype=torch.float32, device=dev),
+         "vp": torch.empty((heads, parts, 128), dtype=torch.float32, device=dev)}
+    if fn(a.data_ptr(), b.data_ptr(), xs.data_ptr(), ws.data_ptr(), t["d"].data_ptr(), freqs.data_ptr(),
+          qw.data_ptr(), kw.data_ptr(), float(eps), t["qi"].data_ptr(), t["qs"].data_ptr(), t["vp"].data_ptr(),
+          t["ki"].data_ptr(), t["ks"].data_ptr(), sk.data_ptr(), anchors.data_ptr(), m, _stream(a)) != 1:
+        raise RuntimeError("reference h3_qkv_quant_kv refused or failed")
+    return t

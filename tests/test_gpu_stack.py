@@ -232,18 +232,47 @@ def test_runtime_backend_block_matches_the_block_plan(device, skip):
     assert torch.equal(via_runtime, via_plan)
 
 
+_GELU_TABLE = {}
+
+
+def _gelu_table(device):
+    """bf(gelu_tanh(v)) for all 65536 BF16 patterns v, from the CPU restatement of
+    Kitchen's GELU (convrot64_exact.cuh:913-923).  The reference has GELU only as a
+    quantiser input act, never after a GEMM, so the FC1 GELU step of the chain is
+    this table; its input comes from the reference's own fc1 kernel."""
+    if device not in _GELU_TABLE:
+        from oracle import cpu as ocpu
+        bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+        n = 1 << 16
+        out = ocpu.dequant(np.zeros((1, n), np.int32), np.ones(1, np.float32), np.ones(n, np.float32), bits,
+                           gelu=True)[0]
+        _GELU_TABLE[device] = torch.from_numpy(out.view(np.int16).copy()).to(device)
+    return _GELU_TABLE[device]
+
+
+def _apply_gelu_table(h, chunk=8192):
+    table = _gelu_table(h.device)
+    flat = h.view(torch.int16)
+    for lo in range(0, h.shape[0], chunk):
+        part = flat[lo:lo + chunk]
+        part.copy_(table[part.to(torch.int32) & 0xFFFF])
+    return h
+
+
 def _reference_kernel_chain(x, blocks, rows, eps=1e-6):
-    """The block chain with every row kernel replaced by the reference's own
-    (norm_quant.cu, the Kitchen quantiser, compiled into oracle/_ref) and the
-    GEMMs by this build's (int32 accumulation and IEEE epilogue, pinned exact by
-    tests/test_gpu_gemm.py).  x is updated in place."""
-    from h3_speedkit.ops import gemm
+    """The block chain built only from the reference's own kernels, compiled from
+    its sources into oracle/_ref: norm_quant.cu for the prologues, fc1.cu
+    (``h3_int8``, config 3) for the QKV and FC1 GEMMs, the register ConvRot or
+    the Kitchen quantiser for V and the FC2 input, gate.cu (``h3_int8_gate``,
+    Stream-K config 13, in place) for outproj and FC2.  The one step the
+    reference has no kernel for, FC1's GELU after the dequant (cfg3/cfg5), is
+    the CPU restatement's exhaustive BF16 table.  x is updated in place."""
     from oracle import ref_gpu
     for b in blocks:
         attn = b.qkv.shape[0] // 3
         swiglu = b.fc1.shape[0] == 2 * b.fc2.shape[1]
         q, qs = ref_gpu.norm_quant(x, b.norm1, b.shift_msa, b.scale_msa, rows, eps)
-        qkv = gemm.int8_linear(q, b.qkv, qs.view(-1), b.qkv_s)
+        qkv = ref_gpu.int8(q, b.qkv, qs.view(-1), b.qkv_s)
         v = qkv[:, 2 * attn:].contiguous()
         del qkv
         if attn in (5376, 7168):   # the reference's register quantiser (runtime.py:144-146)
@@ -251,12 +280,14 @@ def _reference_kernel_chain(x, blocks, rows, eps=1e-6):
             as_ = as_.view(-1)
         else:
             aq, as_ = ref_gpu.kitchen_quant(v, 0)
-        gemm.int8_gate_residual(aq, b.out, as_, b.out_s, x, b.gate_msa, rows)
+        ref_gpu.int8_gate(aq, b.out, as_.view(-1), b.out_s, b.gate_msa, rows, x, out=x)
         q, qs = ref_gpu.norm_quant(x, b.norm2, b.shift_mlp, b.scale_mlp, rows, eps)
-        h = gemm.int8_linear(q, b.fc1, qs.view(-1), b.fc1_s, gelu=not swiglu)
+        h = ref_gpu.int8(q, b.fc1, qs.view(-1), b.fc1_s)
+        if not swiglu:
+            _apply_gelu_table(h)
         hq, hs = ref_gpu.kitchen_quant(h, 2 if swiglu else 0)
         del h
-        gemm.int8_gate_residual(hq, b.fc2, hs, b.fc2_s, x, b.gate_mlp, rows)
+        ref_gpu.int8_gate(hq, b.fc2, hs.view(-1), b.fc2_s, b.gate_mlp, rows, x, out=x)
     return x
 
 
@@ -265,7 +296,7 @@ def test_h3_geometry_stack_against_reference_kernels(device):
     adaLN table rows): two blocks on 8192 tokens equal, bit for bit, the chain
     built from the reference's own row kernels (its K=5376 prologue, register
     ConvRot quantiser for the 7168-wide attention output, Kitchen SwiGLU
-    quantiser) and the pinned GEMMs."""
+    quantiser) and its own CUTLASS GEMMs (fc1.cu, gate.cu)."""
     g = synthetic.H3_GEOMETRY
     m = 8192
     blocks = [synthetic.cfg5_block(i, g["d"], g["ffn"], tables=2, device=device, attn=g["attn"], swiglu=True)
@@ -283,7 +314,8 @@ def test_cfg5_full_size_against_reference_kernels(device):
     """The benchmark workload itself (8 blocks, D=4096, FFN=16384, M=98304, the
     bench's device-drawn weights and tokens):
       * every one of the 98304 output rows equals, bit for bit, the same chain
-        built from the reference's own row kernels;
+        built from the reference's own kernels (row kernels and CUTLASS GEMMs;
+        FC1's GELU from the CPU restatement's BF16 table);
       * 24 sampled rows of the full run equal the same rows run on their own
         (row locality at full size, the basis of token sharding);
       * those rows match the CPU restatement of the 8-block chain within a

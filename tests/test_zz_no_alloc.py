@@ -89,3 +89,76 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
         assert lib.h3_qkv_noalloc(16, 16, 16, 16, 16, 16, 16, 16, eps, 16, 16, 16, 16, 16, 16, 16, 100, heads,
                                   hidden, 0) == 0
         assert b"h3_qkv_noalloc" in lib.h3_int8_error()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fault", ["B", "D", "KS", "VI_misaligned", "xs_misaligned"])
+def test_noalloc_rejects_before_any_launch(device, fault):
+    """A call with one bad operand (a null weight, output or scale buffer, or a
+    misaligned one) is rejected on the host before the first of its five
+    launches: it returns 0 and every sentinel-filled output stays as it was."""
+    m, heads, hidden = 300, 2, 256
+    q, w, xs, ws, rope, qw, kw = _inputs(m, heads, hidden, 77, device, 0.5)
+    parts = (m + 127) // 128
+    out = {
+        "d": torch.full((3, heads, m, 128), -1, dtype=torch.int16, device=device).view(torch.bfloat16),
+        "qi": torch.full((heads, m, 128), 7, dtype=torch.int8, device=device),
+        "ki": torch.full((heads, m, 128), 7, dtype=torch.int8, device=device),
+        "qs": torch.full((heads, parts * 32), -1.0, device=device),
+        "ks": torch.full((heads, parts * 4), -1.0, device=device),
+        "vp": torch.full((heads, parts, 128), -1.0, device=device),
+        "vi": torch.full((heads * 128 * parts * 128 + 16,), 7, dtype=torch.int8, device=device),
+        "vs": torch.full((heads * 128,), -1.0, device=device),
+    }
+    keep = {k: v.clone() for k, v in out.items()}
+    xs_big = torch.zeros((m + 4,), device=device)
+    xs_big[1:m + 1] = xs.view(-1)
+    p = {k: v.data_ptr() for k, v in out.items()}
+    b_ptr = None if fault == "B" else w.data_ptr()
+    if fault == "D":
+        p["d"] = None
+    if fault == "KS":
+        p["ks"] = None
+    if fault == "VI_misaligned":
+        p["vi"] += 1
+    xs_ptr = xs_big.data_ptr() + 4 if fault == "xs_misaligned" else xs.data_ptr()
+    if fault == "xs_misaligned":
+        xs_ptr += 2   # FP32 scales two bytes off their alignment
+    torch.cuda.synchronize()
+    lib = _lib.load()
+    rc = lib.h3_qkv_noalloc(q.data_ptr(), b_ptr, xs_ptr, ws.data_ptr(), p["d"], rope.data_ptr(), qw.data_ptr(),
+                            kw.data_ptr(), ct.c_float(1e-6), p["qi"], p["qs"], p["vp"], p["ki"], p["ks"], p["vi"],
+                            p["vs"], m, heads, hidden, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert lib.h3_int8_last_error() != 0 and lib.h3_int8_error()
+    for k in out:
+        assert _same(out[k], keep[k]), f"{k} was written by a rejected call"
+
+
+@pytest.mark.parametrize("fault", ["B", "D", "KS", "VI_misaligned", "xs_misaligned", "A_misaligned", "eps"])
+def test_noalloc_checks_run_before_any_cuda_call(fault):
+    """The same rejections with stand-in pointer values on any host: each one is
+    caught by a validation message before the entry point makes its first CUDA
+    call (an accepted call would go on to look up the scratch address and, with
+    no GPU, fail with a different message)."""
+    lib = _lib.load()
+    ptr = {k: 0x10000 * (i + 1) for i, k in enumerate(
+        ("A", "B", "xs", "ws", "D", "freqs", "qw", "kw", "QI", "QS", "VP", "KI", "KS", "VI", "VS"))}
+    eps = 1e-6
+    if fault in ("B", "D", "KS"):
+        ptr[fault] = None
+    elif fault == "VI_misaligned":
+        ptr["VI"] += 1
+    elif fault == "xs_misaligned":
+        ptr["xs"] += 2
+    elif fault == "A_misaligned":
+        ptr["A"] += 8
+    else:
+        eps = float("nan")
+    rc = lib.h3_qkv_noalloc(ptr["A"], ptr["B"], ptr["xs"], ptr["ws"], ptr["D"], ptr["freqs"], ptr["qw"], ptr["kw"],
+                            ct.c_float(eps), ptr["QI"], ptr["QS"], ptr["VP"], ptr["KI"], ptr["KS"], ptr["VI"],
+                            ptr["VS"], 300, 2, 256, 0)
+    assert rc == 0
+    msg = lib.h3_int8_error().decode()
+    assert "scratch address" not in msg and ("h3_qkv" in msg), msg

@@ -1,9 +1,9 @@
 """Preallocated, current-stream bindings of the ConvRot256 INT8 quantiser (B200).
 
-``ConvRotRegister`` is the drop-in for h3_speedkit/ops/convrot.py of H3 SpeedKit
+``ConvRotRegister`` stands in for h3_speedkit/ops/convrot.py of H3 SpeedKit
 (:39-111): same modes (0 production, 1 diagnostic, 2 rotation oracle), same
-validation and error behaviour, any K % 256 == 0 up to 16384 (reference: 5376
-and 7168) on a B200.
+error texts and error behaviour, any K % 256 == 0 up to 16384 (reference: 5376
+and 7168) on a B200.  Its operand checks are a rule table (see ``_contract``).
 
 ``quantize_int8_rowwise_convrot64`` replaces the Kitchen call the reference's
 block makes for the FC2 input, ``cuda.quantize_int8_rowwise_convrot64(hidden,
@@ -17,12 +17,14 @@ import ctypes as ct
 import torch
 
 from .. import _lib
+from ._contract import INT32_MAX, Call, Launch, Rule, all_finite, enforce, first_overlap
 from .norm_quant import DEVICE_CAPABILITY, MAX_K
 
 ACT_CODES = {None: 0, 'none': 0, 'gelu_tanh': 1, 'gelu': 1, 'swiglu': 2}
 
 
 class Resources(ct.Structure):
+    """h3_convrot_register_query's report (field order of convrot_register_v2.cu:140-144)."""
     _fields_ = [(n, ct.c_int64) for n in (
         'abi', 'bytes', 'k', 'threads', 'warps', 'num_regs', 'static_shared_bytes',
         'local_bytes', 'max_threads_per_block', 'active_blocks_per_sm',
@@ -32,25 +34,60 @@ class Resources(ct.Structure):
 def finite_bounded(x, rows=128):
     if rows < 1:
         raise ValueError('finite-check row chunk must be positive')
-    for start in range(0, x.shape[0], rows):
-        if not bool(torch.isfinite(x[start:start + rows]).all().item()):
-            raise ValueError('NaN/Inf lies outside this finite-input replay contract')
+    if not all_finite(x, rows):
+        raise ValueError('NaN/Inf lies outside this finite-input replay contract')
 
 
-def _validate(t, shape, dtype, device, name):
-    if (not isinstance(t, torch.Tensor) or tuple(t.shape) != tuple(shape) or t.dtype != dtype
-            or not t.is_cuda or t.device != device or not t.is_contiguous()):
-        raise ValueError(f'{name} requires contiguous {dtype} {tuple(shape)} on {device}')
-    if t.data_ptr() % t.element_size():
-        raise ValueError(f'{name} is not element-aligned')
+def _buffer_rules(name, shape, dtype):
+    """A dense, element-aligned CUDA buffer `name` of `dtype` and shape(call) on x's device."""
+    def placed(c):
+        t = c[name]
+        return (isinstance(t, torch.Tensor) and tuple(t.shape) == tuple(shape(c)) and t.dtype == dtype
+                and t.is_cuda and t.device == c['x'].device and t.is_contiguous())
+    return [Rule(placed, lambda c: f"{name} requires contiguous {dtype} {tuple(shape(c))} on {c['x'].device}"),
+            Rule(lambda c: c[name].data_ptr() % c[name].element_size() == 0, f'{name} is not element-aligned')]
 
 
-def _no_alias(tensors):
-    spans = sorted((t.data_ptr(), t.data_ptr() + t.numel() * t.element_size(), n)
-                   for n, t in tensors if t is not None)
-    for left, right in zip(spans, spans[1:]):
-        if left[1] > right[0]:
-            raise ValueError(f'Overlapping buffers: {left[2]} and {right[2]}')
+def _when(pred, rules):
+    return [Rule(lambda c, r=r: not pred(c) or r.ok(c), r.message) for r in rules]
+
+
+def _x_dims(c):
+    x = c['x']
+    if not (isinstance(x, torch.Tensor) and x.is_cuda and x.dtype == torch.bfloat16 and x.ndim == 2
+            and x.is_contiguous()):
+        return False
+    c.dims.update(m=x.shape[0], k=x.shape[1])
+    return True
+
+
+_MK = lambda c: (c.dims['m'], c.dims['k'])
+_M1 = lambda c: (c.dims['m'], 1)
+
+RULES = [
+    Rule(_x_dims, 'X requires contiguous CUDA BF16 [M,K]'),
+    Rule(lambda c: 1 <= c.dims['m'] <= INT32_MAX and c.dims['k'] % 256 == 0 and 256 <= c.dims['k'] <= MAX_K
+         and c.dims['act_code'] == 0,
+         f'Only M=1..INT32_MAX, K%256==0 (<= {MAX_K}), ACT=none is supported'),
+    Rule(lambda c: c.dims['mode'] in (0, 1, 2), 'Mode must be production=0, diagnostic=1 or oracle=2'),
+    *_buffer_rules('x', _MK, torch.bfloat16),
+    Rule(lambda c: c['x'].data_ptr() % 16 == 0, 'x must be 16-byte aligned'),
+    *_when(lambda c: c.dims['mode'] != 2,
+           _buffer_rules('q', _MK, torch.int8) + _buffer_rules('scale', _M1, torch.float32)),
+    Rule(lambda c: c.dims['mode'] != 2 or (c['q'] is None and c['scale'] is None),
+         'Oracle mode accepts only X and rotated output'),
+    *_when(lambda c: c.dims['mode'] != 0, _buffer_rules('rotated', _MK, torch.float32)),
+    Rule(lambda c: c.dims['mode'] != 0 or c['rotated'] is None, 'Production mode does not accept rotated output'),
+]
+
+
+def _disjoint(c):
+    """Every present buffer must own its bytes (x included: it is never written,
+    but an output over it would be read after it is written)."""
+    bufs = [(n, c[n]) for n in ('x', 'q', 'scale', 'rotated') if c[n] is not None]
+    hit = first_overlap([], bufs)
+    if hit is not None:
+        raise ValueError(f'Overlapping buffers: {hit[1]} and {hit[0]}')
 
 
 def _check_device(device):
@@ -60,6 +97,8 @@ def _check_device(device):
 
 
 class ConvRotRegister:
+    """ctypes front of h3_convrot_register_* (libh3sk_b200.so)."""
+
     def __init__(self, library=None):
         self.lib = _lib.load(library)
         if self.lib.h3_convrot_register_resources_size() != ct.sizeof(Resources):
@@ -70,59 +109,30 @@ class ConvRotRegister:
             raise RuntimeError(f'ConvRot CUDA error {code}: ' + self.lib.h3_convrot_register_error(code).decode())
 
     def query(self, k):
-        resource = Resources()
-        self.check(self.lib.h3_convrot_register_query(k, ct.byref(resource), ct.sizeof(resource)))
-        values = {n: int(getattr(resource, n)) for n, _ in resource._fields_}
+        report = Resources()
+        self.check(self.lib.h3_convrot_register_query(k, ct.byref(report), ct.sizeof(report)))
+        values = {n: int(getattr(report, n)) for n, _ in report._fields_}
         values['active_warps_per_sm'] = values['active_blocks_per_sm'] * values['warps']
         values['theoretical_occupancy'] = (values['active_blocks_per_sm'] * values['threads']
                                            / values['max_threads_per_sm'])
         return values
 
     def bind(self, x, q=None, scale=None, *, rotated=None, mode=0, act_code=0, check_finite=True):
-        if (not isinstance(x, torch.Tensor) or not x.is_cuda or x.dtype != torch.bfloat16
-                or x.ndim != 2 or not x.is_contiguous()):
-            raise ValueError('X requires contiguous CUDA BF16 [M,K]')
-        m, k = x.shape
-        if m < 1 or m > 0x7fffffff or k % 256 or not 256 <= k <= MAX_K or act_code != 0:
-            raise ValueError(f'Only M=1..INT32_MAX, K%256==0 (<= {MAX_K}), ACT=none is supported')
-        if mode not in (0, 1, 2):
-            raise ValueError('Mode must be production=0, diagnostic=1 or oracle=2')
-        _validate(x, (m, k), torch.bfloat16, x.device, 'x')
-        if x.data_ptr() % 16:
-            raise ValueError('x must be 16-byte aligned')
-        if mode != 2:
-            _validate(q, (m, k), torch.int8, x.device, 'q')
-            _validate(scale, (m, 1), torch.float32, x.device, 'scale')
-        elif q is not None or scale is not None:
-            raise ValueError('Oracle mode accepts only X and rotated output')
-        if mode != 0:
-            _validate(rotated, (m, k), torch.float32, x.device, 'rotated')
-        elif rotated is not None:
-            raise ValueError('Production mode does not accept rotated output')
-        _no_alias([('x', x), ('q', q), ('scale', scale), ('rotated', rotated)])
+        call = Call({'x': x, 'q': q, 'scale': scale, 'rotated': rotated}, {'mode': mode, 'act_code': act_code})
+        enforce(RULES, call)
+        _disjoint(call)
         _check_device(x.device)
         if check_finite:
             finite_bounded(x)
-        return Bound(self, x, q, scale, rotated, mode, self.query(k))
+        launch = Bound(self.lib.h3_convrot_register_run, x.device,
+                       [None if t is None else t.data_ptr() for t in (x, q, scale, rotated)] + [*x.shape, mode],
+                       (x, q, scale, rotated), (q, scale, rotated),
+                       rotated if mode == 2 else (q, scale), self.check)
+        launch.mode, launch.resources = mode, self.query(x.shape[1])
+        return launch
 
 
-class Bound:
-    """Owns tensor refs and records allocator stream use; caller orders producers."""
-
-    def __init__(self, library, x, q, scale, rotated, mode, resources):
-        self.library, self.x, self.q, self.scale = library, x, q, scale
-        self.rotated, self.mode, self.resources = rotated, mode, resources
-        self.owners = tuple(t for t in (x, q, scale, rotated) if t is not None)
-        self.pointers = tuple(t.data_ptr() if t is not None else None for t in (x, q, scale, rotated))
-
-    def __call__(self):
-        with torch.cuda.device(self.x.device):
-            stream = torch.cuda.current_stream(self.x.device)
-            for owner in self.owners:
-                owner.record_stream(stream)
-            self.library.check(self.library.lib.h3_convrot_register_run(
-                *self.pointers, *self.x.shape, self.mode, stream.cuda_stream))
-        return self.rotated if self.mode == 2 else (self.q, self.scale)
+Bound = Launch
 
 
 def quantize_int8_rowwise_convrot64(x, groupsize=256, input_act=None, *, out=None, out_scale=None):

@@ -1,89 +1,87 @@
 """Preallocated, current-stream binding of the fused residual prologue (B200).
 
 x <- bf(fma(branch, bf(gate[rows]), x)) in place, then RMSNorm -> adaLN
-x*(1+scale)+shift -> ConvRot256 -> per-token INT8 of the updated rows, one pass.
-Drop-in for h3_speedkit/ops/residual_quant.py of H3 SpeedKit: the same class and
-function names, argument meaning, validation messages and error behaviour
-(``validate`` at :57-112, ``ResidualQuant`` at :115-153, ``Bound`` at :156-171),
-with the differences of ``ops.norm_quant``: K is taken from ``x`` (any
-K % 256 == 0 up to 16384, reference: 5376 only) and the device must be a B200.
+x*(1+scale)+shift -> ConvRot256 -> per-token INT8 of the updated rows, one pass,
+through ``h3_residual_quant_run_t``.  Stands in for
+h3_speedkit/ops/residual_quant.py of H3 SpeedKit: the public names, argument
+meaning and error texts are that module's (:57-171); the checks are a rule table
+built from ``ops.norm_quant``'s (see ``_contract``), with the same two deliberate
+differences: K is read off ``x`` (any K % 256 == 0 up to 16384; reference: 5376)
+and the device must be a B200.
 
-X is both an input and the in-place output; the bound object owns the Torch
-tensors; rows are immutable after validation.  Returned q/q_scale are the
+x is both an input and the in-place output.  Returned q / q_scale are the
 prequantised Linear input.
 """
 from __future__ import annotations
 
 import ctypes as ct
-import math
 
 import torch
 
 from .. import _lib
-from .norm_quant import DEVICE_CAPABILITY, K, MAX_K, Resources, check_disjoint, finite_bounded, span
+from ._contract import INT32_MAX, Call, Launch, Rule, common_rules, debug_rule, dense_rule, disjoint_rule, enforce
+from . import norm_quant as nq
+from .norm_quant import (DEVICE_CAPABILITY, K, MAX_K, Resources, check_disjoint, finite_bounded,  # noqa: F401
+                         require_device, span)
 
 __all__ = ["K", "Resources", "span", "check_disjoint", "finite_bounded", "validate", "ResidualQuant", "Bound"]
+
+INPUTS = ('branch', 'weight', 'gate', 'shift', 'scale', 'rows')
+OUTPUTS = ('x', 'q', 'q_scale', 'debug_norm', 'debug_rotated', 'debug_rstd')
+
+
+def _x_kind_ok(c):
+    x = c['x']
+    if x.dtype != torch.bfloat16 or x.ndim != 2:
+        return False
+    c.dims.update(m=x.shape[0], k=x.shape[1])
+    return True
+
+
+def _x_ok(c):
+    x, (m, k) = c['x'], (c.dims['m'], c.dims['k'])
+    return k % 256 == 0 and 256 <= k <= MAX_K and 1 <= m <= INT32_MAX and x.is_contiguous() and x.data_ptr() % 8 == 0
+
+
+def _branch_ok(c):
+    b, x = c['branch'], c['x']
+    return b.shape == x.shape and b.dtype == torch.bfloat16 and b.is_contiguous() and b.data_ptr() % 8 == 0
+
+
+RULES = [
+    debug_rule(),
+    *common_rules('x'),
+    Rule(_x_kind_ok, 'X requires aligned contiguous BF16 [M,K]'),
+    Rule(_x_ok, lambda c: f"X requires aligned contiguous BF16 [M,{c.dims['k']}]"),
+    Rule(_branch_ok, lambda c: f"Branch requires aligned contiguous BF16 [M,{c.dims['k']}]"),
+    dense_rule('weight', lambda c: (c.dims['k'],), torch.bfloat16, 8),
+    Rule(lambda c: nq._tables_ok(c) and c['shift'].shape[0] <= INT32_MAX,
+         lambda c: f"Tables require matching nonempty FP32/BF16 [T,{c.dims['k']}]"),
+    Rule(lambda c: c['gate'].shape == c['shift'].shape and c['gate'].dtype in (torch.bfloat16, torch.float32),
+         'Gate requires matching table shape and independent FP32/BF16 dtype'),
+    Rule(lambda c: nq._table_rows_ok(c, ('gate', 'shift', 'scale')),
+         'Tables require dense hidden axes and nonoverlapping rows'),
+    dense_rule('rows', lambda c: (c.dims['m'],), torch.int32, 4),
+    dense_rule('q', lambda c: (c.dims['m'], c.dims['k']), torch.int8, 8),
+    dense_rule('q_scale', lambda c: (c.dims['m'], 1), torch.float32, 4),
+    *nq._debug_rules(),
+    Rule(lambda c: nq.normal_fp32(c.dims['eps']), 'Epsilon must be finite, positive, normal FP32'),
+    disjoint_rule(INPUTS, OUTPUTS),
+    *nq._value_rules('shift', ('x', 'branch', 'weight', 'gate', 'shift', 'scale')),
+]
 
 
 def validate(x, branch, weight, gate, shift, scale, rows, q, q_scale, *, eps,
              debug_norm=None, debug_rotated=None, debug_rstd=None,
              check_values=True, require_cuda=True):
-    """Metadata checks; runnable on CPU tensors with require_cuda=False."""
-    inputs = [('branch', branch), ('weight', weight), ('gate', gate), ('shift', shift), ('scale', scale),
-              ('rows', rows)]
-    outputs = [('x', x), ('q', q), ('q_scale', q_scale)]
-    debug = (debug_norm, debug_rotated, debug_rstd)
-    if any(t is not None for t in debug):
-        if any(t is None for t in debug):
-            raise ValueError('Debug requires norm, rotated, and rstd outputs together')
-        outputs.extend(zip(('debug_norm', 'debug_rotated', 'debug_rstd'), debug))
-    if any(type(t) is not torch.Tensor for _, t in inputs + outputs):
-        raise ValueError('All operands must be original plain Torch tensors')
-    if (require_cuda and not x.is_cuda) or any(t.device != x.device for _, t in inputs + outputs):
-        raise ValueError('All operands must use one CUDA device')
-    if any(t.requires_grad for _, t in inputs + outputs):
-        raise ValueError('Inference only; detach only after validating model autograd policy')
-    if x.dtype != torch.bfloat16 or x.ndim != 2:
-        raise ValueError('X requires aligned contiguous BF16 [M,K]')
-    m, k = x.shape
-    if (k % 256 or not 256 <= k <= MAX_K or not 1 <= m <= 0x7fffffff or not x.is_contiguous()
-            or x.data_ptr() % 8):
-        raise ValueError(f'X requires aligned contiguous BF16 [M,{k}]')
-    if (branch.shape != x.shape or branch.dtype != torch.bfloat16 or not branch.is_contiguous()
-            or branch.data_ptr() % 8):
-        raise ValueError(f'Branch requires aligned contiguous BF16 [M,{k}]')
-
-    def dense(name, t, shape, dtype, alignment):
-        if tuple(t.shape) != tuple(shape) or t.dtype != dtype or not t.is_contiguous() or t.data_ptr() % alignment:
-            raise ValueError(f'{name} requires contiguous {dtype} {tuple(shape)} and {alignment}B alignment')
-
-    dense('weight', weight, (k,), torch.bfloat16, 8)
-    if (shift.ndim != 2 or shift.shape[1] != k or shift.shape[0] < 1 or shift.shape[0] > 0x7fffffff
-            or scale.shape != shift.shape or shift.dtype != scale.dtype
-            or shift.dtype not in (torch.bfloat16, torch.float32)):
-        raise ValueError(f'Tables require matching nonempty FP32/BF16 [T,{k}]')
-    if gate.shape != shift.shape or gate.dtype not in (torch.bfloat16, torch.float32):
-        raise ValueError('Gate requires matching table shape and independent FP32/BF16 dtype')
-    for t in (gate, shift, scale):
-        if t.stride(1) != 1 or t.stride(0) < k or t.data_ptr() % t.element_size():
-            raise ValueError('Tables require dense hidden axes and nonoverlapping rows')
-    dense('rows', rows, (m,), torch.int32, 4)
-    dense('q', q, (m, k), torch.int8, 8)
-    dense('q_scale', q_scale, (m, 1), torch.float32, 4)
-    if debug_norm is not None:
-        dense('debug_norm', debug_norm, (m, k), torch.bfloat16, 2)
-        dense('debug_rotated', debug_rotated, (m, k), torch.float32, 4)
-        dense('debug_rstd', debug_rstd, (m,), torch.float32, 4)
-    tiny, big = torch.finfo(torch.float32).tiny, torch.finfo(torch.float32).max
-    if not math.isfinite(float(eps)) or not tiny <= float(eps) <= big:
-        raise ValueError('Epsilon must be finite, positive, normal FP32')
-    check_disjoint(inputs, outputs)
-    if check_values:
-        if int(rows.min().item()) < 0 or int(rows.max().item()) >= shift.shape[0]:
-            raise ValueError('Rows outside modulation table')
-        for tensor in (x, branch, weight, gate, shift, scale):
-            finite_bounded(tensor)
-    return tuple(inputs), tuple(outputs)
+    """Metadata checks (and, with check_values, the row-map and finiteness scans);
+    runnable on CPU tensors with require_cuda=False."""
+    names = {'x': x, 'branch': branch, 'weight': weight, 'gate': gate, 'shift': shift, 'scale': scale,
+             'rows': rows, 'q': q, 'q_scale': q_scale, 'debug_norm': debug_norm,
+             'debug_rotated': debug_rotated, 'debug_rstd': debug_rstd}
+    enforce(RULES, Call(names, {'eps': eps, 'check_values': check_values, 'require_cuda': require_cuda}))
+    return (tuple((n, names[n]) for n in INPUTS),
+            tuple((n, names[n]) for n in OUTPUTS if names[n] is not None))
 
 
 class ResidualQuant:
@@ -92,8 +90,8 @@ class ResidualQuant:
     def __init__(self, library=None):
         self.lib = _lib.load(library)
         self.path = _lib.library_path() if library is None else library
-        if self.lib.h3_residual_quant_abi() != 1 or \
-                self.lib.h3_residual_quant_resources_size() != ct.sizeof(Resources):
+        if (self.lib.h3_residual_quant_abi() != 1
+                or self.lib.h3_residual_quant_resources_size() != ct.sizeof(Resources)):
             raise RuntimeError('ResidualQuant C/ctypes ABI mismatch')
 
     def check(self, code):
@@ -101,44 +99,25 @@ class ResidualQuant:
             raise RuntimeError(f'ResidualQuant CUDA error {code}: ' + self.lib.h3_residual_quant_error(code).decode())
 
     def query(self, gate_dtype=0, table_dtype=0, debug=0, k=K):
-        data = Resources()
-        self.check(self.lib.h3_residual_quant_query_k(k, gate_dtype, table_dtype, debug, ct.byref(data),
-                                                      ct.sizeof(data)))
-        return {name: int(getattr(data, name)) for name, _ in data._fields_}
+        report = Resources()
+        self.check(self.lib.h3_residual_quant_query_k(k, gate_dtype, table_dtype, debug, ct.byref(report),
+                                                      ct.sizeof(report)))
+        return {name: int(getattr(report, name)) for name, _ in report._fields_}
 
     def bind(self, x, branch, weight, gate, shift, scale, rows, q, q_scale, *, eps,
              debug_norm=None, debug_rotated=None, debug_rstd=None, check_values=True):
         inputs, outputs = validate(x, branch, weight, gate, shift, scale, rows, q, q_scale, eps=eps,
                                    debug_norm=debug_norm, debug_rotated=debug_rotated, debug_rstd=debug_rstd,
                                    check_values=check_values)
-        with torch.cuda.device(x.device):
-            if torch.cuda.get_device_capability(x.device) != DEVICE_CAPABILITY:
-                raise RuntimeError('Only the intended B200 (sm_100) device is supported')
-            if torch.compiler.is_compiling():
-                raise RuntimeError('ResidualQuant requires eager execution')
-        pointers = [t.data_ptr() for t in (x, branch, weight, gate, shift, scale, rows, q, q_scale)]
-        pointers += [t.data_ptr() if t is not None else None for t in (debug_norm, debug_rotated, debug_rstd)]
-        args = pointers + [x.shape[0], x.shape[1], shift.shape[0], gate.stride(0), shift.stride(0), scale.stride(0),
-                           float(eps), int(gate.dtype == torch.bfloat16), int(shift.dtype == torch.bfloat16),
-                           int(debug_norm is not None)]
-        return Bound(self, x.device, inputs, outputs, args, (x, q, q_scale))
+        require_device(x.device, 'ResidualQuant')
+        ptr = lambda t: None if t is None else t.data_ptr()
+        args = [ptr(t) for t in (x, branch, weight, gate, shift, scale, rows, q, q_scale, debug_norm, debug_rotated,
+                                 debug_rstd)]
+        args += [x.shape[0], x.shape[1], shift.shape[0], gate.stride(0), shift.stride(0), scale.stride(0),
+                 float(eps), int(gate.dtype == torch.bfloat16), int(shift.dtype == torch.bfloat16),
+                 int(debug_norm is not None)]
+        return Bound(self.lib.h3_residual_quant_run_t, x.device, args, [t for _, t in inputs + outputs],
+                     [t for _, t in outputs], (x, q, q_scale), self.check)
 
 
-class Bound:
-    """A validated launch: owns its tensors, records allocator stream use."""
-
-    def __init__(self, library, device, inputs, outputs, args, result):
-        self.library, self.device, self.inputs, self.outputs = library, device, inputs, outputs
-        self.args, self.result = args, result
-        self.owners = tuple(t for _, t in inputs + outputs)
-
-    def __call__(self):
-        with torch.cuda.device(self.device):
-            stream = torch.cuda.current_stream(self.device)
-            for owner in self.owners:
-                owner.record_stream(stream)
-            code = self.library.lib.h3_residual_quant_run_t(*self.args, stream.cuda_stream)
-            # Stores may already be queued when an error is reported: never retried.
-            torch.autograd.graph.increment_version(tuple(t for _, t in self.outputs))
-            self.library.check(code)
-        return self.result
+Bound = Launch

@@ -21,20 +21,21 @@ ComfyUI and comfy-kitchen are imported lazily, only on the model-patching path.
 """
 from __future__ import annotations
 
-import ctypes as ct
 import hashlib
 import json
 import logging
 import threading
 from collections import Counter
+from contextlib import contextmanager
 from contextvars import ContextVar
+from dataclasses import dataclass, field
 from pathlib import Path
 
 import torch
 
 from . import _lib
 from .ops.convrot import ConvRotRegister, quantize_int8_rowwise_convrot64
-from .ops.gemm import int8_linear
+from .ops.gemm import int8_gate_residual, int8_linear
 from .ops.norm_quant import DEVICE_CAPABILITY, NormQuant
 
 LOG = logging.getLogger(__name__)
@@ -77,41 +78,32 @@ def segment_rows(segments, tokens: int, table_rows: int, device) -> torch.Tensor
 
 
 class Backend:
+    """The B200 kernels of one patched model: the manifest-checked library and the
+    per-block chain of the linear path (the role of runtime.py:40-164)."""
+
     def __init__(self, directory=None, *, require_device=True):
         self.directory = Path(directory) if directory else _lib.NATIVE
         if require_device and (not torch.cuda.is_available()
                                or torch.cuda.get_device_capability() != DEVICE_CAPABILITY):
             raise Unsupported("This build requires a B200 (sm_100) GPU")
         self.build = verify_manifest(self.directory)
-        self.lib = _lib.load(self.directory / _lib.LIB_NAME)
-        self.norm = NormQuant(self.directory / _lib.LIB_NAME)
-        self.convrot = ConvRotRegister(self.directory / _lib.LIB_NAME)
-        self.fc1 = self.lib.h3_int8          # reference names: runtime.py:62-66
-        self.gate = self.lib.h3_int8_gate
-
-    @staticmethod
-    def check(code):
-        if code != 1:
-            raise RuntimeError("SpeedKit GEMM failed; the request is aborted, never retried after mutation")
-
-    @staticmethod
-    def touch(*operands):
-        stream = torch.cuda.current_stream(operands[0].device)
-        for tensor in operands:
-            tensor.record_stream(stream)
-        return stream.cuda_stream
+        library = self.directory / _lib.LIB_NAME
+        self.lib = _lib.load(library)
+        self.norm = NormQuant(library)
+        self.convrot = ConvRotRegister(library)
+        # the reference's GEMM entry points by their own names (runtime.py:62-66)
+        self.fc1, self.gate = self.lib.h3_int8, self.lib.h3_int8_gate
 
     @staticmethod
     def plain_weight(module, x):
-        """INT8 weight [N, K] and FP32 per-channel scale [N] of a linear module:
-        comfy-kitchen QuantizedTensor weights (runtime.py:97-107) or a module that
-        carries ``weight_int8`` / ``weight_scale`` tensors."""
-        weight = module.weight
+        """INT8 weight [N, K] and FP32 per-channel scale [N] of a linear module on x's
+        device: comfy-kitchen QuantizedTensor weights (runtime.py:97-107) or a module
+        that carries ``weight_int8`` / ``weight_scale`` tensors."""
         if hasattr(module, "weight_int8"):
             w, scale = module.weight_int8, module.weight_scale
         else:
             from comfy_kitchen.tensor.int8 import TensorWiseINT8Layout
-            w, scale = TensorWiseINT8Layout.get_plain_tensors(weight)
+            w, scale = TensorWiseINT8Layout.get_plain_tensors(module.weight)
         w = w.to(device=x.device).contiguous()
         scale = scale.to(device=x.device, dtype=torch.float32).contiguous().view(-1)
         if w.dtype != torch.int8 or scale.numel() != w.shape[0]:
@@ -119,21 +111,23 @@ class Backend:
         return w, scale
 
     def normalize(self, module, x, shift, scale, rows):
-        weight = module.weight.to(device=x.device).detach()
-        q = torch.empty(x.shape, device=x.device, dtype=torch.int8)
-        qs = torch.empty((len(x), 1), device=x.device, dtype=torch.float32)
-        self.norm.bind(x, weight, shift, scale, rows, q, qs, eps=module.eps, check_values=False)()
-        return q, qs
+        """The fused prologue of `module` (RMSNorm weight, eps) on x: INT8 codes + scales."""
+        m, k = x.shape
+        q = torch.empty((m, k), device=x.device, dtype=torch.int8)
+        qs = torch.empty((m, 1), device=x.device, dtype=torch.float32)
+        launch = self.norm.bind(x, module.weight.to(device=x.device).detach(), shift, scale, rows, q, qs,
+                                eps=module.eps, check_values=False)
+        return launch()
 
     def gate_projection(self, linear, q, qs, x, gate, rows, skip=0):
+        """x[skip:] <- bf(fmaf(bf(dequant(q . W^T)), gate[rows], x)) in place: the
+        outproj / FC2 gate-residual GEMM over the rows past the window."""
         if skip >= len(x):
             return
         w, ws = self.plain_weight(linear, x)
-        g = gate.to(dtype=torch.bfloat16).contiguous()
-        operands = (q[skip:], w, qs[skip:], ws, x[skip:], g, rows[skip:], x[skip:])
-        st = self.touch(*operands)
-        self.check(self.gate(*(t.data_ptr() for t in operands), len(x) - skip, x.shape[1], w.shape[1], 13, st))
-        torch.autograd.graph.increment_version(x)
+        window = slice(skip, None)
+        int8_gate_residual(q[window], w, qs[window].reshape(-1), ws, x[window],
+                           gate.to(dtype=torch.bfloat16).contiguous(), rows[window])
 
     def block(self, block, x, t_emb, segments, rope=None, *, rows, skip=0, counts=None, attention=None,
               mlp_act="gelu_tanh"):
@@ -184,8 +178,56 @@ def last_block_window(payload, tokens: int) -> int:
     return min(a for a, _ in targets) // 128 * 128
 
 
+@dataclass
+class RequestFrame:
+    """State of one sampler call through the patched model (one diffusion-model
+    evaluation): set by the request wrapper, read by every block replacement."""
+    tokens: int = 0
+    skip: int = 0
+    shape_key: tuple = ()
+    verify: bool = False
+    counts: Counter = field(default_factory=Counter)
+    rows: torch.Tensor | None = None
+    row_key: tuple | None = None
+    fallback: str | None = None
+    verification_failed: int | None = None
+
+    @property
+    def active(self) -> bool:
+        return self.fallback is None and self.verification_failed is None
+
+    def rows_for(self, segments, tokens, table_rows, device):
+        """The int32 row map of `segments`, rebuilt only when the segments change."""
+        key = tuple(segments)
+        if self.row_key != key:
+            self.rows, self.row_key = segment_rows(segments, tokens, table_rows, device), key
+        return self.rows
+
+    def report(self) -> dict:
+        """The last_report record: every field that is set, counters as plain dicts."""
+        out = {}
+        for name in ("tokens", "skip", "shape_key", "verify", "counts", "fallback", "verification_failed"):
+            value = getattr(self, name)
+            if value is not None:
+                out[name] = dict(value) if isinstance(value, Counter) else value
+        return out
+
+
+class BlockReplacement:
+    """The ``("double_block", index)`` replacement ComfyUI calls as run(inputs, extra)."""
+
+    def __init__(self, patch, index):
+        self.patch, self.index = patch, index
+
+    def __call__(self, inputs, extra):
+        frame = self.patch.context.get()
+        if frame is None or not frame.active:
+            return extra["original_block"](inputs)
+        return self.patch.run_block(frame, self.index, inputs, extra)
+
+
 class ModelPatch:
-    """Request wrapper + block replacements (runtime.py:167-308)."""
+    """Request wrapper + block replacements (the roles of runtime.py:167-308)."""
 
     def __init__(self, model, backend, verify_new_shapes=True, attention=None, blocks=BLOCKS):
         self.model = model
@@ -200,71 +242,81 @@ class ModelPatch:
         self.verified_shapes = Counter()
         self.rejected_shapes = set()
 
-    def preflight(self, args, kwargs):
+    def preflight(self, args, kwargs) -> RequestFrame:
+        """Checks that run before any block; raises Unsupported (nothing mutated yet)."""
         if torch.is_grad_enabled():
             raise Unsupported("Eager inference only")
-        x = args[0][0] if args and isinstance(args[0], (list, tuple)) else (args[0] if args else None)
+        first = args[0] if args else None
+        x = first[0] if isinstance(first, (list, tuple)) else first
         if x is None or not x.is_cuda or torch.cuda.get_device_capability(x.device) != DEVICE_CAPABILITY:
             raise Unsupported("B200 GPU required")
         if self.attention is None:
             raise Unsupported("No attention provider for the B200 linear path")
         tokens = int(x.shape[-2]) if x.ndim >= 2 else 0
-        skip = last_block_window(kwargs.get("minimax_payload") or (args[4] if len(args) > 4 else None), tokens)
+        payload = kwargs.get("minimax_payload") or (args[4] if len(args) > 4 else None)
+        skip = last_block_window(payload, tokens)
         key = (tokens, skip)
-        return {"skip": skip, "rows": None, "row_key": None, "counts": Counter(), "tokens": tokens,
-                "shape_key": key, "verify": self.verified_shapes[key] < 8 and self.verify_new_shapes}
+        return RequestFrame(tokens=tokens, skip=skip, shape_key=key,
+                            verify=self.verify_new_shapes and self.verified_shapes[key] < 8)
+
+    def _open(self, args, kwargs) -> RequestFrame:
+        try:
+            return self.preflight(args, kwargs)
+        except Unsupported as error:
+            reason = str(error)
+            if reason not in self.warned:       # one warning per distinct reason
+                self.warned.add(reason)
+                LOG.warning("H3 SpeedKit fallback: %s", reason)
+            return RequestFrame(fallback=reason)
+
+    @contextmanager
+    def _request(self, args, kwargs):
+        frame = self._open(args, kwargs)
+        token = self.context.set(frame)
+        try:
+            yield frame
+        finally:
+            self.context.reset(token)
+
+    def _close(self, frame: RequestFrame) -> None:
+        if frame.fallback is None and frame.counts["attention"] != self.blocks:
+            raise RuntimeError("Incomplete SpeedKit block coverage")
+        if frame.verify and frame.verification_failed is None:
+            self.verified_shapes[frame.shape_key] += 1
+        self.last_report = frame.report()
 
     def wrapper(self, executor, *args, **kwargs):
-        with self.lock:
-            try:
-                frame = self.preflight(args, kwargs)
-            except Unsupported as error:
-                reason = str(error)
-                if reason not in self.warned:
-                    LOG.warning("H3 SpeedKit fallback: %s", reason)
-                    self.warned.add(reason)
-                frame = {"fallback": reason}
-            token = self.context.set(frame)
-            try:
-                result = executor(*args, **kwargs)
-                if "fallback" not in frame and frame["counts"]["attention"] != self.blocks:
-                    raise RuntimeError("Incomplete SpeedKit block coverage")
-                if frame.get("verify") and "verification_failed" not in frame:
-                    self.verified_shapes[frame["shape_key"]] += 1
-                self.last_report = {k: dict(v) if isinstance(v, Counter) else v for k, v in frame.items()
-                                    if k not in ("rows", "row_key")}
-                return result
-            finally:
-                self.context.reset(token)
+        """The DIFFUSION_MODEL wrapper: one request frame around the executor."""
+        with self.lock, self._request(args, kwargs) as frame:
+            result = executor(*args, **kwargs)
+            self._close(frame)
+            return result
 
     def replacement(self, index):
-        def run(inputs, extra):
-            frame = self.context.get()
-            if frame is None or "fallback" in frame or "verification_failed" in frame:
-                return extra["original_block"](inputs)
-            x, segments = inputs["img"], inputs["mod_segments"]
-            if x.dtype != torch.bfloat16 or not x.is_contiguous():
-                raise RuntimeError("Hidden activation changed after preflight")
-            key = tuple(segments)
-            if frame["row_key"] != key:
-                frame["rows"] = segment_rows(segments, len(x), inputs["t_emb"].shape[0] * 3, x.device)
-                frame["row_key"] = key
-            work = x.clone() if frame["verify"] else x
-            reference = extra["original_block"](inputs)["img"] if frame["verify"] else None
-            last = index == self.blocks - 1
-            output = self.backend.block(self.model.blocks[index], work, inputs["t_emb"], segments,
-                                        inputs.get("rope_freqs"), rows=frame["rows"],
-                                        skip=frame["skip"] if last else 0,
-                                        counts=frame["counts"], attention=self.attention)
-            start = frame["skip"] if last else 0   # the final layer reads rows [skip, M) only
-            if reference is not None and not torch.equal(output[start:], reference[start:]):
-                self.rejected_shapes.add(frame["shape_key"])
-                frame["verification_failed"] = index
-                frame["fallback"] = "Exact layout verification failed at block " + str(index)
-                LOG.warning("H3 SpeedKit: %s; using reference", frame["fallback"])
-                return {"img": reference}
-            return {"img": output}
-        return run
+        return BlockReplacement(self, index)
+
+    def run_block(self, frame: RequestFrame, index: int, inputs, extra):
+        """Block `index` on the B200 path.  In a verifying request the block runs on a
+        private clone beside the original block, and a single differing bit (rows
+        the last block's window skips excepted) rejects the layout and returns the
+        original block's result."""
+        x = inputs["img"]
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise RuntimeError("Hidden activation changed after preflight")
+        rows = frame.rows_for(inputs["mod_segments"], len(x), inputs["t_emb"].shape[0] * 3, x.device)
+        window = frame.skip if index == self.blocks - 1 else 0   # the final layer reads rows [skip, M)
+        work = x.clone() if frame.verify else x
+        expected = extra["original_block"](inputs)["img"] if frame.verify else None
+        out = self.backend.block(self.model.blocks[index], work, inputs["t_emb"], inputs["mod_segments"],
+                                 inputs.get("rope_freqs"), rows=rows, skip=window, counts=frame.counts,
+                                 attention=self.attention)
+        if expected is None or torch.equal(out[window:], expected[window:]):
+            return {"img": out}
+        self.rejected_shapes.add(frame.shape_key)
+        frame.verification_failed = index
+        frame.fallback = "Exact layout verification failed at block " + str(index)
+        LOG.warning("H3 SpeedKit: %s; using reference", frame.fallback)
+        return {"img": expected}
 
 
 def patch_model(model, directory=None, *, release_embeddings=True, verify_new_shapes=True, attention=None,

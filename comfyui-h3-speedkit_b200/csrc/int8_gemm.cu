@@ -67,7 +67,16 @@ constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
 constexpr int kDualMinK = 8192;     // K from which the dual (two N-tiles per unit) form is used
 constexpr int kDualMinWaves = 8;    // ... when its units fill at least this many waves of pairs
-constexpr int64_t kBSliceBytes = 32ll << 20;   // B bytes an N-group keeps in L2 (measured best)
+#ifndef H3SK_BSLICE_MB
+#define H3SK_BSLICE_MB 32
+#endif
+#ifndef H3SK_DUAL_BSLICE_MB
+#define H3SK_DUAL_BSLICE_MB 32
+#endif
+// B bytes an N-group keeps in L2: single-tile units (measured best: 32 MB) and
+// dual units (two N-tiles per unit, the long-K form).
+constexpr int64_t kBSliceBytes = int64_t(H3SK_BSLICE_MB) << 20;
+constexpr int64_t kDualBSliceBytes = int64_t(H3SK_DUAL_BSLICE_MB) << 20;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
 enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
@@ -148,43 +157,71 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   nt = first_n + local % gn;
 }
 
-// GELU-tanh, 0.5 v (1 + tanh(u)) with u = 0.7978845608028654 (v + 0.044715 v^3)
-// (convrot64_exact.cuh:913-923).  tanh(u) comes from the identity
-// tanh(u) = 2 / (1 + e^(-2u)) - 1: e^(-2u) = 2^(-2u / ln 2) by ex2.approx
-// (relative error about 2^-22), the reciprocal by rcp.approx, and the final
-// fma rounds tanh(u) to FP32 once.  Near u << 0 that rounding puts 1 + tanh(u)
-// on the same FP32 grid (multiples of 2^-24) as 1 + tanhf(u), so the tiny
-// negative-side outputs keep the reference's cancellation; elsewhere the
-// relative error of 1 + tanh(u) stays below 2^-19, far inside one BF16 ulp.
-// All 65,280 finite BF16 inputs are checked against the CPU restatement (libm
-// tanhf) to 1 BF16 ulp.  u = +-inf and NaN propagate as in the reference.
-__device__ __forceinline__ float gelu_tanh_fast(float v) {
-  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(inner * -2.8853900817779268f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
-  const float t = __fmaf_rn(2.0f, r, -1.0f);
-  return 0.5f * v * (1.0f + t);
+// ---- packed FP32 pairs (sm_100 f32x2), round-to-nearest, no flush -------------
+// Used for the GELU evaluation, whose contract is 1 BF16 ulp against the CPU
+// restatement (checked on every finite BF16 input); packing halves its
+// FMA-pipe instructions.
+__device__ __forceinline__ uint64_t p2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float p2_lo(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float p2_hi(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+__device__ __forceinline__ uint64_t p2_mul(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t p2_add(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t p2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// The two BF16 halves of a word as a packed FP32 pair (low half first).
+__device__ __forceinline__ uint64_t p2_from_bf2(uint32_t w) {
+  return p2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
-// GELU of a BF16 input, rounded to BF16 (the expression of
-// convrot64_exact.cuh:913-923 evaluated on the BF16 dequant value).
-__device__ __forceinline__ uint32_t bf_round_bits(float a) {
-  unsigned short b;
-  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(b) : "f"(a));
-  return b;
-}
-__device__ __forceinline__ uint32_t gelu_bits(uint32_t b) {
-  return bf_round_bits(gelu_tanh_fast(__uint_as_float(b << 16)));
-}
-
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 // Two FP32 values -> one word of two BF16 (round to nearest even), low half = lo.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
   uint32_t w;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
   return w;
+}
+__device__ __forceinline__ uint32_t pack_bf2(uint64_t v) { return pack_bf2(p2_lo(v), p2_hi(v)); }
+
+// GELU-tanh of both BF16 halves of a word, 0.5 v (1 + tanh(u)) with
+// u = 0.7978845608028654 (v + 0.044715 v^3) (convrot64_exact.cuh:913-923),
+// evaluated left to right with one IEEE rounding per operation, as written:
+// ((0.044715 v) v) v, v + that, times 0.7978845608028654.  tanh(u) comes from the
+// identity tanh(u) = 2 / (1 + e^(-2u)) - 1: e^(-2u) = 2^(-2u / ln 2) by ex2.approx
+// (relative error about 2^-22), the reciprocal by rcp.approx, and the final fma
+// rounds tanh(u) to FP32 once.  Near u << 0 that rounding puts 1 + tanh(u) on the
+// same FP32 grid (multiples of 2^-24) as 1 + tanhf(u), so the tiny negative-side
+// outputs keep the reference's cancellation; elsewhere the relative error of
+// 1 + tanh(u) stays below 2^-19, far inside one BF16 ulp.  All 65,280 finite
+// BF16 inputs are checked against the CPU restatement (libm tanhf) to 1 BF16 ulp.
+// u = +-inf and NaN propagate as in the reference.  Result rounded to BF16.
+__device__ __forceinline__ uint32_t gelu_bf2(uint32_t w) {
+  const uint64_t v = p2_from_bf2(w);
+  const uint64_t cube = p2_mul(p2_mul(p2_mul(p2(0.044715f, 0.044715f), v), v), v);
+  const uint64_t inner = p2_mul(p2(0.7978845608028654f, 0.7978845608028654f), p2_add(v, cube));
+  const uint64_t arg = p2_mul(inner, p2(-2.8853900817779268f, -2.8853900817779268f));
+  float e0, e1, r0, r1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(p2_lo(arg)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(p2_hi(arg)));
+  const uint64_t den = p2_add(p2(1.0f, 1.0f), p2(e0, e1));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(p2_lo(den)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(p2_hi(den)));
+  const uint64_t t = p2_fma(p2(2.0f, 2.0f), p2(r0, r1), p2(-1.0f, -1.0f));
+  const uint64_t g = p2_mul(p2_mul(p2(0.5f, 0.5f), v), p2_add(p2(1.0f, 1.0f), t));
+  return pack_bf2(g);
 }
 
 // Named barrier among the four epilogue warps only.
@@ -206,9 +243,9 @@ __device__ __forceinline__ void store_chunk_acc(const GemmParams& p, const uint3
 // columns >= N produce unused values and read no memory.
 // BF16 results of one 32-column chunk of one row: y = bf((acc * xs) * ws + bias)
 // (fc1.cu / gate.cu epilogue order), then GELU or the gate-residual update.
-// Column scales and bias come from shared memory as 16-byte broadcasts.  (Packed
-// f32x2 multiplies and adds were measured to differ from these scalar IEEE
-// operations on rare cancelling inputs, so the dequant stays scalar.)
+// Column scales and bias come from shared memory as 16-byte broadcasts.  The
+// dequant and the gate FMA stay scalar: packed f32x2 forms of them were measured
+// to differ from the scalar IEEE operations on rare inputs.
 template <int kEpi>
 __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t (&r)[32], bool row_ok, int row,
                                              int col0, int c, float xs_row, const __nv_bfloat16* gate_row,
@@ -228,10 +265,7 @@ __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t
   }
   if constexpr (kEpi == kEpiGelu) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t w = packed[i];
-      packed[i] = gelu_bits(w & 0xffffu) | (gelu_bits(w >> 16) << 16);
-    }
+    for (int i = 0; i < 16; ++i) packed[i] = gelu_bf2(packed[i]);
   }
   if constexpr (kEpi == kEpiGate) {
     // D may alias the residual: every element is read here, before its store is issued.
@@ -247,8 +281,10 @@ __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const uint32_t yw = packed[4 * v + w];
-        const float lo = __fmaf_rn(bf_lo(yw), bf_lo(gw[w]), bf_lo(rw[w]));
-        const float hi = __fmaf_rn(bf_hi(yw), bf_hi(gw[w]), bf_hi(rw[w]));
+        const float lo = __fmaf_rn(__uint_as_float(yw << 16), __uint_as_float(gw[w] << 16),
+                                   __uint_as_float(rw[w] << 16));
+        const float hi = __fmaf_rn(__uint_as_float(yw & 0xffff0000u), __uint_as_float(gw[w] & 0xffff0000u),
+                                   __uint_as_float(rw[w] & 0xffff0000u));
         packed[4 * v + w] = pack_bf2(lo, hi);
       }
     }
@@ -820,7 +856,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.work = p.m_tiles * p.n_units;
   {
     const int64_t slice = int64_t(kBN) * dual_n * K;   // B bytes of one work unit's N-tiles
-    const int64_t g = kBSliceBytes / (slice > 0 ? slice : 1);
+    const int64_t g = (dual ? kDualBSliceBytes : kBSliceBytes) / (slice > 0 ? slice : 1);
     p.group_n = int(g < 1 ? 1 : (g > p.n_units ? p.n_units : g));
   }
   p.timeout_ns = kWaitTimeoutNs;

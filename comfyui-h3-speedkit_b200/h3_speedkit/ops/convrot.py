@@ -158,8 +158,8 @@ def quantize_int8_rowwise_convrot64(x, groupsize=256, input_act=None, *, out=Non
         raise ValueError(f'K must be a multiple of 256 in [256, {MAX_K}]')
     q = torch.empty((m, k), dtype=torch.int8, device=x.device) if out is None else out
     s = torch.empty((m, 1), dtype=torch.float32, device=x.device) if out_scale is None else out_scale
-    _validate(q, (m, k), torch.int8, x.device, 'q')
-    _validate(s, (m, 1), torch.float32, x.device, 'scale')
+    outputs = Call({'x': x, 'q': q, 'scale': s}, {'m': m, 'k': k})
+    enforce(_buffer_rules('q', _MK, torch.int8) + _buffer_rules('scale', _M1, torch.float32), outputs)
     lib = _lib.load()
     with torch.cuda.device(x.device):
         stream = torch.cuda.current_stream(x.device)

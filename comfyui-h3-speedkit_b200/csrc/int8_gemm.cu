@@ -67,6 +67,25 @@ constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kTmemCols = 512;
 constexpr int kDualMinK = 8192;     // K from which the dual (two N-tiles per unit) form is used
 constexpr int kDualMinWaves = 8;    // ... when its units fill at least this many waves of pairs
+// Pipeline depths (operand stages of the CTA-pair and dual forms), output
+// staging buffers per epilogue warp (2: a chunk's store may still be reading one
+// buffer while the next chunk fills the other) and TMEM load prefetch (the next
+// chunk's tcgen05.ld is issued before the current chunk is computed; 1: every
+// form, 2: the dual form only, whose epilogue the MMA waits for).  Measured on
+// the cfg5 stack (M = 98304): prefetch shortens the dual FC2 by ~1 % and slows
+// the overlapped FC1 by ~2 %; 5 vs 6 stages and double staging are within noise.
+#ifndef H3SK_PAIR_STAGES
+#define H3SK_PAIR_STAGES 6
+#endif
+#ifndef H3SK_DUAL_STAGES
+#define H3SK_DUAL_STAGES 4
+#endif
+#ifndef H3SK_STAGE_BUFS
+#define H3SK_STAGE_BUFS 1
+#endif
+#ifndef H3SK_TMEM_PREFETCH
+#define H3SK_TMEM_PREFETCH 2
+#endif
 #ifndef H3SK_BSLICE_MB
 #define H3SK_BSLICE_MB 32
 #endif
@@ -100,7 +119,8 @@ struct Shape {
   static constexpr int b_rows = kPair ? kBN / 2 : kBN;    // B rows loaded per CTA
   static constexpr int b_tile_bytes = b_rows * kBK;
   static constexpr int stage_bytes = kATileBytes + dual_n * b_tile_bytes;
-  static constexpr int stages = kPair ? (kDual ? 4 : 6) : 4;
+  static constexpr int stages = kPair ? (kDual ? H3SK_DUAL_STAGES : H3SK_PAIR_STAGES) : 4;
+  static constexpr int stage_bufs = (kPair && !kDual) ? H3SK_STAGE_BUFS : 1;   // output staging buffers per warp
   static constexpr uint32_t idesc = idesc_i8(kBM * pair, kBN);
   static constexpr uint32_t tempty_count = kPair ? 2 * kEpilogueWarps : kEpilogueWarps;
 };
@@ -116,7 +136,7 @@ struct SmemLayout {
   static constexpr int misc = (bars + nbars * 8 + 15) / 16 * 16;  // tmem slot, abort flag, ready flag
   static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float (16-byte aligned)
   static constexpr int stage = ((colv + 2 * kBN * 4) + 1023) / 1024 * 1024;   // per-warp output staging
-  static constexpr int stage_warp_bytes = 32 * 32 * 2;           // 32 rows x 32 BF16 columns
+  static constexpr int stage_warp_bytes = 32 * 32 * 2 * S::stage_bufs;   // stage_bufs x (32 rows x 32 BF16 columns)
   static constexpr int total = stage + kEpilogueWarps * stage_warp_bytes;
   static constexpr int dynamic_bytes = total + 1024;             // slack for 1024 alignment
 };
@@ -506,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader = kPair ? map_to_rank(smem_addr(tempty), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t stored = 0;   // chunks this warp has staged (selects the staging buffer)
     // Tiles in the MMA's order: the dual_n tiles of each work unit in turn, so
     // the accumulators alternate 0, 1, 0, 1 as in the single-tile form.
     for (int it = 0;; ++it) {
@@ -537,21 +558,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __nv_bfloat16* gate_row = nullptr;
       if (kEpi == kEpiGate && row_ok) gate_row = p.gate + int64_t(p.rows[row]) * p.gate_ld;
       const uint32_t t_row = tmem_base + uint32_t(acc * kBN) + (uint32_t(quarter * 32) << 16);
-#pragma unroll 1
-      for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
-        uint32_t r[32];
+      const int c_first = half * (kBN / 64), c_last = c_first + kBN / 64 - 1;
+      // This warp's last read of the accumulator has landed: release it to the MMA issuer.
+      auto release = [&]() {
+        tc_fence_before();
         __syncwarp();
-        tmem_load_32cols(t_row + uint32_t(c * 32), r);
-        tmem_load_wait();
-        if (c == (half + 1) * (kBN / 64) - 1) {
-          // This warp's last read of the accumulator: release it to the MMA issuer.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (kPair) mbar_arrive_remote(tempty_leader + uint32_t(acc) * 8u);
-            else mbar_arrive(&tempty[acc]);
-          }
+        if (lane == 0) {
+          if constexpr (kPair) mbar_arrive_remote(tempty_leader + uint32_t(acc) * 8u);
+          else mbar_arrive(&tempty[acc]);
         }
+      };
+      auto emit = [&](int c, const uint32_t (&r)[32]) {
         const int col0 = n0 + c * 32;
         if constexpr (kEpi == kEpiAcc) {
           if (row_ok && col0 < p.n) store_chunk_acc(p, r, row, col0);
@@ -560,10 +577,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // one TMA tensor store (rows >= M and columns >= N are clipped by TMA).
           uint32_t packed[16];
           chunk_values<kEpi>(p, r, row_ok, row, col0, c, xs_row, gate_row, col_ws, col_bias, packed);
-          if (lane == 0) bulk_wait_read_all();    // the previous store has read the buffer
+          uint8_t* buf = stage + (stored & (S::stage_bufs - 1)) * (L::stage_warp_bytes / S::stage_bufs);
+          ++stored;
+          // the store that last read `buf` is done reading it
+          if (lane == 0) {
+            if constexpr (S::stage_bufs == 2) bulk_wait_read_1();
+            else bulk_wait_read_all();
+          }
           __syncwarp();
           // 64-byte swizzle: 16-byte chunk v of row i sits at chunk v ^ ((i >> 1) & 3)
-          uint8_t* srow = stage + lane * 64;
+          uint8_t* srow = buf + lane * 64;
 #pragma unroll
           for (int v = 0; v < 4; ++v)
             *reinterpret_cast<uint4*>(srow + ((v ^ ((lane >> 1) & 3)) << 4)) =
@@ -571,10 +594,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_shared();
           __syncwarp();
           if (lane == 0) {
-            if (p.head_major) tma_store_3d(&map_d, stage, col0 & 127, row_base, col0 >> 7);
-            else tma_store_2d(&map_d, stage, col0, row_base);
+            if (p.head_major) tma_store_3d(&map_d, buf, col0 & 127, row_base, col0 >> 7);
+            else tma_store_2d(&map_d, buf, col0, row_base);
             bulk_commit();
           }
+        }
+      };
+      if constexpr (H3SK_TMEM_PREFETCH == 1 || (H3SK_TMEM_PREFETCH == 2 && kDual)) {
+        // chunk c + 1's TMEM load is in flight while chunk c is computed
+        uint32_t r[32];
+        __syncwarp();
+        tmem_load_32cols(t_row + uint32_t(c_first * 32), r);
+#pragma unroll
+        for (int i = 0; i < kBN / 64; ++i) {
+          const int c = c_first + i;
+          tmem_load_wait();
+          if (c == c_last) release();
+          uint32_t cur[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cur[j] = r[j];
+          if (c < c_last) {
+            __syncwarp();
+            tmem_load_32cols(t_row + uint32_t((c + 1) * 32), r);
+          }
+          emit(c, cur);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = c_first; c <= c_last; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_load_32cols(t_row + uint32_t(c * 32), r);
+          tmem_load_wait();
+          if (c == c_last) release();
+          emit(c, r);
         }
       }
       __syncwarp();

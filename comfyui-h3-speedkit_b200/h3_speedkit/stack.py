@@ -23,6 +23,8 @@ ctypes calls on the current stream (and can be captured in a CUDA graph).
 """
 from __future__ import annotations
 
+import weakref
+
 from dataclasses import dataclass
 
 import torch
@@ -172,7 +174,20 @@ def shared_host_output(rows: int, d: int, dtype=torch.bfloat16, group=None,
         if ok and base is not None:
             torch.cuda.cudart().cudaHostUnregister(base.data_ptr())
         return None
-    return base.view(dtype).view(rows, d)
+    out = base.view(dtype).view(rows, d)
+    # Page-locking lasts as long as the returned tensor: when it is collected the
+    # registration is removed before the mapping itself can go (the finalizer holds
+    # the mapping until then).  Views taken from `out` that outlive it keep the
+    # memory mapped but no longer page-locked.
+    weakref.finalize(out, _host_unregister, base.data_ptr(), base)
+    return out
+
+
+def _host_unregister(ptr: int, _mapping) -> None:
+    try:
+        torch.cuda.cudart().cudaHostUnregister(ptr)
+    except Exception:   # interpreter shutdown: the process exit releases it
+        pass
 
 
 def gather_shards(send: torch.Tensor, out: torch.Tensor, total: int, group=None) -> torch.Tensor:

@@ -1,6 +1,7 @@
 // Host-side launch helpers shared by the row-quantiser translation units.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -20,6 +21,31 @@ int* status_device_ptr();
 // Returns 1 on success, 0 on failure (reason in h3_int8_error).
 int gemm_dequant_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int N,
                        int K, cudaStream_t stream);
+// Operands of the QKV head epilogue fused into the INT8 GEMM: the GEMM writes the
+// dequantised product into D's head-major planes [3, heads, M, 128] and finishes
+// every row of every head in its epilogue warps (per-head RMS, weight, RoPE,
+// rotation, INT8 codes and scales of Q and K, V tile maxima).
+struct HeadsArgs {
+  const __nv_bfloat16* freqs;     // [M, 192]: (a, b, c, e) of RoPE pair d < 48
+  const __nv_bfloat16* qw;        // [128]
+  const __nv_bfloat16* kw;        // [128]
+  const __nv_bfloat16* sk;        // [heads, 9, 128] sampled keys, or null (no centring)
+  const int* anchors;             // [heads] anchor sample or -1, or null
+  int8_t* qi;                     // [heads, M, 128]
+  float* qs;                      // [heads, parts * 32]
+  int8_t* ki;                     // [heads, M, 128]
+  float* ks;                      // [heads, parts * 4]
+  float* vp;                      // [heads, parts, 128]
+  float eps;
+  int heads, parts;
+};
+
+// The QKV GEMM with the head epilogue fused (kernels/gemm/r84_kfourwarp.cu:213-375):
+// D [3, heads, M, 128] BF16 (Q and K normalised and roped, V raw), Q/K codes and
+// scales, V tile maxima, all from the GEMM's epilogue warps.  heads must be even.
+// Returns 1 on success, 0 on failure (reason in h3_int8_error).
+int gemm_qkv_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int K,
+                   const HeadsArgs& hd, cudaStream_t stream);
 int last_gemm_error();
 // Set the thread's h3_int8_last_error / h3_int8_error record (returns 0), or clear it.
 int record_failure(int code, const char* what);

@@ -44,6 +44,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "host_util.h"
 #include "sm100.cuh"
 #include "../../include/h3sk_b200.h"
 
@@ -98,7 +99,7 @@ constexpr int64_t kBSliceBytes = int64_t(H3SK_BSLICE_MB) << 20;
 constexpr int64_t kDualBSliceBytes = int64_t(H3SK_DUAL_BSLICE_MB) << 20;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
-enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3 };
+enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads = 4, kEpiKinds = 5 };
 
 // Tile geometry of the two kernel shapes.
 //   single CTA: a 128 x 256 tile per CTA, B tile 256 rows, 4 stages of 48 KB;
@@ -135,7 +136,8 @@ struct SmemLayout {
   static constexpr int nbars = 2 * S::stages + 5;
   static constexpr int misc = (bars + nbars * 8 + 15) / 16 * 16;  // tmem slot, abort flag, ready flag
   static constexpr int colv = misc + 16;                         // ws[256], bias[256] as float (16-byte aligned)
-  static constexpr int stage = ((colv + 2 * kBN * 4) + 1023) / 1024 * 1024;   // per-warp output staging
+  static constexpr int hred = colv + 2 * kBN * 4;                // head epilogue: V maxima [2][4][128] u32, K maxima [2][4][4]
+  static constexpr int stage = ((hred + 2 * 4 * 128 * 4 + 2 * 4 * 4 * 4) + 1023) / 1024 * 1024;   // per-warp output staging
   static constexpr int stage_warp_bytes = 32 * 32 * 2 * S::stage_bufs;   // stage_bufs x (32 rows x 32 BF16 columns)
   static constexpr int total = stage + kEpilogueWarps * stage_warp_bytes;
   static constexpr int dynamic_bytes = total + 1024;             // slack for 1024 alignment
@@ -161,6 +163,7 @@ struct GemmParams {
   int work;                       // m_tiles * n_units
   int group_n;                    // N units per weight-stationary group
   int head_major;                 // 1: D is [N/128, M, 128] (one plane per 128 columns)
+  HeadsArgs hd;                   // kEpiHeads only
   int* status;
   uint64_t timeout_ns;
 };
@@ -247,6 +250,140 @@ __device__ __forceinline__ uint32_t gelu_bf2(uint32_t w) {
 // Named barrier among the four epilogue warps only.
 __device__ __forceinline__ void epilogue_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+}
+
+// Named barrier among the four epilogue warps of one column half (one head).
+__device__ __forceinline__ void half_sync(int half) {
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
+}
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t x) {
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(x));
+  return r;
+}
+__device__ __forceinline__ float bf_at(const uint32_t (&y)[64], int ch) {
+  const uint32_t w = y[ch >> 1];
+  return __uint_as_float((ch & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+__device__ __forceinline__ float bf_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint32_t bf_pair(float lo, float hi) {
+  uint32_t w;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
+  return w;
+}
+// Four codes cvt.rni.sat.s8.f32(v * inv), packed little-endian (r84_kfourwarp.cu:300-306).
+__device__ __forceinline__ uint32_t codes4_rni(float a, float b, float c, float d, float inv) {
+  int ia, ib, ic, id;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ia) : "f"(a * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ib) : "f"(b * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(ic) : "f"(c * inv));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(id) : "f"(d * inv));
+  uint32_t hi, word;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(id), "r"(ic), "r"(0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(word) : "r"(ib), "r"(ia), "r"(hi));
+  return word;
+}
+
+// Per-head RMS normalisation, weight and RoPE of one row held by one thread, in
+// place on its 64 BF16 pair words (r84_kfourwarp.cu:262-282): the 32 chains
+// fmaf(v, v, s) over channels l, l + 32, l + 64, l + 96 in that order, the
+// shfl_down tree of the reference folded in registers (s_l += s_{l+off}, off =
+// 16 .. 1), rrms = rsqrtf(sum / 128 + eps); then x = bf((t * rrms) * w) and, for
+// the pairs (d, d + 48), d < 48: bf(a * x0 + b * x1), bf(c * x0 + e * x1) with the
+// row's RoPE coefficients; channels 96..127 are normalised and weighted only.
+// The expressions are written as the reference writes them, in a unit compiled
+// like the reference's QKV unit (no fast math), so each rounds the same way.
+__device__ __forceinline__ void rms_rope_row(uint32_t (&y)[64], const __nv_bfloat16* w, const __nv_bfloat16* f,
+                                             float eps) {
+  float chain[32];
+#pragma unroll
+  for (int l = 0; l < 32; ++l) chain[l] = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const float v = bf_at(y, 32 * k + l);
+      chain[l] = fmaf(v, v, chain[l]);
+    }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int l = 0; l < off; ++l) chain[l] += chain[l + off];
+  const float rrms = rsqrtf(chain[0] / 128.f + eps);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  const uint4* f4 = reinterpret_cast<const uint4*>(f);
+  // pairs: words j (channels 2j, 2j+1) and j + 24 (channels 2j + 48, 2j + 49), j < 24
+#pragma unroll
+  for (int q = 0; q < 6; ++q) {              // 8 channels d = 8q .. 8q+7 per round
+    const uint4 wa = __ldg(w4 + q), wb = __ldg(w4 + 6 + q);
+    const uint32_t wlo[4] = {wa.x, wa.y, wa.z, wa.w}, whi[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int j = 4 * q + h;               // word of channels d = 2j, 2j + 1
+      const uint4 fc = __ldg(f4 + j);         // (a, b | c, e) of pair 2j, then of pair 2j + 1
+      float out0[2], out1[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float t0 = bf_at(y, 2 * j + k), t1 = bf_at(y, 2 * j + k + 48);
+        const float w0 = __uint_as_float(k ? (wlo[h] & 0xffff0000u) : (wlo[h] << 16));
+        const float w1 = __uint_as_float(k ? (whi[h] & 0xffff0000u) : (whi[h] << 16));
+        const float x0 = bf_round(t0 * rrms * w0), x1 = bf_round(t1 * rrms * w1);
+        const uint32_t ab = k ? fc.z : fc.x, ce = k ? fc.w : fc.y;
+        const float a = __uint_as_float(ab << 16), b = __uint_as_float(ab & 0xffff0000u);
+        const float c = __uint_as_float(ce << 16), e = __uint_as_float(ce & 0xffff0000u);
+        out0[k] = a * x0 + b * x1;
+        out1[k] = c * x0 + e * x1;
+      }
+      y[j] = bf_pair(out0[0], out0[1]);
+      y[j + 24] = bf_pair(out1[0], out1[1]);
+    }
+  }
+#pragma unroll
+  for (int q = 12; q < 16; ++q) {             // channels 96..127
+    const uint4 wt = __ldg(w4 + q);
+    const uint32_t ww[4] = {wt.x, wt.y, wt.z, wt.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int j = 4 * q + h;
+      const float t0 = bf_at(y, 2 * j), t1 = bf_at(y, 2 * j + 1);
+      y[j] = bf_pair(t0 * rrms * __uint_as_float(ww[h] << 16), t1 * rrms * __uint_as_float(ww[h] & 0xffff0000u));
+    }
+  }
+}
+
+// The signed H128 rotation of one row held by one thread (r84_kfourwarp.cu:123-191
+// in the reference's 4-channels-per-lane form): channel ch is negated where bit
+// ch % 32 of sign word ch / 32 is clear, then the 4-point block on channel bits
+// 0-1 ((a0 + a2) * 0.5 ...), then butterflies lo' = lo + hi, hi' = lo - hi on
+// channel bits 2..6 in that order, then the factor 0.1767766952966369f.  With
+// `full` false (M <= 256) only the 4-point block runs (r84:297, 330).
+__device__ __forceinline__ void rotate128(float (&v)[128], bool full) {
+  if (full) {
+    constexpr uint32_t kSigns[4] = {0x1035997bu, 0x8087f5eeu, 0xee2e4e1au, 0x71132418u};
+#pragma unroll
+    for (int ch = 0; ch < 128; ++ch)
+      if (((kSigns[ch >> 5] >> (ch & 31)) & 1u) == 0u) v[ch] = -v[ch];
+  }
+#pragma unroll
+  for (int j = 0; j < 128; j += 4) {
+    const float a0 = v[j] + v[j + 1], a1 = v[j] - v[j + 1], a2 = v[j + 2] + v[j + 3], a3 = v[j + 2] - v[j + 3];
+    v[j] = (a0 + a2) * 0.5f;
+    v[j + 1] = (a1 + a3) * 0.5f;
+    v[j + 2] = (a0 - a2) * 0.5f;
+    v[j + 3] = (a1 - a3) * 0.5f;
+  }
+  if (!full) return;
+#pragma unroll
+  for (int bit = 4; bit < 128; bit <<= 1)
+#pragma unroll
+    for (int j = 0; j < 128; ++j) {
+      if (j & bit) continue;
+      const float lo = v[j], hi = v[j | bit];
+      v[j] = lo + hi;
+      v[j | bit] = lo - hi;
+    }
+#pragma unroll
+  for (int j = 0; j < 128; ++j) v[j] *= 0.1767766952966369f;
 }
 
 // Raw int32 accumulators of one row, columns [col0, col0+32) (debug epilogue).
@@ -568,39 +705,161 @@ __global__ void __launch_bounds__(kThreads, 1)
           else mbar_arrive(&tempty[acc]);
         }
       };
+      // BF16 chunk: 32 rows x 32 columns through this warp's staging buffer and
+      // one TMA tensor store (rows >= M and columns >= N are clipped by TMA).
+      auto store_chunk = [&](int col0, const uint32_t* packed) {
+        uint8_t* buf = stage + (stored & (S::stage_bufs - 1)) * (L::stage_warp_bytes / S::stage_bufs);
+        ++stored;
+        // the store that last read `buf` is done reading it
+        if (lane == 0) {
+          if constexpr (S::stage_bufs == 2) bulk_wait_read_1();
+          else bulk_wait_read_all();
+        }
+        __syncwarp();
+        // 64-byte swizzle: 16-byte chunk v of row i sits at chunk v ^ ((i >> 1) & 3)
+        uint8_t* srow = buf + lane * 64;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(srow + ((v ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (p.head_major) tma_store_3d(&map_d, buf, col0 & 127, row_base, col0 >> 7);
+          else tma_store_2d(&map_d, buf, col0, row_base);
+          bulk_commit();
+        }
+      };
       auto emit = [&](int c, const uint32_t (&r)[32]) {
         const int col0 = n0 + c * 32;
         if constexpr (kEpi == kEpiAcc) {
           if (row_ok && col0 < p.n) store_chunk_acc(p, r, row, col0);
         } else if (col0 < p.n && row_base < p.m) {
-          // BF16 chunk: 32 rows x 32 columns through this warp's staging buffer and
-          // one TMA tensor store (rows >= M and columns >= N are clipped by TMA).
           uint32_t packed[16];
           chunk_values<kEpi>(p, r, row_ok, row, col0, c, xs_row, gate_row, col_ws, col_bias, packed);
-          uint8_t* buf = stage + (stored & (S::stage_bufs - 1)) * (L::stage_warp_bytes / S::stage_bufs);
-          ++stored;
-          // the store that last read `buf` is done reading it
-          if (lane == 0) {
-            if constexpr (S::stage_bufs == 2) bulk_wait_read_1();
-            else bulk_wait_read_all();
-          }
-          __syncwarp();
-          // 64-byte swizzle: 16-byte chunk v of row i sits at chunk v ^ ((i >> 1) & 3)
-          uint8_t* srow = buf + lane * 64;
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(srow + ((v ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          fence_async_shared();
-          __syncwarp();
-          if (lane == 0) {
-            if (p.head_major) tma_store_3d(&map_d, buf, col0 & 127, row_base, col0 >> 7);
-            else tma_store_2d(&map_d, buf, col0, row_base);
-            bulk_commit();
-          }
+          store_chunk(col0, packed);
         }
       };
-      if constexpr (H3SK_TMEM_PREFETCH == 1 || (H3SK_TMEM_PREFETCH == 2 && kDual)) {
+      if constexpr (kEpi == kEpiHeads) {
+        // ---- QKV head epilogue: this thread finishes row `row` of one head ----
+        // (128 columns = one head; the tile's two heads are the two column halves)
+        const HeadsArgs& hd = p.hd;
+        const int plane_w = hd.heads * 128;
+        const int g = n0 / plane_w;                          // 0 Q, 1 K, 2 V (a tile never straddles)
+        const int head = (n0 - g * plane_w) / 128 + half;
+        const int part = (mt * S::tile_m + int(rank) * kBM) / 128;   // this CTA's 128 rows = one part
+        // The second CTA of a pair may hold no row < M (the last M-tile): its part
+        // does not exist and it writes no scale or maximum.
+        const bool part_ok = part < hd.parts;
+        uint32_t y[64];                                      // the row's 128 dequantised BF16 values
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = c_first + cc;
+          uint32_t r[32];
+          __syncwarp();
+          tmem_load_32cols(t_row + uint32_t(c * 32), r);
+          tmem_load_wait();
+          if (c == c_last) release();
+          uint32_t packed[16];
+          chunk_values<kEpiDequant>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws, col_bias, packed);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) y[16 * cc + i] = packed[i];
+        }
+        uint32_t* vred = reinterpret_cast<uint32_t*>(smem + L::hred);   // [2][4][128]
+        float* kred = reinterpret_cast<float*>(smem + L::hred + 2 * 4 * 128 * 4);   // [2][4][4]
+        if (g == 2) {
+          // V: raw values to D, per-channel maxima of |BF16| over the part's 128 rows
+          if (row_base < p.m) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) store_chunk(n0 + (c_first + cc) * 32, y + 16 * cc);
+          }
+          uint32_t mine[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int ch = 0; ch < 128; ++ch) {
+            const uint32_t w = y[ch >> 1];
+            const uint32_t mag = row_ok ? (((ch & 1) ? (w >> 16) : w) & 0x7fffu) : 0u;
+            const uint32_t mx = warp_max_u32(mag);
+            if (lane == (ch & 31)) mine[ch >> 5] = mx;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) vred[(half * 4 + quarter) * 128 + 32 * k + lane] = mine[k];
+          half_sync(half);
+          if (quarter == 0 && part_ok && hd.vp != nullptr) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int ch = 32 * k + lane;
+              uint32_t mx = 0;
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) mx = max(mx, vred[(half * 4 + qq) * 128 + ch]);
+              hd.vp[(int64_t(head) * hd.parts + part) * 128 + ch] = __uint_as_float(mx << 16);
+            }
+          }
+        } else {
+          // Q / K: normalise and rope, write D, rotate, quantise
+          if (row_ok) rms_rope_row(y, g == 0 ? hd.qw : hd.kw, hd.freqs + int64_t(row) * 192, hd.eps);
+          if (row_base < p.m) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) store_chunk(n0 + (c_first + cc) * 32, y + 16 * cc);
+          }
+          float v[128];
+#pragma unroll
+          for (int ch = 0; ch < 128; ++ch) v[ch] = row_ok ? bf_at(y, ch) : 0.f;
+          if (g == 1 && row_ok && hd.anchors != nullptr && hd.sk != nullptr) {
+            const int anchor = hd.anchors[head];
+            if (anchor >= 0 && anchor < 9) {   // an out-of-range anchor reads nothing
+              const uint4* s4 = reinterpret_cast<const uint4*>(hd.sk + (int64_t(head) * 9 + anchor) * 128);
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const uint4 b = __ldg(s4 + q);
+                const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  v[8 * q + 2 * i] = v[8 * q + 2 * i] - __uint_as_float(bw[i] << 16);
+                  v[8 * q + 2 * i + 1] = v[8 * q + 2 * i + 1] - __uint_as_float(bw[i] & 0xffff0000u);
+                }
+              }
+            }
+          }
+          rotate128(v, p.m > 256);
+          float mx = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 128; ++ch) mx = fmaxf(mx, fabsf(v[ch]));
+          float sc, inv;
+          if (g == 0) {
+            // Q group 8 * quarter + lane % 8: rows s, s + 8, s + 16, s + 24 of the quarter
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            sc = fmaf(mx, 1.f / 127.f, 1e-7f);
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(sc));
+            if (lane < 8 && part_ok && hd.qs != nullptr)
+              hd.qs[int64_t(head) * hd.parts * 32 + part * 32 + quarter * 8 + lane] = sc;
+          } else {
+            // K group kg: rows tr with tr % 8 in {2kg, 2kg + 1}, across the four quarters
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const int kg = (lane & 7) >> 1;
+            if ((lane & ~6) == 0) kred[(half * 4 + quarter) * 4 + kg] = mx;   // lanes 0, 2, 4, 6
+            half_sync(half);
+            mx = fmaxf(fmaxf(kred[(half * 4 + 0) * 4 + kg], kred[(half * 4 + 1) * 4 + kg]),
+                       fmaxf(kred[(half * 4 + 2) * 4 + kg], kred[(half * 4 + 3) * 4 + kg]));
+            sc = fmaf(mx, 1.f / 127.f, 1e-7f);
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(sc));
+            if (quarter == 0 && part_ok && (lane & ~6) == 0 && hd.ks != nullptr)
+              hd.ks[(int64_t(head) * hd.parts + part) * 4 + kg] = sc;
+          }
+          int8_t* codes = g == 0 ? hd.qi : hd.ki;
+          if (row_ok && codes != nullptr) {
+            uint4* out = reinterpret_cast<uint4*>(codes + (int64_t(head) * p.m + row) * 128);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              out[q] = make_uint4(codes4_rni(v[16 * q], v[16 * q + 1], v[16 * q + 2], v[16 * q + 3], inv),
+                                  codes4_rni(v[16 * q + 4], v[16 * q + 5], v[16 * q + 6], v[16 * q + 7], inv),
+                                  codes4_rni(v[16 * q + 8], v[16 * q + 9], v[16 * q + 10], v[16 * q + 11], inv),
+                                  codes4_rni(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15], inv));
+          }
+        }
+      } else if constexpr (H3SK_TMEM_PREFETCH == 1 || (H3SK_TMEM_PREFETCH == 2 && kDual)) {
         // chunk c + 1's TMEM load is in flight while chunk c is computed
         uint32_t r[32];
         __syncwarp();
@@ -784,8 +1043,8 @@ bool make_output_map_heads(CUtensorMap* map, const void* base, int rows, int hea
 
 struct DeviceInfo {
   int sms = 0;
-  bool attrs_set[2][2][4] = {};   // [pair][dual][epilogue]
-  int max_pairs[2][4] = {};       // co-resident clusters of two CTAs, per [dual][epilogue]
+  bool attrs_set[2][2][kEpiKinds] = {};   // [pair][dual][epilogue]
+  int max_pairs[2][kEpiKinds] = {};       // co-resident clusters of two CTAs, per [dual][epilogue]
 };
 
 DeviceInfo& device_info(int device) {
@@ -853,11 +1112,14 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 
 int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
              void* D, int64_t ldd, const void* gate, const int32_t* rows, const void* residual, int M, int N,
-             int K, cudaStream_t stream, bool heads = false) {
+             int K, cudaStream_t stream, bool heads = false, const HeadsArgs* hd = nullptr) {
   if (!A || !B || !D || M < 1 || N < 1 || K < 16 || K % 16 || N % 8 || ldd < N || ldd % 8)
     return fail(cudaErrorInvalidValue, "h3_int8: invalid shape or null operand");
-  if (heads && (epi != kEpiDequant || N % 128))
+  if (heads && ((epi != kEpiDequant && epi != kEpiHeads) || N % 128))
     return fail(cudaErrorInvalidValue, "h3_int8: head-major output needs the dequant epilogue and N % 128 == 0");
+  if (epi == kEpiHeads && (!heads || !hd || hd->heads < 2 || hd->heads % 2 || N != 3 * hd->heads * 128 ||
+                           !hd->freqs || !hd->qw || !hd->kw))
+    return fail(cudaErrorInvalidValue, "h3_qkv: the fused head epilogue needs an even head count and N = 3*heads*128");
   if ((uintptr_t(A) & 15u) || (uintptr_t(B) & 15u) || (uintptr_t(D) & 15u))
     return fail(cudaErrorInvalidValue, "h3_int8: A, B and D must be 16-byte aligned");
   if (epi != kEpiAcc && (!xs || !ws || (uintptr_t(xs) & 3u) || (uintptr_t(ws) & 3u)))
@@ -892,6 +1154,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.n = N;
   p.k = K;
   p.head_major = heads ? 1 : 0;
+  if (hd) p.hd = *hd;
   p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
@@ -902,7 +1165,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return fail(cudaErrorInvalidDevice, "h3_int8: no device");
   const int approx_pairs = device_info(device).sms / 2;
-  const bool dual = pair && K >= kDualMinK && p.n_tiles % 2 == 0 &&
+  const bool dual = pair && epi != kEpiHeads && K >= kDualMinK && p.n_tiles % 2 == 0 &&
                     int64_t(p.m_tiles) * (p.n_tiles / 2) >= int64_t(kDualMinWaves) * approx_pairs;
   const int dual_n = dual ? 2 : 1;
   p.n_units = p.n_tiles / dual_n;
@@ -926,6 +1189,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiDequant: e = launch_gemm<kEpiDequant, true>(ma, mb, md, p, stream); break;
       case kEpiGelu: e = launch_gemm<kEpiGelu, true>(ma, mb, md, p, stream); break;
       case kEpiGate: e = launch_gemm<kEpiGate, true>(ma, mb, md, p, stream); break;
+      case kEpiHeads: e = launch_gemm<kEpiHeads, true>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, true>(ma, mb, md, p, stream); break;
     }
   } else {
@@ -933,6 +1197,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiDequant: e = launch_gemm<kEpiDequant, false>(ma, mb, md, p, stream); break;
       case kEpiGelu: e = launch_gemm<kEpiGelu, false>(ma, mb, md, p, stream); break;
       case kEpiGate: e = launch_gemm<kEpiGate, false>(ma, mb, md, p, stream); break;
+      case kEpiHeads: e = launch_gemm<kEpiHeads, false>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, false>(ma, mb, md, p, stream); break;
     }
   }
@@ -949,6 +1214,12 @@ int* status_device_ptr() { return status_ptr(); }
 int gemm_dequant_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int N,
                        int K, cudaStream_t stream) {
   return run_gemm(kEpiDequant, A, B, xs, ws, nullptr, D, N, nullptr, nullptr, nullptr, M, N, K, stream, true);
+}
+
+int gemm_qkv_heads(const int8_t* A, const int8_t* B, const float* xs, const float* ws, void* D, int M, int K,
+                   const HeadsArgs& hd, cudaStream_t stream) {
+  return run_gemm(kEpiHeads, A, B, xs, ws, nullptr, D, 3 * hd.heads * 128, nullptr, nullptr, nullptr, M,
+                  3 * hd.heads * 128, K, stream, true, &hd);
 }
 
 int last_gemm_error() { return t_last_error; }

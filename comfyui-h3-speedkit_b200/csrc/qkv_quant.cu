@@ -552,7 +552,26 @@ int qkv_run(const int8_t* A, const int8_t* B, const float* xs, const float* ws, 
     p.plane0 = 1;
     p.quant = 0;
     if (!launch_heads(p, 1, stream)) return 0;
+  } else if (rrms == nullptr && heads % 2 == 0) {
+    // The head epilogue inside the GEMM's epilogue warps: no Q/K plane round trip.
+    HeadsArgs hd{};
+    hd.freqs = p.freqs;
+    hd.qw = p.qw;
+    hd.kw = p.kw;
+    hd.sk = static_cast<const __nv_bfloat16*>(SK);
+    hd.anchors = anchors;
+    hd.qi = QI;
+    hd.qs = QS;
+    hd.ki = KI;
+    hd.ks = KS;
+    hd.vp = VP;
+    hd.eps = eps;
+    hd.heads = heads;
+    hd.parts = p.parts;
+    if (!gemm_qkv_heads(A, B, xs, ws, D, M, hidden, hd, stream)) return 0;
   } else {
+    // Odd head counts (a 256-column tile would straddle two heads' planes) and the
+    // rrms debug output: the GEMM writes the planes, a second kernel finishes them.
     if (!gemm_dequant_heads(A, B, xs, ws, D, M, int(3 * plane), hidden, stream)) return 0;
     p.sk = static_cast<const __nv_bfloat16*>(SK);
     p.anchors = anchors;

@@ -1,15 +1,17 @@
 """GPU parity of the QKV op: projection -> pre-quantised attention operands.
 
-Pinned against the reference's own kernels where they build without CUTLASS:
-  * the sample-row gather (r82_sample_konly.cu:345-357) and
-  * the K anchor detector (r79_sample_anchor.cu:467-605)
-run from oracle/_ref on the same inputs and must give the same bits.
-The QKV epilogue itself (r84_kfourwarp.cu:193-375) is only in a CUTLASS kernel
-the oracle build cannot compile, so it is checked against the CPU restatement
-(oracle/qkv.py, h3_oracle.c) with the GPU's rrms injected: D, the scales, the
-V maxima, V scales and the anchors must be bit-exact; the INT8 codes may differ
-by 1 where rcp.approx (GPU) and the correctly rounded 1/scale (CPU) put
-v * inv on opposite sides of a rounding boundary.
+The QKV GEMM with its head epilogue is pinned to the reference's own
+r84_kfourwarp.cu in tests/test_gpu_ref_gemm.py.  Here:
+  * the sample-row gather (r82_sample_konly.cu:345-357) and the K anchor
+    detector (r79_sample_anchor.cu:467-605) run from oracle/_ref on the same
+    inputs and must give the same bits;
+  * the whole op (any head count and hidden size) is checked against the CPU
+    restatement (oracle/qkv.py, h3_oracle.c) with the GPU's rrms injected: D,
+    the scales, the V maxima, V scales and the anchors must be bit-exact; the
+    INT8 codes may differ by 1 where rcp.approx (GPU) and the correctly rounded
+    1/scale (CPU) put v * inv on opposite sides of a rounding boundary;
+  * the head epilogue fused into the GEMM's epilogue warps equals the two-kernel
+    form (GEMM, then the separate head kernel) bit for bit.
 """
 import numpy as np
 import pytest
@@ -166,3 +168,22 @@ def test_h3_geometry_call_matches_cpu_restatement(device):
     _compare(dbg, ref, cpu_args[0])
     with pytest.raises(ValueError, match="H3 56 x 128"):
         op(args[0][:, :256].contiguous(), *args[1:], 1e-6)
+
+
+@pytest.mark.parametrize("m,heads,hidden,offset", [(300, 2, 256, 0.5), (200, 2, 256, 0.7), (1, 2, 256, 0.0),
+                                                   (1000, 4, 512, 0.8), (129, 2, 1024, 0.0), (257, 6, 256, 0.9),
+                                                   (4096, 56, 5376, 0.6)])
+def test_fused_head_epilogue_equals_the_two_kernel_form(device, m, heads, hidden, offset):
+    """h3_qkv_quant_kv_ex runs the head epilogue inside the GEMM's epilogue warps
+    for an even head count; with the rrms debug output it runs the GEMM and the
+    separate head kernel instead.  Both forms (and the anchors they share) must
+    give the same bits: D, Q/K codes and scales, V maxima."""
+    args, _ = _inputs(m, heads, hidden, 31 * m + heads, device, offset)
+    op = QKV()
+    fused = op.run(*args, 1e-6)
+    split = op.run(*args, 1e-6, debug=True)
+    torch.cuda.synchronize()
+    assert torch.equal(fused["anchors"], split["anchors"])
+    assert torch.equal(fused["d"].view(torch.int16), split["d"].view(torch.int16)), "D planes"
+    for key in ("qi", "ki", "qs", "ks", "vp", "vs", "vi"):
+        assert torch.equal(fused[key], split[key]), key

@@ -190,3 +190,35 @@ def test_h3_qkv_quant_kv_equals_reference_r84(device, m, anchored):
             kw.data_ptr(), 1e-6, p["qi"], p["qs"], p["vp"], p["ki"], p["ks"], sk.data_ptr(), anchors.data_ptr(),
             m, st))
         print(f"\nh3_qkv_quant_kv M={m}: reference r84 {t_ref:.3f} ms, ours {t_ours:.3f} ms")
+
+
+def test_cfg1_w8a8_linear_end_to_end_against_reference_kernels(device):
+    """BASELINE config 1 end to end on its seeded inputs (synthetic.cfg1: X BF16
+    [1024, 2048] with 8 outlier channels x30, W [2048, 2048], bias [2048]): X per
+    token and W per output channel through ConvRot256 + INT8 (this build's
+    quantiser vs the reference's Kitchen kernel: same codes and scales), then the
+    INT8 GEMM with the dequant epilogue (this build vs the reference's fc1.cu: same
+    BF16 output), and with the bias, which the reference GEMM lacks, against the C
+    restatement of r84_kfourwarp.cu:240's explicit formula (same bits)."""
+    from h3_speedkit import synthetic
+    from h3_speedkit.ops.convrot import quantize_int8_rowwise_convrot64
+    from helpers import bf16_bits, np_
+    from oracle import cpu as ocpu
+    _need("ref_fc1.so")
+    inp = synthetic.cfg1()
+    x, w, bias = (inp[k].to(device) for k in ("x", "w", "bias"))
+    xq, xs = quantize_int8_rowwise_convrot64(x)
+    wq, ws = quantize_int8_rowwise_convrot64(w)
+    rxq, rxs = ref_gpu.kitchen_quant(x, 0)
+    rwq, rws = ref_gpu.kitchen_quant(w, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(xq, rxq) and torch.equal(xs.view(-1), rxs.view(-1)), "activation codes / scales"
+    assert torch.equal(wq, rwq) and torch.equal(ws.view(-1), rws.view(-1)), "weight codes / scales"
+    y = gemm.int8_linear(xq, wq, xs.view(-1), ws.view(-1))
+    ref = ref_gpu.int8(rxq, rwq, rxs.view(-1), rws.view(-1), config=3)
+    yb = gemm.int8_linear(xq, wq, xs.view(-1), ws.view(-1), bias=bias)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), "dequant output vs fc1.cu"
+    acc = ocpu.gemm_s32(np_(xq), np_(wq))
+    want = ocpu.dequant(acc, np_(xs).reshape(-1), np_(ws).reshape(-1), bf16_bits(bias))
+    assert np.array_equal(bf16_bits(yb), want), "dequant + bias vs the C restatement"

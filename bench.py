@@ -724,10 +724,14 @@ def run_qkv(args):
     vq_ms = _median_ms(lambda _: lib.h3_quant_v(out["vp"].data_ptr(), v.data_ptr(), out["vi"].data_ptr(),
                                                 out["vs"].data_ptr(), out["vinv"].data_ptr(), m, heads, st),
                        warmup=3, iters=max(3, args.steps))
-    # bytes the head epilogue must move: Q/K planes read + written, codes and
-    # scales written, V plane read (its maxima written)
-    parts = (m + 127) // 128
-    epi_bytes = 2 * (2 * m * heads * 128 * 2) + 2 * m * heads * 128 + heads * parts * 36 * 4 + m * heads * 128 * 2
+    # the QKV GEMM with its head epilogue fused (one launch), timed alone: its
+    # tensor roofline, and its cost over the plain dequant GEMM
+    fused_ms = _median_ms(lambda _: lib.h3_qkv_quant_kv_ex(
+        q.data_ptr(), w.data_ptr(), xs.data_ptr(), ws.data_ptr(), out["d"].data_ptr(), args_dev[4].data_ptr(),
+        args_dev[5].data_ptr(), args_dev[6].data_ptr(), ct.c_float(1e-6), out["qi"].data_ptr(),
+        out["qs"].data_ptr(), out["vp"].data_ptr(), out["ki"].data_ptr(), out["ks"].data_ptr(),
+        out["sk"].data_ptr(), out["anchors"].data_ptr(), m, heads, hidden, None, st),
+        warmup=3, iters=max(3, args.steps))
     # end to end: q and the RoPE rows from pinned host memory, the three code
     # tensors and their scales back to pinned host memory, inside the timed region
     pin = lambda t: t.pin_memory()
@@ -760,15 +764,13 @@ def run_qkv(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg,
         "tops": ops / (ms / 1e3) / 1e12,
-        "kernels_ms": {"op": ms, "gemm_alone": gemm_ms, "v_quant": vq_ms,
-                       "head_epilogue_and_samples": ms - gemm_ms - vq_ms},
-        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
-                     "frac": gemm_tops / int8_peak, "traffic": None,
-                     "peak_source": "burst INT8: " + i8["burst_source"]},
-        "roofline_epilogue": {"bound": "hbm", "bytes": epi_bytes,
-                              "achieved": epi_bytes / max(1e-9, (ms - gemm_ms - vq_ms) / 1e3) / 1e9,
-                              "peak": hbm_peak, "unit": "GB/s",
-                              "frac": epi_bytes / max(1e-9, (ms - gemm_ms - vq_ms) / 1e3) / 1e9 / hbm_peak},
+        "kernels_ms": {"op": ms, "gemm_alone": gemm_ms, "gemm_with_head_epilogue": fused_ms, "v_quant": vq_ms,
+                       "samples_and_anchors": ms - fused_ms - vq_ms},
+        "roofline": {"bound": "tensor", "kernel": "int8_gemm_persistent (fused QKV head epilogue)",
+                     "achieved": ops / (fused_ms / 1e3) / 1e12, "peak": int8_peak, "unit": "TOPS",
+                     "frac": ops / (fused_ms / 1e3) / 1e12 / int8_peak, "traffic": None,
+                     "peak_source": "burst INT8: " + i8["burst_source"],
+                     "gemm_alone_tops": gemm_tops, "head_epilogue_cost": fused_ms / gemm_ms - 1.0},
         "e2e": {"value": m / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "cpu_baseline": None if args.no_cpu_baseline else {

@@ -1,0 +1,560 @@
+// INT8 attention of the H3 block on B200 (sm_100a): the consumer of the QKV op's
+// pre-quantised operands (kernels/dense/dense_ring.cu:32-94 and
+// qk_int_sv_i8_cuda.cuh of H3 SpeedKit, a SageAttention-derived mma.sync kernel
+// for SM120).  Same C ABI (H3DenseArgs, h3_dense_*), same arithmetic, written
+// for tcgen05: S = Q K^T and O_blk = P V run as kind::i8 MMAs with int32
+// accumulators in TMEM, and one thread owns one query row for the softmax.
+//
+// Operands (one batch, any head count; qo_heads % kv_heads == 0):
+//   Q  INT8 [B, Hq, Sq, 128], one FP32 scale per 4 rows {32b + s + 8j} of a
+//      128-row block:           QS [B, Hq, ceil(Sq/128) * 32]
+//   K  INT8 [B, Hk, Sk, 128], one FP32 scale per 128-key block and key class
+//      t = (key % 8) / 2:       KS [B, Hk, ceil(Sk/128) * 4]
+//   V  INT8 [B*Hk*128, ceil(Sk/128)*128] channel-major, keys permuted inside
+//      every run of 16 as [0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15];  VS [B*Hk*128]
+//   O  BF16, BHSD or BSHD strides.
+//
+// Arithmetic, per query row and 128-key block j (the reference's, exactly):
+//   s = int32 Q.K (exact; float(s) is exact, |s| < 2^22);
+//   per key class t: scale_t = (sm_scale * log2e) * (q_scale * k_scale[j][t]);
+//   m_t = fmaf(max_t(s), scale_t, -7.9943534), tile_m = max_t m_t,
+//   m = max(m_prev, tile_m), r = ex2(-|m_prev - tile_m|),
+//   o_scale = m_prev < tile_m ? r : 1, tile_scale = tile_m < m_prev ? r : 1;
+//   d_t *= o_scale, O *= o_scale (the per-row state is rescaled);
+//   p = ex2(fmaf(s, scale_t, -tile_m)), P = u8(rni, saturated);
+//   blocks before the last: d_t = fmaf(sum of the 4 P of (16-key tile, t), tile_scale, d_t)
+//   (the integer sum dp4a gives, as a float), tile by tile;
+//   the last block: keys >= Sk score -1e30, the row maximum starts at -50000,
+//   and d_t = fmaf((p0 + p1) + (p8 + p9), tile_scale, d_t) on the unrounded p;
+//   O = fmaf(float(int32 P.V), tile_scale, O);
+//   at the end d = (d_0 + d_1) + (d_2 + d_3), O = (O * rcp.approx(d)) * v_scale, BF16.
+// The 4 "key classes" t are the 4 threads of a quad of the reference's mma.sync
+// layout; their partial maxima and denominators are kept apart here so that
+// every FP32 operation has the reference's operands in the reference's order.
+// The unit is compiled with --use_fast_math, like the reference's dense unit.
+//
+// Roles (192 threads): warp 0 TMA producer (Q once, K and V tiles into a ring),
+// warp 1 TMEM owner and MMA issuer, warps 2-5 the softmax / output (thread =
+// query row = TMEM lane).  Every mbarrier wait is bounded (2 s) and reports a
+// status code instead of hanging.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace h3sk {
+namespace attn {
+
+using namespace sm100;
+
+constexpr int kRows = 128;             // query rows per CTA (TMEM lanes)
+constexpr int kKeys = 128;             // keys per block
+constexpr int kDim = 128;              // head dimension
+constexpr int kTileBytes = 128 * 128;  // one INT8 [128 x 128] tile
+constexpr int kStages = 3;             // K and V ring depth
+constexpr int kThreads = 192;
+constexpr float kExpOffset = 7.9943534f;          // attn_utils.cuh:40 (S_U8_OFFSET)
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+struct Args {
+  int q_heads, kv_heads, batch;
+  int q_len, kv_len, q_blocks, kv_blocks;
+  int q_block_start;
+  const float* qs;   // [B, Hq, q_blocks * 32]
+  const float* ks;   // [B, Hk, kv_blocks * 4]
+  const float* vs;   // [B * Hk * 128]
+  __nv_bfloat16* o;
+  int64_t o_sb, o_sh, o_ss;   // element strides
+  float sm_scale;
+  int* status;
+};
+
+struct Smem {
+  // 1024-aligned operand tiles (128-byte swizzle)
+  uint8_t q[kTileBytes];
+  uint8_t k[kStages][kTileBytes];
+  uint8_t v[kStages][kTileBytes];
+  uint8_t p[kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full, s_empty, p_full, o_full, o_empty, drain;
+  uint32_t tmem;
+  int abort;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp(float x) {
+  float y;
+  asm volatile("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Four probabilities -> four u8 codes (cvt.rni.s32 then a saturating pack;
+// mma.cuh:769-786), low byte = a.
+__device__ __forceinline__ uint32_t u8x4(float a, float b, float c, float d) {
+  uint32_t qa, qb, qc, qd, hi, w;
+  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qa) : "f"(a));
+  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qb) : "f"(b));
+  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qc) : "f"(c));
+  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qd) : "f"(d));
+  asm volatile("cvt.pack.sat.u8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(qd), "r"(qc));
+  asm volatile("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(qb), "r"(qa), "r"(hi));
+  return w;
+}
+__device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// mbarrier wait by lane 0 of a warp, verdict shared with the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Smem& sm, int* status, int code) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0)
+    ok = mbar_wait_bounded(bar, parity, reinterpret_cast<volatile int*>(&sm.abort), status, code, kTimeoutNs) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Instruction descriptors (sm100.cuh idesc_i8 fields): s8 x s8 and u8 x s8, M=N=128.
+constexpr uint32_t kIdescQK = idesc_i8(kRows, kKeys);
+constexpr uint32_t kIdescPV = idesc_i8(kRows, kDim) & ~(7u << 7);   // A format 0 = u8
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bx = int(blockIdx.x) + a.q_block_start;     // 128-row query block
+  const int head = int(blockIdx.y), batch = int(blockIdx.z);
+  const int kv_head = head / (a.q_heads / a.kv_heads);
+  const int bh_q = batch * a.q_heads + head, bh_k = batch * a.kv_heads + kv_head;
+  const int nblk = a.kv_blocks;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.o_full, 1);
+    mbar_init(&sm.s_empty, 4);
+    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.o_empty, 4);
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_map(&map_q);
+    tma_prefetch_map(&map_k);
+    tma_prefetch_map(&map_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+  const uint32_t t_s = tmem, t_o = tmem + 128, t_ro = tmem + 256;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    int issued = 0;
+    bool ok = true;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
+      tma_load_3d(sm.q, &map_q, &sm.q_full, 0, bx * kRows, bh_q);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = uint32_t(j / kStages) & 1u;
+        if (j >= kStages) {
+          ok = mbar_wait_bounded(&sm.k_empty[s], ph ^ 1u, reinterpret_cast<volatile int*>(&sm.abort), a.status, 41,
+                                 kTimeoutNs);
+          if (ok)
+            ok = mbar_wait_bounded(&sm.v_empty[s], ph ^ 1u, reinterpret_cast<volatile int*>(&sm.abort), a.status,
+                                   42, kTimeoutNs);
+        }
+        if (!ok) break;
+        mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
+        tma_load_3d(sm.k[s], &map_k, &sm.k_full[s], 0, j * kKeys, bh_k);
+        mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
+        tma_load_3d(sm.v[s], &map_v, &sm.v_full[s], j * kKeys, 0, bh_k);
+        issued = j + 1;
+      }
+      // every copy this CTA issued lands before the CTA exits
+      mbar_wait_bounded(&sm.q_full, 0, nullptr, a.status, 43, kTimeoutNs);
+      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j) {
+        const uint32_t ph = uint32_t(j / kStages) & 1u;
+        mbar_wait_bounded(&sm.k_full[j % kStages], ph, nullptr, a.status, 43, kTimeoutNs);
+        mbar_wait_bounded(&sm.v_full[j % kStages], ph, nullptr, a.status, 43, kTimeoutNs);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    bool ok = warp_wait(&sm.q_full, 0, sm, a.status, 51);
+    const uint64_t qd = smem_desc_k_sw128(sm.q), pd = smem_desc_k_sw128(sm.p);
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int s = j % kStages;
+      const uint32_t ph = uint32_t(j / kStages) & 1u;
+      ok = warp_wait(&sm.k_full[s], ph, sm, a.status, 52) &&
+           (j == 0 || warp_wait(&sm.s_empty, uint32_t(j - 1) & 1u, sm, a.status, 53));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t kd = smem_desc_k_sw128(sm.k[s]);
+#pragma unroll
+        for (int kk = 0; kk < kDim / 32; ++kk) mma_i8(t_s, qd + uint64_t(2 * kk), kd + uint64_t(2 * kk), kIdescQK, kk);
+        mma_commit(&sm.k_empty[s]);
+        mma_commit(&sm.s_full);
+      }
+      __syncwarp();
+      ok = warp_wait(&sm.p_full, uint32_t(j) & 1u, sm, a.status, 54) &&
+           warp_wait(&sm.v_full[s], ph, sm, a.status, 55) &&
+           (j == 0 || warp_wait(&sm.o_empty, uint32_t(j - 1) & 1u, sm, a.status, 56));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t vd = smem_desc_k_sw128(sm.v[s]);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 32; ++kk) mma_i8(t_o, pd + uint64_t(2 * kk), vd + uint64_t(2 * kk), kIdescPV, kk);
+        mma_commit(&sm.v_empty[s]);
+        mma_commit(&sm.o_full);
+      }
+      __syncwarp();
+    }
+    // every MMA issued here completes before TMEM is released
+    if (lane == 0) {
+      mma_commit(&sm.drain);
+      mbar_wait_bounded(&sm.drain, 0, nullptr, a.status, 57, kTimeoutNs);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax and output: thread = query row ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                  // row within the block (TMEM lane)
+    const int row = bx * kRows + r;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const float q_scale = a.qs[int64_t(bh_q) * a.q_blocks * 32 + bx * 32 + (r >> 5) * 8 + (r & 7)];
+    const float sm_base = a.sm_scale * kLog2e;
+    float m = -50000.0f;
+    float d[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+    bool ok = true;
+    int j = 0;
+    for (; j < nblk; ++j) {
+      const bool last = j == nblk - 1;
+      if (!warp_wait(&sm.s_full, uint32_t(j) & 1u, sm, a.status, 61)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float scale[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        scale[t] = sm_base * (q_scale * a.ks[int64_t(bh_k) * nblk * 4 + j * 4 + t]);
+      // pass 1: the per-class maxima (integers; in the last block, floats with
+      // the keys past Sk at -1e30 and the maximum starting at -50000)
+      float mt[4];
+      if (!last) {
+        int imax[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
+          tmem_load_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) imax[(i & 7) >> 1] = max(imax[(i & 7) >> 1], int(v[i]));
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) mt[t] = fmaf(float(imax[t]), scale[t], -kExpOffset);
+      } else {
+        float fmax_[4] = {-50000.0f, -50000.0f, -50000.0f, -50000.0f};
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
+          tmem_load_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = j * kKeys + 32 * c + i;
+            const float sc = key < a.kv_len ? float(int(v[i])) : -1.0e30f;
+            fmax_[(i & 7) >> 1] = fmaxf(fmax_[(i & 7) >> 1], sc);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) mt[t] = fmaf(fmax_[t], scale[t], -kExpOffset);
+      }
+      const float tile_m = fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3]));
+      const float m_prev = m;
+      m = fmaxf(m_prev, tile_m);
+      const float smaller = ex2(-fabsf(m_prev - tile_m));
+      const float o_scale = m_prev < tile_m ? smaller : 1.0f;
+      const float tile_scale = tile_m < m_prev ? smaller : 1.0f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) d[t] *= o_scale;
+      // pass 2: probabilities -> u8 P (key order of V: the four keys of class t
+      // of each 16-key run in one word at byte 4t), denominators
+      const float neg_m = -tile_m;
+      uint8_t* prow = sm.p + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
+        tmem_load_wait();
+#pragma unroll
+        for (int run = 0; run < 2; ++run) {      // 16-key runs of this chunk
+          uint32_t words[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int i0 = 16 * run + 2 * t, i1 = i0 + 1, i2 = i0 + 8, i3 = i0 + 9;
+            float s0 = float(int(v[i0])), s1 = float(int(v[i1])), s2 = float(int(v[i2])), s3 = float(int(v[i3]));
+            if (last) {
+              const int k0 = j * kKeys + 32 * c;
+              if (k0 + i0 >= a.kv_len) s0 = -1.0e30f;
+              if (k0 + i1 >= a.kv_len) s1 = -1.0e30f;
+              if (k0 + i2 >= a.kv_len) s2 = -1.0e30f;
+              if (k0 + i3 >= a.kv_len) s3 = -1.0e30f;
+            }
+            const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
+            const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
+            words[t] = u8x4(p0, p1, p2, p3);
+            if (!last) {
+              const float den = __uint2float_rn(__dp4a(words[t], 0x01010101u, 0u));
+              d[t] = fmaf(den, tile_scale, d[t]);
+            } else {
+              d[t] = fmaf((p0 + p1) + (p2 + p3), tile_scale, d[t]);
+            }
+          }
+          const int chunk = 2 * c + run;          // 16-byte chunk of the P row
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
+                                                                                 words[3]);
+        }
+      }
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.s_empty);
+        mbar_arrive(&sm.p_full);
+      }
+      // O <- fmaf(float(P.V), tile_scale, O * o_scale)
+      if (!warp_wait(&sm.o_full, uint32_t(j) & 1u, sm, a.status, 62)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pv[32], ro[32];
+        __syncwarp();
+        tmem_load_32cols(t_o + lane_off + uint32_t(32 * c), pv);
+        if (j > 0) tmem_load_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
+        tmem_load_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float o = j > 0 ? __uint_as_float(ro[i]) : 0.0f;
+          if (o_scale != 1.0f) o = o * o_scale;
+          ro[i] = __float_as_uint(fmaf(float(int(pv[i])), tile_scale, o));
+        }
+        tmem_store_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
+      }
+      tmem_store_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.o_empty);
+    }
+    if (ok && j == nblk) {
+      tc_fence_after();
+      const float den = (d[0] + d[1]) + (d[2] + d[3]);
+      const float inv = rcp(den);
+      const float* vs = a.vs + int64_t(bh_k) * kDim;
+      __nv_bfloat16* out = a.o + int64_t(batch) * a.o_sb + int64_t(head) * a.o_sh + int64_t(row) * a.o_ss;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ro[32];
+        __syncwarp();
+        tmem_load_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
+        tmem_load_wait();
+        if (row < a.q_len) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float o0 = (__uint_as_float(ro[i]) * inv) * __ldg(vs + 32 * c + i);
+            const float o1 = (__uint_as_float(ro[i + 1]) * inv) * __ldg(vs + 32 * c + i + 1);
+            __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
+            packed[i / 2] = *reinterpret_cast<uint32_t*>(&h);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            reinterpret_cast<uint4*>(out + 32 * c)[q] =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace attn
+}  // namespace h3sk
+
+// ---- C ABI: the reference's h3_dense_* (dense_ring.cu:16-107) -------------------------
+
+struct H3DenseArgs {
+  void *q, *k, *v, *o, *q_scale, *k_scale, *v_scale;
+  uint32_t batch, qo_len, kv_len, qo_heads, kv_heads;
+  uint32_t q_stride_b, q_stride_h, q_stride_s;
+  uint32_t k_stride_b, k_stride_h, k_stride_s;
+  uint32_t v_stride_b, v_stride_h, v_stride_d;
+  uint32_t o_stride_b, o_stride_h, o_stride_s;
+  float sm_scale;
+};
+
+#define H3SK_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+bool encode_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2) {
+  auto fn = h3sk::tensor_map_encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+H3SK_EXPORT size_t h3_dense_args_size(void) { return sizeof(H3DenseArgs); }
+// The reference reports its build's experiment id here (H3_VARIANT_ID); this
+// library implements the arithmetic of variant 8102.
+H3SK_EXPORT int h3_dense_query_group(void) { return 8102; }
+H3SK_EXPORT const char* h3_dense_error_string(int code) {
+  return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
+
+H3SK_EXPORT int h3_dense_launch_window(const H3DenseArgs* a, uintptr_t stream_ptr, uint32_t start) {
+  using namespace h3sk::attn;
+  if (!a || !a->q || !a->k || !a->v || !a->o || !a->q_scale || !a->k_scale || !a->v_scale || !a->batch ||
+      !a->qo_len || !a->kv_len || !a->qo_heads || !a->kv_heads || a->qo_heads % a->kv_heads != 0)
+    return cudaErrorInvalidValue;
+  const uint64_t q_blocks = (a->qo_len + 127) / 128, kv_blocks = (a->kv_len + 127) / 128;
+  // the operand layouts of the QKV op (and of the reference's own checks,
+  // dense_ring.cu:44-47): Q and K contiguous [B, H, S, 128], V [B*Hk*128, padded Sk]
+  if (a->q_stride_s != 128 || a->q_stride_h != a->qo_len * 128 || a->q_stride_b != a->qo_heads * a->q_stride_h ||
+      a->k_stride_s != 128 || a->k_stride_h != a->kv_len * 128 || a->k_stride_b != a->kv_heads * a->k_stride_h ||
+      a->v_stride_h != 128 * a->v_stride_d || a->v_stride_b != a->kv_heads * a->v_stride_h ||
+      a->v_stride_d < kv_blocks * 128 || a->v_stride_d % 16)
+    return cudaErrorInvalidValue;
+  const bool bhsd = a->o_stride_s == 128 && a->o_stride_h == a->qo_len * 128;
+  const bool bshd = a->o_stride_s == a->qo_heads * 128 && a->o_stride_h == 128;
+  if (!bhsd && !bshd) return cudaErrorInvalidValue;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) ||
+      (reinterpret_cast<uintptr_t>(a->q_scale) & 3u) || (reinterpret_cast<uintptr_t>(a->k_scale) & 3u) ||
+      (reinterpret_cast<uintptr_t>(a->v_scale) & 3u))
+    return cudaErrorInvalidValue;
+  if (!(a->sm_scale == a->sm_scale) || start >= q_blocks) return cudaErrorInvalidValue;
+  if (q_blocks > 65535u * 65535u || a->qo_heads > 65535u || a->batch > 65535u) return cudaErrorInvalidValue;
+  const cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  CUtensorMap mq, mk, mv;
+  if (!encode_3d(&mq, a->q, 128, a->qo_len, uint64_t(a->batch) * a->qo_heads, a->q_stride_s, a->q_stride_h) ||
+      !encode_3d(&mk, a->k, 128, a->kv_len, uint64_t(a->batch) * a->kv_heads, a->k_stride_s, a->k_stride_h) ||
+      !encode_3d(&mv, a->v, a->v_stride_d, 128, uint64_t(a->batch) * a->kv_heads, a->v_stride_d, a->v_stride_h))
+    return cudaErrorInvalidValue;
+  int* status = h3sk::status_device_ptr();
+  if (!status) return cudaErrorInvalidSymbol;
+  if (start) {
+    // rows before the window are zero (dense_ring.cu:68-80)
+    const size_t rows = size_t(start) * 128;
+    for (uint32_t b = 0; b < a->batch; ++b) {
+      char* base = static_cast<char*>(a->o) + size_t(b) * a->o_stride_b * 2;
+      cudaError_t e = bshd ? cudaMemsetAsync(base, 0, rows * a->qo_heads * 128 * 2, stream)
+                           : cudaMemset2DAsync(base, size_t(a->o_stride_h) * 2, 0, rows * 128 * 2, a->qo_heads, stream);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  Args args{};
+  args.q_heads = int(a->qo_heads);
+  args.kv_heads = int(a->kv_heads);
+  args.batch = int(a->batch);
+  args.q_len = int(a->qo_len);
+  args.kv_len = int(a->kv_len);
+  args.q_blocks = int(q_blocks);
+  args.kv_blocks = int(kv_blocks);
+  args.q_block_start = int(start);
+  args.qs = static_cast<const float*>(a->q_scale);
+  args.ks = static_cast<const float*>(a->k_scale);
+  args.vs = static_cast<const float*>(a->v_scale);
+  args.o = static_cast<__nv_bfloat16*>(a->o);
+  args.o_sb = a->o_stride_b;
+  args.o_sh = a->o_stride_h;
+  args.o_ss = a->o_stride_s;
+  args.sm_scale = a->sm_scale;
+  args.status = status;
+  const int smem = int(sizeof(Smem)) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid(unsigned(q_blocks - start), a->qo_heads, a->batch);
+  attention_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, args);
+  return cudaGetLastError();
+}
+
+H3SK_EXPORT int h3_dense_launch(const H3DenseArgs* a, uintptr_t stream) { return h3_dense_launch_window(a, stream, 0); }
+
+// numRegs, localSizeBytes, sharedSizeBytes (dynamic), maxThreadsPerBlock, binaryVersion
+// (the reference's field order, dense_ring.cu:96-104).
+H3SK_EXPORT int h3_dense_resources(int* out) {
+  if (!out) return cudaErrorInvalidValue;
+  cudaFuncAttributes attr;
+  const cudaError_t e = cudaFuncGetAttributes(&attr, h3sk::attn::attention_kernel);
+  if (e != cudaSuccess) return e;
+  out[0] = attr.numRegs;
+  out[1] = int(attr.localSizeBytes);
+  out[2] = int(sizeof(h3sk::attn::Smem)) + 1024;
+  out[3] = attr.maxThreadsPerBlock;
+  out[4] = attr.binaryVersion;
+  return 0;
+}

@@ -10,8 +10,9 @@ The quantiser translation units are compiled with ``--use_fast_math`` exactly
 as the reference compiles its norm/convrot kernels (tools/build_kernels.py:32-34),
 because the quantiser's division must be the same operation; the GEMM unit is
 compiled without it and spells every epilogue rounding explicitly.  The QKV head
-epilogue is compiled without it and the K anchor detector with it, as the
-reference compiles its qkv/sample and anchor units (tools/build_kernels.py:35-37).
+epilogue is compiled without it and the K anchor detector and the INT8
+attention with it, as the reference compiles its qkv/sample, anchor and dense
+units (tools/build_kernels.py:30-37).
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ PKG = CSRC.parent
 NATIVE = PKG / "h3_speedkit" / "_native"
 BUILD = PKG / "_build"
 LIB_NAME = "libh3sk_b200.so"
-ALIASES = ("norm", "residual", "convrot", "fc1", "gate", "qkv", "sample", "anchor")
+ALIASES = ("norm", "residual", "convrot", "fc1", "gate", "qkv", "sample", "anchor", "dense")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-std=c++17", "-O3", "-DNDEBUG", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
           "--expt-relaxed-constexpr"]
@@ -39,6 +40,7 @@ UNITS = (
     ("int8_gemm.cu", []),
     ("qkv_quant.cu", []),
     ("anchor.cu", ["--use_fast_math"]),
+    ("attention.cu", ["--use_fast_math"]),
 )
 
 
@@ -94,7 +96,7 @@ def build(nvcc: str | None = None, force: bool = False, quiet: bool = True) -> P
     digest = sha256(lib)
     sources = {"norm": "norm_quant.cu", "residual": "norm_quant.cu", "convrot": "convrot_quant.cu",
                "fc1": "int8_gemm.cu", "gate": "int8_gemm.cu", "qkv": "qkv_quant.cu", "sample": "qkv_quant.cu",
-               "anchor": "anchor.cu"}
+               "anchor": "anchor.cu", "dense": "attention.cu"}
     for name in ALIASES:
         alias = NATIVE / (name + ".so")
         if alias.is_symlink() or alias.exists():

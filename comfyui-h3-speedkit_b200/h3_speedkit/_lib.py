@@ -56,6 +56,12 @@ EXPORTS = {
     "h3_sample_anchor_ex": ([_P, _P, _I, _SZ], _I),
     "h3_quant_v": ([_P] * 5 + [_I, _I, _SZ], _I),
     "h3_qkv_noalloc": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _I, _I, _SZ], _I),
+    "h3_dense_args_size": ([], _SZ),
+    "h3_dense_query_group": ([], _I),
+    "h3_dense_error_string": ([_I], ct.c_char_p),
+    "h3_dense_launch_window": ([_P, _SZ, ct.c_uint32], _I),
+    "h3_dense_launch": ([_P, _SZ], _I),
+    "h3_dense_resources": ([_P], _I),
     "h3sk_pipeline_status": ([_P, _I, _SZ], _I),
     "h3sk_wait_selftest": ([_I, _P, _SZ], _I),
     "h3sk_int8_mma_peak": ([_I, _P, _SZ], _I),

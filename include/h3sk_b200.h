@@ -329,6 +329,46 @@ int h3_qkv_noalloc(const int8_t* A, const int8_t* B, const float* xs, const floa
                    uintptr_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* INT8 attention on the QKV op's operands (SageAttention-style, D = 128)     */
+/* ------------------------------------------------------------------------ */
+
+/* Argument block of kernels/dense/dense_ring.cu:16-24 (same field order and types).
+ * Strides are in elements.  q [B, Hq, Sq, 128] and k [B, Hk, Sk, 128] INT8 contiguous;
+ * v INT8 [B*Hk*128, v_stride_d] channel-major, v_stride_d >= ceil(Sk/128)*128 tokens,
+ * keys permuted in every run of 16 as [0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15];
+ * o BF16 BHSD or BSHD; q_scale FP32 [B, Hq, ceil(Sq/128)*32], k_scale FP32
+ * [B, Hk, ceil(Sk/128)*4], v_scale FP32 [B*Hk*128]; sm_scale = head_dim^-0.5. */
+typedef struct H3DenseArgs {
+  void *q, *k, *v, *o, *q_scale, *k_scale, *v_scale;
+  uint32_t batch, qo_len, kv_len, qo_heads, kv_heads;
+  uint32_t q_stride_b, q_stride_h, q_stride_s;
+  uint32_t k_stride_b, k_stride_h, k_stride_s;
+  uint32_t v_stride_b, v_stride_h, v_stride_d;
+  uint32_t o_stride_b, o_stride_h, o_stride_s;
+  float sm_scale;
+} H3DenseArgs;
+
+/* Replaces h3_dense_args_size (dense_ring.cu:26). */
+size_t h3_dense_args_size(void);
+/* Replaces h3_dense_query_group (dense_ring.cu:27): the arithmetic variant, 8102. */
+int h3_dense_query_group(void);
+/* Replaces h3_dense_error_string (dense_ring.cu:28-30): cudaGetErrorString. */
+const char* h3_dense_error_string(int code);
+/*
+ * Replaces h3_dense_launch_window (dense_ring.cu:32-94): O = softmax(Q K^T * scales) V
+ * with the reference's INT8 arithmetic (u8 probabilities, int32 P.V, FP32 running
+ * rescale), rows of query blocks [start, ceil(Sq/128)); the rows before block
+ * `start` are set to zero.  Returns a cudaError_t (0 = success); a rejected
+ * argument launches nothing.
+ */
+int h3_dense_launch_window(const H3DenseArgs* args, uintptr_t stream, uint32_t start);
+/* Replaces h3_dense_launch (dense_ring.cu:107): the window from block 0. */
+int h3_dense_launch(const H3DenseArgs* args, uintptr_t stream);
+/* Replaces h3_dense_resources (dense_ring.cu:96-105): out[5] = registers, local
+ * bytes, shared bytes, max threads per block, binary version. */
+int h3_dense_resources(int* out);
+
+/* ------------------------------------------------------------------------ */
 /* Pipeline health and diagnostics                                           */
 /* ------------------------------------------------------------------------ */
 

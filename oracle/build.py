@@ -28,6 +28,10 @@
        ``-DCOMFY_HAVE_CUTLASS -DH3_EVT_STAGES=2``;
      * ``ref_gate.so``       kernels/gemm/gate.cu, unmodified (``h3_int8_gate``,
        the gate-residual EVT epilogue, configs 0 and 13), ``-DH3_EVT_STAGES=1``;
+     * ``ref_dense.so``      kernels/dense/dense_ring.cu, unmodified (the INT8
+       attention ``h3_dense_launch_window``, variant 8102), with the reference's
+       dense flags (``--use_fast_math -lineinfo --maxrregcount=168
+       -DH3_VARIANT_ID=8102 -lcuda``) and ``sm_100a`` in place of ``sm_120a``;
      * ``ref_qkv.so``        kernels/gemm/r84_kfourwarp.cu, unmodified
        (``h3_qkv_quant_kv``, the QKV GEMM fused with the per-head RMS / RoPE /
        rotation / quantisation epilogue), ``-DH3_EVT_STAGES=2``.
@@ -155,6 +159,12 @@ def build_ref(force: bool = False) -> list[Path]:
         _compile(nvcc, launcher, target, [vendor], ["--use_fast_math"])
     built.append(target)
     built += _build_ref_gemms(nvcc, gemm_dir, force)
+    dense_dir = kernels / "dense"
+    target = REF_OUT / "ref_dense.so"
+    if force or not _newer(target, *sorted(dense_dir.glob("*"))):
+        _compile(nvcc, dense_dir / "dense_ring.cu", target, [dense_dir],
+                 ["--use_fast_math", "-lineinfo", "--maxrregcount=168", "-DH3_VARIANT_ID=8102", "-lcuda"])
+    built.append(target)
     return built
 
 

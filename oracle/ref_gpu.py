@@ -3,8 +3,8 @@
 Loads the libraries ``oracle/build.py`` compiled into ``oracle/_ref`` from the
 reference sources (norm_quant.cu, residual_quant.cu, convrot_register_v2.cu, the
 vendored Kitchen quantiser, the K anchor detector, the sample-row gather, and the
-CUTLASS GEMMs fc1.cu, gate.cu and r84_kfourwarp.cu) and runs them on torch CUDA
-tensors.  Output buffers are
+CUTLASS GEMMs fc1.cu, gate.cu and r84_kfourwarp.cu, and the INT8 attention of
+dense_ring.cu) and runs them on torch CUDA tensors.  Output buffers are
 allocated by the caller-side helpers here with torch; nothing in the product
 path uses this module.
 """
@@ -215,3 +215,44 @@ def qkv_quant_kv(a, b, xs, ws, freqs, qw, kw, eps, sk, anchors):
           t["ki"].data_ptr(), t["ks"].data_ptr(), sk.data_ptr(), anchors.data_ptr(), m, _stream(a)) != 1:
         raise RuntimeError("reference h3_qkv_quant_kv refused or failed")
     return t
+
+
+class DenseArgs(ct.Structure):
+    """dense_ring.cu:16-24: seven pointers, seventeen uint32 sizes and strides, sm_scale."""
+    _fields_ = ([(n, ct.c_void_p) for n in ("q", "k", "v", "o", "q_scale", "k_scale", "v_scale")]
+                + [(n, ct.c_uint32) for n in ("batch", "qo_len", "kv_len", "qo_heads", "kv_heads",
+                                               "q_stride_b", "q_stride_h", "q_stride_s",
+                                               "k_stride_b", "k_stride_h", "k_stride_s",
+                                               "v_stride_b", "v_stride_h", "v_stride_d",
+                                               "o_stride_b", "o_stride_h", "o_stride_s")]
+                + [("sm_scale", ct.c_float)])
+
+
+def dense_args(q, k, v, qs, ks, vs, o, sm_scale):
+    """The argument block for q [B, H, S, 128], k [B, Hk, Sk, 128], v [B*Hk*128, padded],
+    o a BHSD-shaped view (BHSD or BSHD storage)."""
+    b, h, s, d = q.shape
+    hk, sk = k.shape[1:3]
+    padded = v.shape[1]
+    return DenseArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), qs.data_ptr(), ks.data_ptr(),
+                     vs.data_ptr(), b, s, sk, h, hk, *q.stride()[:3], *k.stride()[:3],
+                     hk * d * padded, d * padded, padded, *o.stride()[:3], float(sm_scale))
+
+
+def dense(q, k, v, qs, ks, vs, sm_scale, *, layout="bshd", start=0):
+    """Reference h3_dense_launch_window (dense_ring.cu:32-94): BF16 output, a BHSD view."""
+    import torch
+    so = _load("ref_dense.so")
+    fn = so.h3_dense_launch_window
+    fn.argtypes = [ct.POINTER(DenseArgs), ct.c_size_t, ct.c_uint32]
+    fn.restype = ct.c_int
+    b, h, s, d = q.shape
+    if layout == "bshd":
+        o = torch.empty((b, s, h, d), dtype=torch.bfloat16, device=q.device).transpose(1, 2)
+    else:
+        o = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=q.device)
+    args = dense_args(q, k, v, qs, ks, vs, o, sm_scale)
+    rc = fn(ct.byref(args), _stream(q), start)
+    if rc:
+        raise RuntimeError(f"reference h3_dense_launch_window failed with CUDA error {rc}")
+    return o

@@ -20,12 +20,15 @@
 //   m_t = fmaf(max_t(s), scale_t, -7.9943534), tile_m = max_t m_t,
 //   m = max(m_prev, tile_m), r = ex2(-|m_prev - tile_m|),
 //   o_scale = m_prev < tile_m ? r : 1, tile_scale = tile_m < m_prev ? r : 1;
-//   d_t *= o_scale, O *= o_scale (the per-row state is rescaled);
+//   d_t *= o_scale (but see the last block), O *= o_scale;
 //   p = ex2(fmaf(s, scale_t, -tile_m)), P = u8(rni, saturated);
 //   blocks before the last: d_t = fmaf(sum of the 4 P of (16-key tile, t), tile_scale, d_t)
 //   (the integer sum dp4a gives, as a float), tile by tile;
 //   the last block: keys >= Sk score -1e30, the row maximum starts at -50000,
-//   and d_t = fmaf((p0 + p1) + (p8 + p9), tile_scale, d_t) on the unrounded p;
+//   and d_t = fmaf((p0 + p1) + (p8 + p9), tile_scale, d_t) on the unrounded p,
+//   except that its first 16-key tile folds the rescale in:
+//   d_t = fmaf(d_t, o_scale, round(((p0 + p1) + (p8 + p9)) * tile_scale)) -- the
+//   contraction the reference's compiler picks on that straight-line path;
 //   O = fmaf(float(int32 P.V), tile_scale, O);
 //   at the end d = (d_0 + d_1) + (d_2 + d_3), O = (O * rcp.approx(d)) * v_scale, BF16.
 // The 4 "key classes" t are the 4 threads of a quad of the reference's mma.sync
@@ -321,8 +324,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float smaller = ex2(-fabsf(m_prev - tile_m));
       const float o_scale = m_prev < tile_m ? smaller : 1.0f;
       const float tile_scale = tile_m < m_prev ? smaller : 1.0f;
+      // blocks before the last rescale d_t on their own (the reference applies
+      // o_scale under a branch); the last block folds d_t * o_scale into its
+      // first denominator update, as the reference's straight-line float path
+      // compiles (fma(d, o_scale, round(sum * tile_scale)))
+      if (!last) {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) d[t] *= o_scale;
+        for (int t = 0; t < 4; ++t) d[t] *= o_scale;
+      }
       // pass 2: probabilities -> u8 P (key order of V: the four keys of class t
       // of each 16-key run in one word at byte 4t), denominators
       const float neg_m = -tile_m;
@@ -350,12 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
             const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
             words[t] = u8x4(p0, p1, p2, p3);
-            if (!last) {
-              const float den = __uint2float_rn(__dp4a(words[t], 0x01010101u, 0u));
-              d[t] = fmaf(den, tile_scale, d[t]);
-            } else {
-              d[t] = fmaf((p0 + p1) + (p2 + p3), tile_scale, d[t]);
-            }
+            const float add = last ? (p0 + p1) + (p2 + p3)
+                                   : __uint2float_rn(__dp4a(words[t], 0x01010101u, 0u));
+            if (last && c == 0 && run == 0)
+              d[t] = fmaf(d[t], o_scale, __fmul_rn(add, tile_scale));
+            else
+              d[t] = fmaf(add, tile_scale, d[t]);
           }
           const int chunk = 2 * c + run;          // 16-byte chunk of the P row
           *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],

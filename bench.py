@@ -64,9 +64,12 @@ def parse_args():
                     help="block geometry of the stack: cfg5 (default) or the H3 model's own (SwiGLU)")
     ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
                     help="5 (default): the 8-block stack; 1-4: the single-op BASELINE configs on one GPU")
-    ap.add_argument("--op", choices=("qkv",), default=None,
+    ap.add_argument("--op", choices=("qkv", "attention"), default=None,
                     help="qkv: the QKV op (projection -> pre-quantised attention operands) at the H3 "
-                         "geometry on one GPU, --tokens rows")
+                         "geometry on one GPU, --tokens rows; attention: the INT8 attention on those "
+                         "operands (56 heads, one sequence of --attn-tokens tokens)")
+    ap.add_argument("--attn-tokens", type=int, default=32768,
+                    help="sequence length of the --op attention line (default 32768)")
     return ap.parse_args()
 
 
@@ -782,12 +785,121 @@ def run_qkv(args):
     return 0
 
 
+def _attention_operands(m: int, heads: int, dev, seed: int = 4321):
+    """Seeded INT8 codes and FP32 scales in the QKV op's output layouts (Q/K
+    [1, H, S, 128], V channel-major [H*128, padded S], per-group scales), made
+    on the device."""
+    import torch
+    from h3_speedkit.ops.qkv import PrequantizedInt8Attention
+    g = torch.Generator(device=dev).manual_seed(seed)
+    parts = (m + 127) // 128
+    codes = lambda shape: torch.randint(-127, 128, shape, generator=g, device=dev, dtype=torch.int8)
+    rand = lambda shape: torch.rand(shape, generator=g, device=dev)
+    return PrequantizedInt8Attention(
+        q=codes((1, heads, m, 128)), k=codes((1, heads, m, 128)), v=codes((heads * 128, parts * 128)),
+        q_scale=rand((1, heads, parts * 32)) * 0.02 + 0.001, k_scale=rand((1, heads, parts * 4)) * 0.02 + 0.001,
+        v_scale=rand((heads * 128,)) * 0.01 + 0.0005, original_head_dim=128, input_dtype=torch.bfloat16,
+        attention_scale=128 ** -0.5, cta_k=128, attn_mask=None)
+
+
+def run_attention(args):
+    """The INT8 attention of the H3 block (56 heads x 128, one sequence of
+    --attn-tokens tokens attending to itself) on one GPU: h3_dense_launch_window
+    on the QKV op's operand layouts, BF16 output stored BSHD.  Median over
+    `--steps` launches after `--warmup`; Q, K and V (2.75 GB at 32768 tokens)
+    are larger than L2.  `--impl reference` times the reference's own kernel
+    (kernels/dense/dense_ring.cu, compiled from its sources into oracle/_ref) on
+    the same operands: the reference has no CPU attention to time."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import ctypes as ct
+    import torch
+
+    from h3_speedkit import _lib
+    from h3_speedkit.ops.dense import DenseLibrary, allocate_output
+    heads, m = 56, args.attn_tokens
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    packed = _attention_operands(m, heads, dev)
+    ops = 4.0 * m * m * 128 * heads          # Q K^T and P V, 2 ops per multiply-add
+    scores = float(m) * m * heads            # one ex2 per score
+    cfg = {"workload": f"INT8 attention, H3 geometry: 56 heads x 128, Sq = Sk = {m}, batch 1",
+           "tokens": m, "heads": heads, "head_dim": 128, "layout": "Q/K [1,H,S,128], V [H*128, S], O BSHD",
+           "l2": "inputs larger than L2", "timing": f"median of {args.steps} launches"}
+    base = {"metric": "INT8 attention TOPS (H3 geometry)", "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic", "config": cfg}
+    st = torch.cuda.current_stream().cuda_stream
+    if args.impl == "reference":
+        from oracle import ref_gpu
+        out = allocate_output(packed, "bshd")
+        ra = ref_gpu.dense_args(packed.q, packed.k, packed.v, packed.q_scale, packed.k_scale, packed.v_scale,
+                                out, packed.attention_scale)
+        fn = ref_gpu._load("ref_dense.so").h3_dense_launch_window
+        fn.argtypes = [ct.POINTER(ref_gpu.DenseArgs), ct.c_size_t, ct.c_uint32]
+        fn.restype = ct.c_int
+        ms = _median_ms(lambda _: fn(ct.byref(ra), st, 0), warmup=max(3, args.warmup), iters=max(3, args.steps))
+        value = ops / (ms / 1e3) / 1e12
+        line = dict(base, value=value, ms_per_step=ms, impl="reference",
+                    cpu_baseline={"value": value, "unit": "TOPS", "cores": 0, "kind": "reference",
+                                  "sample": "the reference's GPU kernel on the same operands (no CPU attention "
+                                            "exists in the reference)"},
+                    e2e={"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return 0
+    lib = _lib.load()
+    dense = DenseLibrary()
+    out = allocate_output(packed, "bshd")
+    call = dense.bind(packed, out)
+    gex2 = ct.c_double(0.0)
+    ex2_peak = gex2.value if lib.h3sk_ex2_peak(1 << 14, ct.byref(gex2), st) == 0 else None
+    clocks = ClockSampler()
+    clocks.start()
+    ms = _median_ms(lambda _: call(), warmup=max(3, args.warmup), iters=max(3, args.steps))
+    clock = clocks.stop()
+    if lib.h3sk_ex2_peak(1 << 14, ct.byref(gex2), st) == 0 and ex2_peak:
+        ex2_peak = max(ex2_peak, gex2.value)
+    i8 = int8_peaks(lib, st)
+    # end to end: codes and scales from pinned host memory, the BF16 output back
+    names = ("q", "k", "v", "q_scale", "k_scale", "v_scale")
+    host = {k: getattr(packed, k).cpu().pin_memory() for k in names}
+    dev_in = {k: torch.empty_like(getattr(packed, k)) for k in names}
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    import dataclasses
+    staged = dataclasses.replace(packed, **dev_in)
+    call_e2e = dense.bind(staged, out)
+
+    def e2e(_):
+        for k in names:
+            dev_in[k].copy_(host[k], non_blocking=True)
+        call_e2e()
+        out_h.copy_(out, non_blocking=True)
+    e2e_ms = _median_ms(e2e, warmup=1, iters=max(3, min(args.steps, 5)))
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_h.numel() * out_h.element_size()
+    achieved = scores / (ms / 1e3) / 1e9
+    line = dict(base, value=ops / (ms / 1e3) / 1e12, ms_per_step=ms,
+                roofline={"bound": "sfu", "kernel": "attention_kernel (h3_dense_launch_window)",
+                          "achieved": achieved, "peak": ex2_peak, "unit": "G ex2/s",
+                          "frac": achieved / ex2_peak if ex2_peak else None, "traffic": None,
+                          "peak_source": "live ex2.approx throughput probe (h3sk_ex2_peak)",
+                          "tensor_frac_of_burst_int8": ops / (ms / 1e3) / 1e12 / i8["burst"]},
+                e2e={"value": ops / (e2e_ms / 1e3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": h2d,
+                     "d2h_bytes_per_step": d2h},
+                cpu_baseline=None, cpu_baseline_note="no CPU attention: the arithmetic is the GPU's ex2.approx",
+                clocks=clock, gpu_launches=1)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     global D, ATTN, FFN, SWIGLU
     args = parse_args()
     D, ATTN, FFN, SWIGLU = GEOMETRIES[args.geometry]
     if args.op == "qkv":
         return run_qkv(args)
+    if args.op == "attention":
+        return run_attention(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.config != 5:

@@ -36,10 +36,14 @@
 // every FP32 operation has the reference's operands in the reference's order.
 // The unit is compiled with --use_fast_math, like the reference's dense unit.
 //
-// Roles (192 threads): warp 0 TMA producer (Q once, K and V tiles into a ring),
-// warp 1 TMEM owner and MMA issuer, warps 2-5 the softmax / output (thread =
-// query row = TMEM lane).  Every mbarrier wait is bounded (2 s) and reports a
-// status code instead of hanging.
+// Roles: warp 0 TMA producer (Q once, K and V tiles into a 4-stage ring), warp
+// 1 TMEM owner and MMA issuer, warps 2-5 the correction (one thread per query
+// row: each block's P.V joins O, then the normalised output), and 4 x kParts
+// softmax warps (kParts threads per query row, each with kKeys / kParts of the
+// keys).  S is double-buffered in TMEM and the block's P.V joins O one block
+// late, so the tensor core and the correction warps work under the softmax.
+// Every mbarrier wait is bounded (2 s) and reports a status code instead of
+// hanging.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -59,11 +63,25 @@ constexpr int kRows = 128;             // query rows per CTA (TMEM lanes)
 constexpr int kKeys = 128;             // keys per block
 constexpr int kDim = 128;              // head dimension
 constexpr int kTileBytes = 128 * 128;  // one INT8 [128 x 128] tile
-constexpr int kStages = 3;             // K and V ring depth
-constexpr int kThreads = 192;
+constexpr int kStages = 4;             // K and V ring depth
+constexpr int kSoftWarps = 4;          // one per TMEM lane quadrant: thread = query row
+constexpr int kCorrWarps = 8;          // two per quadrant: thread = (query row, 64 output channels)
+constexpr int kThreads = 32 * (2 + kCorrWarps + kSoftWarps);
+constexpr int kScSlots = 4;            // ring of per-block (o_scale, tile_scale) hand-offs
 constexpr float kExpOffset = 7.9943534f;          // attn_utils.cuh:40 (S_U8_OFFSET)
 constexpr float kLog2e = 1.44269504088896340736f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+// Every int32 accumulator starts at the bit pattern of 1.5 * 2^23.  For |x| < 2^22
+// the accumulated bits read as the float 1.5 * 2^23 + x, and one exact FP32
+// subtraction gives x back -- the bias the reference's own accumulators carry
+// (attn_utils.cuh:211-235, 1019-1038).  |s| <= 128 * 127 * 127 and
+// |P.V| <= 128 * 255 * 127 both stay below 2^22.  The maxima are taken on the
+// biased values as floats: positive floats order like their integers.
+constexpr uint32_t kBias = 0x4b400000u;
+constexpr float kBiasF = 12582912.0f;
+// TMEM columns: two S buffers and two P.V buffers (block j in buffer j % 2).
+// O lives in the correction warps' registers.
+constexpr uint32_t kColS = 0, kColPV = 256;
 
 struct Args {
   int q_heads, kv_heads, batch;
@@ -83,36 +101,83 @@ struct Smem {
   uint8_t q[kTileBytes];
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint8_t p[kTileBytes];
+  uint8_t p[2][kTileBytes];
+  float2 sc[kScSlots][kRows];   // [block % kScSlots][row]: (o_scale, tile_scale)
+  float xinv[kRows];            // 1 / d, from the softmax to the correction warps
   uint64_t q_full;
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full, s_empty, p_full, o_full, o_empty, drain;
+  uint64_t s_full[2], s_empty[2], p_full[2];
+  uint64_t pv_full[2], pv_empty[2];
+  uint64_t sc_full[kScSlots], inv_full, drain;
   uint32_t tmem;
   int abort;
 };
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 __device__ __forceinline__ float rcp(float x) {
   float y;
-  asm volatile("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float as_f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ float unbias(uint32_t x) { return __fadd_rn(__uint_as_float(x), -kBiasF); }
 // Four probabilities -> four u8 codes (cvt.rni.s32 then a saturating pack;
 // mma.cuh:769-786), low byte = a.
 __device__ __forceinline__ uint32_t u8x4(float a, float b, float c, float d) {
   uint32_t qa, qb, qc, qd, hi, w;
-  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qa) : "f"(a));
-  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qb) : "f"(b));
-  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qc) : "f"(c));
-  asm volatile("cvt.rni.s32.f32 %0, %1;" : "=r"(qd) : "f"(d));
-  asm volatile("cvt.pack.sat.u8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(qd), "r"(qc));
-  asm volatile("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(qb), "r"(qa), "r"(hi));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(qa) : "f"(a));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(qb) : "f"(b));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(qc) : "f"(c));
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(qd) : "f"(d));
+  asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(qd), "r"(qc));
+  asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(qb), "r"(qa), "r"(hi));
   return w;
+}
+// ---- packed FP32 pairs (sm_100 f32x2), flushing subnormals like the unit's scalar math ----
+__device__ __forceinline__ uint64_t pk(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pkf(float lo, float hi) { return pk(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ void upk(uint64_t x, uint32_t& lo, uint32_t& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(x));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// The same four codes as u8x4 without the conversion pipe: min(p, 255) + 1.5 * 2^23
+// rounds to the nearest integer, ties to even, exactly as cvt.rni does, and leaves
+// it in the low byte (p >= 0 always: it is an exp2); three byte permutes gather
+// the bytes.  min(p, 255) before rounding equals the saturating pack after it.
+__device__ __forceinline__ uint32_t u8x4_fast(float a, float b, float c, float d) {
+  const uint64_t magic = pkf(kBiasF, kBiasF);
+  uint32_t ya, yb, yc, yd;
+  upk(add2(pkf(fminf(a, 255.0f), fminf(b, 255.0f)), magic), ya, yb);
+  upk(add2(pkf(fminf(c, 255.0f), fminf(d, 255.0f)), magic), yc, yd);
+  return __byte_perm(__byte_perm(ya, yb, 0x0040), __byte_perm(yc, yd, 0x4000), 0x7610);
 }
 __device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -125,14 +190,108 @@ __device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const uint32_t
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns (load, store, fill).
+__device__ __forceinline__ void tmem_load_16cols(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_store_16cols(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_fill_16cols(uint32_t taddr, uint32_t x) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(x)
+      : "memory");
+}
+// The same 32-bit value into 32 consecutive columns of the warp's 32 lanes.
+__device__ __forceinline__ void tmem_fill_32cols(uint32_t taddr, uint32_t x) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(x)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_load_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_load_32cols(taddr, r);
+}
+// 32 lanes x 64 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_load_64cols(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_load_cols<64>(uint32_t taddr, uint32_t (&r)[64]) {
+  tmem_load_64cols(taddr, r);
+}
 
-// mbarrier wait by lane 0 of a warp, verdict shared with the warp.
+// Bounded mbarrier wait that sleeps: try_wait with a suspend-time hint parks the
+// warp until the phase completes (or the hint runs out) instead of spinning, so a
+// waiting warp leaves its scheduler's issue slots to the warps still computing.
+// Gives up after kTimeoutNs (raising *abort, recording `code`) or once another
+// role raised *abort.
+constexpr uint32_t kSuspendHintNs = 10000000u;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                           int code) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - start > kTimeoutNs) {
+      if (abort != nullptr) *abort = 1;
+      if (status != nullptr) atomicExch(status, code);
+      return false;
+    }
+  }
+}
+
+// mbarrier wait by a whole warp; the warp's verdict is unanimous.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Smem& sm, int* status, int code) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0)
-    ok = mbar_wait_bounded(bar, parity, reinterpret_cast<volatile int*>(&sm.abort), status, code, kTimeoutNs) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  // every lane tests the barrier (one instruction for the warp, no divergent branch)
+  const bool ok = wait_sleep(bar, parity, reinterpret_cast<volatile int*>(&sm.abort), status, code);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Instruction descriptors (sm100.cuh idesc_i8 fields): s8 x s8 and u8 x s8, M=N=128.
@@ -158,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kv_head = head / (a.q_heads / a.kv_heads);
   const int bh_q = batch * a.q_heads + head, bh_k = batch * a.kv_heads + kv_head;
   const int nblk = a.kv_blocks;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(&sm.abort);
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
@@ -167,11 +327,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.v_full[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.o_full, 1);
-    mbar_init(&sm.s_empty, 4);
-    mbar_init(&sm.p_full, 4);
-    mbar_init(&sm.o_empty, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.s_full[b], 1);
+      mbar_init(&sm.s_empty[b], kSoftWarps);
+      mbar_init(&sm.p_full[b], kSoftWarps);
+      mbar_init(&sm.pv_full[b], 1);
+      mbar_init(&sm.pv_empty[b], kCorrWarps);
+    }
+    for (int s = 0; s < kScSlots; ++s) mbar_init(&sm.sc_full[s], kSoftWarps);
+    mbar_init(&sm.inv_full, kSoftWarps);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -187,73 +351,81 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
-  const uint32_t t_s = tmem, t_o = tmem + 128, t_ro = tmem + 256;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    int issued = 0;
-    bool ok = true;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
-      tma_load_3d(sm.q, &map_q, &sm.q_full, 0, bx * kRows, bh_q);
+    // ---------------- TMA producer: lane 0 Q and the K ring, lane 1 the V ring ----------------
+    // (two independent threads, so that a K load never waits behind a V stage)
+    if (lane < 2) {
+      const bool is_k = lane == 0;
+      uint64_t* full = is_k ? sm.k_full : sm.v_full;
+      uint64_t* empty = is_k ? sm.k_empty : sm.v_empty;
+      int issued = 0;
+      bool ok = true;
+      if (is_k) {
+        mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
+        tma_load_3d(sm.q, &map_q, &sm.q_full, 0, bx * kRows, bh_q);
+      }
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kStages;
         const uint32_t ph = uint32_t(j / kStages) & 1u;
-        if (j >= kStages) {
-          ok = mbar_wait_bounded(&sm.k_empty[s], ph ^ 1u, reinterpret_cast<volatile int*>(&sm.abort), a.status, 41,
-                                 kTimeoutNs);
-          if (ok)
-            ok = mbar_wait_bounded(&sm.v_empty[s], ph ^ 1u, reinterpret_cast<volatile int*>(&sm.abort), a.status,
-                                   42, kTimeoutNs);
-        }
+        if (j >= kStages) ok = wait_sleep(&empty[s], ph ^ 1u, abort_flag, a.status, is_k ? 41 : 42);
         if (!ok) break;
-        mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
-        tma_load_3d(sm.k[s], &map_k, &sm.k_full[s], 0, j * kKeys, bh_k);
-        mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
-        tma_load_3d(sm.v[s], &map_v, &sm.v_full[s], j * kKeys, 0, bh_k);
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        if (is_k)
+          tma_load_3d(sm.k[s], &map_k, &full[s], 0, j * kKeys, bh_k);
+        else
+          tma_load_3d(sm.v[s], &map_v, &full[s], j * kKeys, 0, bh_k);
         issued = j + 1;
       }
-      // every copy this CTA issued lands before the CTA exits
-      mbar_wait_bounded(&sm.q_full, 0, nullptr, a.status, 43, kTimeoutNs);
-      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j) {
-        const uint32_t ph = uint32_t(j / kStages) & 1u;
-        mbar_wait_bounded(&sm.k_full[j % kStages], ph, nullptr, a.status, 43, kTimeoutNs);
-        mbar_wait_bounded(&sm.v_full[j % kStages], ph, nullptr, a.status, 43, kTimeoutNs);
-      }
+      // every copy this thread issued lands before the CTA exits
+      if (is_k) mbar_wait_bounded(&sm.q_full, 0, nullptr, a.status, 43, kTimeoutNs);
+      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+        mbar_wait_bounded(&full[j % kStages], uint32_t(j / kStages) & 1u, nullptr, a.status, 43, kTimeoutNs);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // S(0), S(1), then per block j: P.V(j) into P.V buffer j % 2, and S(j + 2)
+    // into S buffer j % 2.  Issued in this order from one thread, the MMAs
+    // complete in order, so the completion of S(j + 2) also shows P.V(j) done.
     bool ok = warp_wait(&sm.q_full, 0, sm, a.status, 51);
-    const uint64_t qd = smem_desc_k_sw128(sm.q), pd = smem_desc_k_sw128(sm.p);
-    for (int j = 0; ok && j < nblk; ++j) {
-      const int s = j % kStages;
-      const uint32_t ph = uint32_t(j / kStages) & 1u;
-      ok = warp_wait(&sm.k_full[s], ph, sm, a.status, 52) &&
-           (j == 0 || warp_wait(&sm.s_empty, uint32_t(j - 1) & 1u, sm, a.status, 53));
-      if (!ok) break;
+    const uint64_t qd = smem_desc_k_sw128(sm.q);
+    auto issue_s = [&](int jj) -> bool {
+      const int s = jj % kStages, b = jj & 1;
+      if (!warp_wait(&sm.k_full[s], uint32_t(jj / kStages) & 1u, sm, a.status, 52) ||
+          !warp_wait(&sm.s_empty[b], uint32_t(jj >> 1) & 1u, sm, a.status, 53))
+        return false;
       tc_fence_after();
       if (lane == 0) {
         const uint64_t kd = smem_desc_k_sw128(sm.k[s]);
 #pragma unroll
-        for (int kk = 0; kk < kDim / 32; ++kk) mma_i8(t_s, qd + uint64_t(2 * kk), kd + uint64_t(2 * kk), kIdescQK, kk);
+        for (int kk = 0; kk < kDim / 32; ++kk)
+          mma_i8(tmem + kColS + 128u * b, qd + uint64_t(2 * kk), kd + uint64_t(2 * kk), kIdescQK, 1);
         mma_commit(&sm.k_empty[s]);
-        mma_commit(&sm.s_full);
+        mma_commit(&sm.s_full[b]);
       }
       __syncwarp();
-      ok = warp_wait(&sm.p_full, uint32_t(j) & 1u, sm, a.status, 54) &&
-           warp_wait(&sm.v_full[s], ph, sm, a.status, 55) &&
-           (j == 0 || warp_wait(&sm.o_empty, uint32_t(j - 1) & 1u, sm, a.status, 56));
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    if (ok && nblk > 1) ok = issue_s(1);
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int s = j % kStages, b = j & 1;
+      ok = warp_wait(&sm.p_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 54) &&
+           warp_wait(&sm.v_full[s], uint32_t(j / kStages) & 1u, sm, a.status, 55) &&
+           warp_wait(&sm.pv_empty[b], uint32_t(j >> 1) & 1u, sm, a.status, 56);
       if (!ok) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint64_t vd = smem_desc_k_sw128(sm.v[s]);
+        const uint64_t pd = smem_desc_k_sw128(sm.p[b]), vd = smem_desc_k_sw128(sm.v[s]);
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 32; ++kk) mma_i8(t_o, pd + uint64_t(2 * kk), vd + uint64_t(2 * kk), kIdescPV, kk);
+        for (int kk = 0; kk < kKeys / 32; ++kk)
+          mma_i8(tmem + kColPV + 128u * b, pd + uint64_t(2 * kk), vd + uint64_t(2 * kk), kIdescPV, 1);
         mma_commit(&sm.v_empty[s]);
-        mma_commit(&sm.o_full);
+        mma_commit(&sm.pv_full[b]);
       }
       __syncwarp();
+      if (j + 2 < nblk) ok = issue_s(j + 2);
     }
     // every MMA issued here completes before TMEM is released
     if (lane == 0) {
@@ -261,176 +433,291 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(&sm.drain, 0, nullptr, a.status, 57, kTimeoutNs);
     }
     __syncwarp();
-  } else {
-    // ---------------- softmax and output: thread = query row ----------------
+  } else if (warp < 2 + kCorrWarps) {
+    // ---------------- correction: O <- fmaf(float(P.V), tile_scale, O * o_scale) ----------------
+    // Thread = (query row, half): TMEM lane r of quadrant warp % 4 and output
+    // channels [64 h, 64 h + 64), O of them in registers.  Block j's P.V joins O
+    // here while the softmax works on block j + 1; o_scale and tile_scale come
+    // from the softmax warp of the row.  x * 1 == x for every value O takes (FTZ
+    // arithmetic makes no subnormals), so a warp rescales all of its rows when
+    // any of them needs it.
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;                  // row within the block (TMEM lane)
+    const int half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
     const int row = bx * kRows + r;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t col0 = uint32_t(64 * half);
+    const uint64_t nbias2 = pkf(-kBiasF, -kBiasF);
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      tmem_fill_32cols(tmem + kColPV + 128u * b + lane_off + col0, kBias);
+      tmem_fill_32cols(tmem + kColPV + 128u * b + lane_off + col0 + 32, kBias);
+    }
+    tmem_store_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&sm.pv_empty[0]);
+      mbar_arrive(&sm.pv_empty[1]);
+    }
+    uint64_t o2[32];   // O of channels col0 + [0, 64), as FP32 pairs
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o2[i] = 0ull;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1, slot = j % kScSlots;
+      if (!warp_wait(&sm.sc_full[slot], uint32_t(j / kScSlots) & 1u, sm, a.status, 71)) {
+        ok = false;
+        break;
+      }
+      const float2 sc = sm.sc[slot][r];
+      if (!warp_wait(&sm.pv_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 72)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j > 0 && __any_sync(0xffffffffu, sc.x != 1.0f)) {
+        const uint64_t os2 = pkf(sc.x, sc.x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o2[i] = mul2(o2[i], os2);
+      }
+      const uint64_t ts2 = pkf(sc.y, sc.y);
+      const uint32_t t_pv = tmem + kColPV + 128u * b + lane_off + col0;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t pv[16];
+        tmem_load_16cols(t_pv + 16 * g, pv);
+        tmem_load_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o2[8 * g + i] = fma2(add2(pk(pv[2 * i], pv[2 * i + 1]), nbias2), ts2, o2[8 * g + i]);
+      }
+      // P.V buffer b is rebiased for block j + 2
+      tmem_fill_32cols(t_pv, kBias);
+      tmem_fill_32cols(t_pv + 32, kBias);
+      tmem_store_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.pv_empty[b]);
+    }
+    // O = (O / d) * v_scale in BF16
+    if (ok && warp_wait(&sm.inv_full, 0, sm, a.status, 73) && row < a.q_len) {
+      const float inv = sm.xinv[r];
+      const float* vs = a.vs + int64_t(bh_k) * kDim + col0;
+      __nv_bfloat16* out =
+          a.o + int64_t(batch) * a.o_sb + int64_t(head) * a.o_sh + int64_t(row) * a.o_ss + col0;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t lo, hi;
+          upk(o2[4 * g + q], lo, hi);
+          const float o0 = (as_f(lo) * inv) * __ldg(vs + 8 * g + 2 * q);
+          const float o1 = (as_f(hi) * inv) * __ldg(vs + 8 * g + 2 * q + 1);
+          __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
+          w[q] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(out)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  } else {
+    // ---------------- softmax: thread = query row = TMEM lane ----------------
+    // The row's 128 scores are read from TMEM in two 64-column halves, twice:
+    // once for the class maxima, once for the probabilities.  The four class
+    // denominators are kept in key order, as the reference's four quad threads
+    // keep theirs.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) tmem_fill_32cols(tmem + kColS + 128u * b + lane_off + 32 * g, kBias);
+    }
+    tmem_store_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&sm.s_empty[0]);
+      mbar_arrive(&sm.s_empty[1]);
+    }
     const float q_scale = a.qs[int64_t(bh_q) * a.q_blocks * 32 + bx * 32 + (r >> 5) * 8 + (r & 7)];
     const float sm_base = a.sm_scale * kLog2e;
+    const float* kscale = a.ks + int64_t(bh_k) * nblk * 4;
+    float kn[4];                              // the next block's K scales, loaded a block early
+#pragma unroll
+    for (int t = 0; t < 4; ++t) kn[t] = __ldg(kscale + t);
+    const uint64_t nbias2 = pkf(-kBiasF, -kBiasF);
     float m = -50000.0f;
     float d[4] = {1.0f, 1.0f, 1.0f, 1.0f};
     bool ok = true;
-    int j = 0;
-    for (; j < nblk; ++j) {
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
       const bool last = j == nblk - 1;
-      if (!warp_wait(&sm.s_full, uint32_t(j) & 1u, sm, a.status, 61)) {
+      const uint32_t t_s = tmem + kColS + 128u * b + lane_off;
+      // S buffer b ^ 1 (block j - 1's scores, read) is rebiased for block j + 1;
+      // the stores complete under the maxima below
+      if (j > 0) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) tmem_fill_32cols(tmem + kColS + 128u * (b ^ 1) + lane_off + 32 * g, kBias);
+      }
+      if (!warp_wait(&sm.s_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 61)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float scale[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        scale[t] = sm_base * (q_scale * a.ks[int64_t(bh_k) * nblk * 4 + j * 4 + t]);
-      // pass 1: the per-class maxima (integers; in the last block, floats with
-      // the keys past Sk at -1e30 and the maximum starting at -50000)
-      float mt[4];
+      for (int t = 0; t < 4; ++t) scale[t] = sm_base * (q_scale * kn[t]);
       if (!last) {
-        int imax[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) kn[t] = __ldg(kscale + (j + 1) * 4 + t);
+      }
+      // per-class maxima: class t holds keys 2t, 2t+1, 2t+8, 2t+9 of every run
+      // of 16 (integers; in the last block floats, with the keys past Sk at
+      // -1e30 and the maximum starting at -50000)
+      float mx[4];
+      uint32_t v[64];
+      if (!last) {
+        // two chains per class (keys 2t, 2t+1 and keys 2t+8, 2t+9 of each run)
+        float mb[4][2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_load_64cols(t_s + 64 * hh, v);
           tmem_load_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) imax[(i & 7) >> 1] = max(imax[(i & 7) >> 1], int(v[i]));
-        }
+          for (int t = 0; t < 4; ++t) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) mt[t] = fmaf(float(imax[t]), scale[t], -kExpOffset);
-      } else {
-        float fmax_[4] = {-50000.0f, -50000.0f, -50000.0f, -50000.0f};
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
-          tmem_load_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = j * kKeys + 32 * c + i;
-            const float sc = key < a.kv_len ? float(int(v[i])) : -1.0e30f;
-            fmax_[(i & 7) >> 1] = fmaxf(fmax_[(i & 7) >> 1], sc);
+            for (int e = 0; e < 2; ++e) {
+              const int o = 2 * t + 8 * e;
+              float x = hh == 0 ? max3(as_f(v[o]), as_f(v[o + 1]), as_f(v[16 + o]))
+                                : max3(mb[t][e], as_f(v[o]), as_f(v[o + 1]));
+              x = hh == 0 ? max3(x, as_f(v[17 + o]), as_f(v[32 + o])) : max3(x, as_f(v[16 + o]), as_f(v[17 + o]));
+              x = hh == 0 ? max3(x, as_f(v[33 + o]), as_f(v[48 + o])) : max3(x, as_f(v[32 + o]), as_f(v[33 + o]));
+              x = hh == 0 ? fmaxf(x, as_f(v[49 + o])) : max3(x, as_f(v[48 + o]), as_f(v[49 + o]));
+              mb[t][e] = x;
+            }
           }
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) mt[t] = fmaf(fmax_[t], scale[t], -kExpOffset);
+        for (int t = 0; t < 4; ++t) mx[t] = __fadd_rn(fmaxf(mb[t][0], mb[t][1]), -kBiasF);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) mx[t] = -50000.0f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_load_64cols(t_s + 64 * hh, v);
+          tmem_load_wait();
+          const int key0 = j * kKeys + 64 * hh;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float sc = key0 + i < a.kv_len ? unbias(v[i]) : -1.0e30f;
+            mx[(i & 7) >> 1] = fmaxf(mx[(i & 7) >> 1], sc);
+          }
+        }
       }
+      if (j > 0) {
+        tmem_store_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_empty[b ^ 1]);
+      }
+      float mt[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) mt[t] = fmaf(mx[t], scale[t], -kExpOffset);
       const float tile_m = fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3]));
       const float m_prev = m;
       m = fmaxf(m_prev, tile_m);
       const float smaller = ex2(-fabsf(m_prev - tile_m));
       const float o_scale = m_prev < tile_m ? smaller : 1.0f;
       const float tile_scale = tile_m < m_prev ? smaller : 1.0f;
-      // blocks before the last rescale d_t on their own (the reference applies
-      // o_scale under a branch); the last block folds d_t * o_scale into its
+      // o_scale and tile_scale of this block to the row's correction threads.
+      // Slot j % 4 was last read for block j - 4, whose fold completed before
+      // P.V(j - 2) was issued, which came before S(j) (waited on above).
+      sm.sc[j % kScSlots][r] = make_float2(o_scale, tile_scale);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.sc_full[j % kScSlots]);
+      // blocks before the last rescale d on their own (the reference applies
+      // o_scale under a branch); the last block folds d * o_scale into its
       // first denominator update, as the reference's straight-line float path
-      // compiles (fma(d, o_scale, round(sum * tile_scale)))
+      // compiles: fma(d, o_scale, round(sum * tile_scale))
       if (!last) {
 #pragma unroll
         for (int t = 0; t < 4; ++t) d[t] *= o_scale;
       }
       // pass 2: probabilities -> u8 P (key order of V: the four keys of class t
-      // of each 16-key run in one word at byte 4t), denominators
+      // of each 16-key run in one word at byte 4t), denominators in key order.
+      // P buffer b was last read by P.V(j - 2), complete since S(j) is.
       const float neg_m = -tile_m;
-      uint8_t* prow = sm.p + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        __syncwarp();
-        tmem_load_32cols(t_s + lane_off + uint32_t(32 * c), v);
-        tmem_load_wait();
+      const uint64_t negm2 = pkf(neg_m, neg_m);
+      uint64_t scale2[4];
 #pragma unroll
-        for (int run = 0; run < 2; ++run) {      // 16-key runs of this chunk
-          uint32_t words[4];
+      for (int t = 0; t < 4; ++t) scale2[t] = pkf(scale[t], scale[t]);
+      uint8_t* prow = sm.p[b] + (r >> 3) * 1024 + (r & 7) * 128;
+      // (two copies of the loop, so that neither has a branch inside: the
+      // groups of four keys then interleave freely)
+      if (!last) {
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int i0 = 16 * run + 2 * t, i1 = i0 + 1, i2 = i0 + 8, i3 = i0 + 9;
-            float s0 = float(int(v[i0])), s1 = float(int(v[i1])), s2 = float(int(v[i2])), s3 = float(int(v[i3]));
-            if (last) {
-              const int k0 = j * kKeys + 32 * c;
-              if (k0 + i0 >= a.kv_len) s0 = -1.0e30f;
-              if (k0 + i1 >= a.kv_len) s1 = -1.0e30f;
-              if (k0 + i2 >= a.kv_len) s2 = -1.0e30f;
-              if (k0 + i3 >= a.kv_len) s3 = -1.0e30f;
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_load_64cols(t_s + 64 * hh, v);
+          tmem_load_wait();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t words[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i0 = 16 * c + 2 * t;
+              // s = biased - 1.5 * 2^23 and x = fmaf(s, scale_t, -tile_m), two keys per instruction
+              uint32_t x0, x1, x2, x3;
+              upk(fma2(add2(pk(v[i0], v[i0 + 1]), nbias2), scale2[t], negm2), x0, x1);
+              upk(fma2(add2(pk(v[i0 + 8], v[i0 + 9]), nbias2), scale2[t], negm2), x2, x3);
+              words[t] = u8x4(ex2(as_f(x0)), ex2(as_f(x1)), ex2(as_f(x2)), ex2(as_f(x3)));
+              // the integer sum of the four codes (dp4a onto the bias: the float comes out exact)
+              d[t] = fmaf(unbias(__dp4a(words[t], 0x01010101u, kBias)), tile_scale, d[t]);
             }
-            const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
-            const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
-            words[t] = u8x4(p0, p1, p2, p3);
-            const float add = last ? (p0 + p1) + (p2 + p3)
-                                   : __uint2float_rn(__dp4a(words[t], 0x01010101u, 0u));
-            if (last && c == 0 && run == 0)
-              d[t] = fmaf(d[t], o_scale, __fmul_rn(add, tile_scale));
-            else
-              d[t] = fmaf(add, tile_scale, d[t]);
+            const int chunk = 4 * hh + c;        // 16-byte chunk of the P row
+            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
+                                                                                   words[3]);
           }
-          const int chunk = 2 * c + run;          // 16-byte chunk of the P row
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
-                                                                                 words[3]);
+        }
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_load_64cols(t_s + 64 * hh, v);
+          tmem_load_wait();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t words[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i0 = 16 * c + 2 * t;
+              const int k0 = j * kKeys + 64 * hh + i0;
+              const float s0 = k0 < a.kv_len ? unbias(v[i0]) : -1.0e30f;
+              const float s1 = k0 + 1 < a.kv_len ? unbias(v[i0 + 1]) : -1.0e30f;
+              const float s2 = k0 + 8 < a.kv_len ? unbias(v[i0 + 8]) : -1.0e30f;
+              const float s3 = k0 + 9 < a.kv_len ? unbias(v[i0 + 9]) : -1.0e30f;
+              const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
+              const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
+              words[t] = u8x4(p0, p1, p2, p3);
+              const float den = (p0 + p1) + (p2 + p3);   // the last block sums the unrounded p
+              d[t] = (hh == 0 && c == 0) ? fmaf(d[t], o_scale, __fmul_rn(den, tile_scale))
+                                         : fmaf(den, tile_scale, d[t]);
+            }
+            const int chunk = 4 * hh + c;
+            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
+                                                                                   words[3]);
+          }
         }
       }
       fence_async_shared();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.s_empty);
-        mbar_arrive(&sm.p_full);
-      }
-      // O <- fmaf(float(P.V), tile_scale, O * o_scale)
-      if (!warp_wait(&sm.o_full, uint32_t(j) & 1u, sm, a.status, 62)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pv[32], ro[32];
-        __syncwarp();
-        tmem_load_32cols(t_o + lane_off + uint32_t(32 * c), pv);
-        if (j > 0) tmem_load_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
-        tmem_load_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float o = j > 0 ? __uint_as_float(ro[i]) : 0.0f;
-          if (o_scale != 1.0f) o = o * o_scale;
-          ro[i] = __float_as_uint(fmaf(float(int(pv[i])), tile_scale, o));
-        }
-        tmem_store_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
-      }
-      tmem_store_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.o_empty);
+      if (lane == 0) mbar_arrive(&sm.p_full[b]);
     }
-    if (ok && j == nblk) {
-      tc_fence_after();
-      const float den = (d[0] + d[1]) + (d[2] + d[3]);
-      const float inv = rcp(den);
-      const float* vs = a.vs + int64_t(bh_k) * kDim;
-      __nv_bfloat16* out = a.o + int64_t(batch) * a.o_sb + int64_t(head) * a.o_sh + int64_t(row) * a.o_ss;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ro[32];
-        __syncwarp();
-        tmem_load_32cols(t_ro + lane_off + uint32_t(32 * c), ro);
-        tmem_load_wait();
-        if (row < a.q_len) {
-          uint32_t packed[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float o0 = (__uint_as_float(ro[i]) * inv) * __ldg(vs + 32 * c + i);
-            const float o1 = (__uint_as_float(ro[i + 1]) * inv) * __ldg(vs + 32 * c + i + 1);
-            __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
-            packed[i / 2] = *reinterpret_cast<uint32_t*>(&h);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            reinterpret_cast<uint4*>(out + 32 * c)[q] =
-                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        }
-      }
+    if (ok) {
+      sm.xinv[r] = rcp((d[0] + d[1]) + (d[2] + d[3]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.inv_full);
     }
   }
   tc_fence_before();
@@ -440,6 +727,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// The exp2 roofline: every score of the attention takes one ex2.approx (the
+// reference's arithmetic; no other unit computes it bit for bit), and the SFU
+// that executes it is the attention's bound.  Eight independent chains per thread,
+// eight 256-thread CTAs per SM.
+// Each chain runs x <- -2^x, which stays in [-1, 0).
+__global__ void __launch_bounds__(256) ex2_peak_kernel(int iters, float* sink) {
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = -1.0e-3f * float(threadIdx.x + i);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(x[i]));
+      x[i] = -x[i];
+    }
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc += x[i];
+  if (sink != nullptr) sink[blockIdx.x * blockDim.x + threadIdx.x] = acc;
 }
 
 }  // namespace attn
@@ -566,4 +875,30 @@ H3SK_EXPORT int h3_dense_resources(int* out) {
   out[3] = attr.maxThreadsPerBlock;
   out[4] = attr.binaryVersion;
   return 0;
+}
+
+// ex2.approx throughput of the whole GPU (G ex2 / s), measured now: the attention's roofline denominator.
+H3SK_EXPORT int h3sk_ex2_peak(int iters, double* gops, uintptr_t stream) {
+  if (!gops || iters < 64 || iters > (1 << 20)) return cudaErrorInvalidValue;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int device = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  cudaEvent_t t0, t1;
+  cudaEventCreate(&t0);
+  cudaEventCreate(&t1);
+  h3sk::attn::ex2_peak_kernel<<<sms * 8, 256, 0, s>>>(64, nullptr);   // warm-up
+  cudaEventRecord(t0, s);
+  h3sk::attn::ex2_peak_kernel<<<sms * 8, 256, 0, s>>>(iters, nullptr);
+  cudaEventRecord(t1, s);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventSynchronize(t1);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t0, t1);
+  cudaEventDestroy(t0);
+  cudaEventDestroy(t1);
+  if (e != cudaSuccess) return e;
+  *gops = double(sms) * 8 * 256 * 8 * double(iters) / (double(ms) * 1e-3) / 1e9;
+  return cudaSuccess;
 }

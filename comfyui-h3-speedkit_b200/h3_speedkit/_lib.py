@@ -65,6 +65,7 @@ EXPORTS = {
     "h3sk_pipeline_status": ([_P, _I, _SZ], _I),
     "h3sk_wait_selftest": ([_I, _P, _SZ], _I),
     "h3sk_int8_mma_peak": ([_I, _P, _SZ], _I),
+    "h3sk_ex2_peak": ([_I, _P, _SZ], _I),
     "h3sk_version": ([], ct.c_char_p),
 }
 

@@ -392,6 +392,10 @@ int h3sk_wait_selftest(int timeout_us, int* status, uintptr_t stream);
  * dense INT8 tera-ops per second.  Returns cudaError_t.
  */
 int h3sk_int8_mma_peak(int iters, double* tops, uintptr_t stream);
+/* The GPU's ex2.approx.ftz.f32 throughput (G ex2 / s), measured by the call:
+ * the INT8 attention takes one ex2 per score, and that unit bounds it.  No
+ * counterpart in the reference (a measurement aid of this library). */
+int h3sk_ex2_peak(int iters, double* gops, uintptr_t stream);
 /* Library version string. */
 const char* h3sk_version(void);
 

@@ -64,24 +64,21 @@ constexpr int kKeys = 128;             // keys per block
 constexpr int kDim = 128;              // head dimension
 constexpr int kTileBytes = 128 * 128;  // one INT8 [128 x 128] tile
 constexpr int kStages = 4;             // K and V ring depth
-constexpr int kSoftWarps = 4;          // one per TMEM lane quadrant: thread = query row
+constexpr int kSlots = 4;              // TMEM slots: block j's S, then its P.V, in slot j % 4
+constexpr int kSoftWarps = 8;          // two per TMEM lane quadrant (alternate blocks): thread = query row
 constexpr int kCorrWarps = 8;          // two per quadrant: thread = (query row, 64 output channels)
-constexpr int kThreads = 32 * (2 + kCorrWarps + kSoftWarps);
-constexpr int kScSlots = 4;            // ring of per-block (o_scale, tile_scale) hand-offs
+// Warpgroups: 0 = TMA producer, MMA issuer and two idle warps; 1-2 = correction;
+// 3-4 = softmax.  setmaxnreg moves registers from warpgroup 0 to the others.
+constexpr int kCorrWarp0 = 4, kSoftWarp0 = kCorrWarp0 + kCorrWarps;
+constexpr int kThreads = 32 * (kSoftWarp0 + kSoftWarps);
+constexpr int kRegsLaunch = 96;        // per thread at launch (the compiler's cap for kThreads)
+constexpr int kRegsSetup = 32, kRegsCorr = 104, kRegsSoft = 120;
+static_assert(kRegsSetup * 128 + kRegsCorr * 32 * kCorrWarps + kRegsSoft * 32 * kSoftWarps <=
+                  kRegsLaunch * kThreads,
+              "setmaxnreg shares must fit in the block's launch registers");
 constexpr float kExpOffset = 7.9943534f;          // attn_utils.cuh:40 (S_U8_OFFSET)
 constexpr float kLog2e = 1.44269504088896340736f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-// Every int32 accumulator starts at the bit pattern of 1.5 * 2^23.  For |x| < 2^22
-// the accumulated bits read as the float 1.5 * 2^23 + x, and one exact FP32
-// subtraction gives x back -- the bias the reference's own accumulators carry
-// (attn_utils.cuh:211-235, 1019-1038).  |s| <= 128 * 127 * 127 and
-// |P.V| <= 128 * 255 * 127 both stay below 2^22.  The maxima are taken on the
-// biased values as floats: positive floats order like their integers.
-constexpr uint32_t kBias = 0x4b400000u;
-constexpr float kBiasF = 12582912.0f;
-// TMEM columns: two S buffers and two P.V buffers (block j in buffer j % 2).
-// O lives in the correction warps' registers.
-constexpr uint32_t kColS = 0, kColPV = 256;
 
 struct Args {
   int q_heads, kv_heads, batch;
@@ -101,15 +98,17 @@ struct Smem {
   uint8_t q[kTileBytes];
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint8_t p[2][kTileBytes];
-  float2 sc[kScSlots][kRows];   // [block % kScSlots][row]: (o_scale, tile_scale)
-  float xinv[kRows];            // 1 / d, from the softmax to the correction warps
+  uint8_t p[kSlots][kTileBytes];  // P of block j in buffer j % 4
+  float2 sc[kSlots][kRows];       // [block % 4][row]: (o_scale, tile_scale) to the correction warps
+  float xinv[kRows];              // 1 / d, from the softmax to the correction warps
+  float cm[kRows];                // the running maximum after the last chained block
+  float4 cd[kRows];               // the four class denominators after it
   uint64_t q_full;
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], s_empty[2], p_full[2];
-  uint64_t pv_full[2], pv_empty[2];
-  uint64_t sc_full[kScSlots], inv_full, drain;
+  uint64_t s_full[kSlots], p_full[kSlots], pv_full[kSlots], slot_free[kSlots];
+  uint64_t sc_full[kSlots], inv_full, drain;
+  uint64_t cbar[4];               // [quadrant]: the chain step of the previous block is done
   uint32_t tmem;
   int abort;
 };
@@ -130,7 +129,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 __device__ __forceinline__ float as_f(uint32_t x) { return __uint_as_float(x); }
-__device__ __forceinline__ float unbias(uint32_t x) { return __fadd_rn(__uint_as_float(x), -kBiasF); }
 // Four probabilities -> four u8 codes (cvt.rni.s32 then a saturating pack;
 // mma.cuh:769-786), low byte = a.
 __device__ __forceinline__ uint32_t u8x4(float a, float b, float c, float d) {
@@ -167,17 +165,6 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
-}
-// The same four codes as u8x4 without the conversion pipe: min(p, 255) + 1.5 * 2^23
-// rounds to the nearest integer, ties to even, exactly as cvt.rni does, and leaves
-// it in the low byte (p >= 0 always: it is an exp2); three byte permutes gather
-// the bytes.  min(p, 255) before rounding equals the saturating pack after it.
-__device__ __forceinline__ uint32_t u8x4_fast(float a, float b, float c, float d) {
-  const uint64_t magic = pkf(kBiasF, kBiasF);
-  uint32_t ya, yb, yc, yd;
-  upk(add2(pkf(fminf(a, 255.0f), fminf(b, 255.0f)), magic), ya, yb);
-  upk(add2(pkf(fminf(c, 255.0f), fminf(d, 255.0f)), magic), yc, yd);
-  return __byte_perm(__byte_perm(ya, yb, 0x0040), __byte_perm(yc, yd, 0x4000), 0x7610);
 }
 __device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -226,6 +213,18 @@ __device__ __forceinline__ void tmem_fill_32cols(uint32_t taddr, uint32_t x) {
 }
 __device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 template <int N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+// this warpgroup's share, from the launch count
+template <int N>
+__device__ __forceinline__ void regs_set() {
+  if constexpr (N < kRegsLaunch)
+    regs_dec<N>();
+  else if constexpr (N > kRegsLaunch)
+    regs_inc<N>();
+}
+template <int N>
 __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&r)[N]);
 template <>
 __device__ __forceinline__ void tmem_load_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
@@ -272,8 +271,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
       : "memory");
   return done != 0;
 }
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
 __device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
                                            int code) {
+  if (mbar_test_wait(bar, parity)) return true;   // the common case: already complete
   if (mbar_try_wait_sleep(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (;;) {
@@ -327,16 +338,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.v_full[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.s_empty[b], kSoftWarps);
-      mbar_init(&sm.p_full[b], kSoftWarps);
-      mbar_init(&sm.pv_full[b], 1);
-      mbar_init(&sm.pv_empty[b], kCorrWarps);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.p_full[s], 4);
+      mbar_init(&sm.pv_full[s], 1);
+      mbar_init(&sm.slot_free[s], kCorrWarps);
+      mbar_init(&sm.sc_full[s], 4);
     }
-    for (int s = 0; s < kScSlots; ++s) mbar_init(&sm.sc_full[s], kSoftWarps);
-    mbar_init(&sm.inv_full, kSoftWarps);
-    mbar_init(&sm.drain, 1);
+    mbar_init(&sm.inv_full, 4);
+    for (int q = 0; q < 4; ++q) mbar_init(&sm.cbar[q], 1);
+    mbar_init(&sm.drain, 2);
     sm.abort = 0;
     fence_mbar_init();
     tma_prefetch_map(&map_q);
@@ -352,126 +363,114 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
 
-  if (warp == 0) {
-    // ---------------- TMA producer: lane 0 Q and the K ring, lane 1 the V ring ----------------
-    // (two independent threads, so that a K load never waits behind a V stage)
-    if (lane < 2) {
-      const bool is_k = lane == 0;
-      uint64_t* full = is_k ? sm.k_full : sm.v_full;
-      uint64_t* empty = is_k ? sm.k_empty : sm.v_empty;
-      int issued = 0;
-      bool ok = true;
-      if (is_k) {
-        mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
-        tma_load_3d(sm.q, &map_q, &sm.q_full, 0, bx * kRows, bh_q);
-      }
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = uint32_t(j / kStages) & 1u;
-        if (j >= kStages) ok = wait_sleep(&empty[s], ph ^ 1u, abort_flag, a.status, is_k ? 41 : 42);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&full[s], kTileBytes);
-        if (is_k)
-          tma_load_3d(sm.k[s], &map_k, &full[s], 0, j * kKeys, bh_k);
-        else
-          tma_load_3d(sm.v[s], &map_v, &full[s], j * kKeys, 0, bh_k);
-        issued = j + 1;
-      }
-      // every copy this thread issued lands before the CTA exits
-      if (is_k) mbar_wait_bounded(&sm.q_full, 0, nullptr, a.status, 43, kTimeoutNs);
-      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
-        mbar_wait_bounded(&full[j % kStages], uint32_t(j / kStages) & 1u, nullptr, a.status, 43, kTimeoutNs);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    // S(0), S(1), then per block j: P.V(j) into P.V buffer j % 2, and S(j + 2)
-    // into S buffer j % 2.  Issued in this order from one thread, the MMAs
-    // complete in order, so the completion of S(j + 2) also shows P.V(j) done.
-    bool ok = warp_wait(&sm.q_full, 0, sm, a.status, 51);
-    const uint64_t qd = smem_desc_k_sw128(sm.q);
-    auto issue_s = [&](int jj) -> bool {
-      const int s = jj % kStages, b = jj & 1;
-      if (!warp_wait(&sm.k_full[s], uint32_t(jj / kStages) & 1u, sm, a.status, 52) ||
-          !warp_wait(&sm.s_empty[b], uint32_t(jj >> 1) & 1u, sm, a.status, 53))
-        return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint64_t kd = smem_desc_k_sw128(sm.k[s]);
-#pragma unroll
-        for (int kk = 0; kk < kDim / 32; ++kk)
-          mma_i8(tmem + kColS + 128u * b, qd + uint64_t(2 * kk), kd + uint64_t(2 * kk), kIdescQK, 1);
-        mma_commit(&sm.k_empty[s]);
-        mma_commit(&sm.s_full[b]);
+  // Each warpgroup's branch opens with its register share (setmaxnreg, executed
+  // by all four warps of the warpgroup at one site).
+  if (warp < kCorrWarp0) {
+    regs_set<kRegsSetup>();
+    if (warp == 0) {
+      // ---------------- TMA producer: lane 0 Q and the K ring, lane 1 the V ring ----------------
+      // (two independent threads, so that a K load never waits behind a V stage)
+      if (lane < 2) {
+        const bool is_k = lane == 0;
+        uint64_t* full = is_k ? sm.k_full : sm.v_full;
+        uint64_t* empty = is_k ? sm.k_empty : sm.v_empty;
+        int issued = 0;
+        bool ok = true;
+        if (is_k) {
+          mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
+          tma_load_3d(sm.q, &map_q, &sm.q_full, 0, bx * kRows, bh_q);
+        }
+        for (int j = 0; ok && j < nblk; ++j) {
+          const int s = j % kStages;
+          const uint32_t ph = uint32_t(j / kStages) & 1u;
+          if (j >= kStages) ok = wait_sleep(&empty[s], ph ^ 1u, abort_flag, a.status, is_k ? 41 : 42);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[s], kTileBytes);
+          if (is_k)
+            tma_load_3d(sm.k[s], &map_k, &full[s], 0, j * kKeys, bh_k);
+          else
+            tma_load_3d(sm.v[s], &map_v, &full[s], j * kKeys, 0, bh_k);
+          issued = j + 1;
+        }
+        // every copy this thread issued lands before the CTA exits
+        if (is_k) mbar_wait_bounded(&sm.q_full, 0, nullptr, a.status, 43, kTimeoutNs);
+        for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+          mbar_wait_bounded(&full[j % kStages], uint32_t(j / kStages) & 1u, nullptr, a.status, 43, kTimeoutNs);
       }
       __syncwarp();
-      return true;
-    };
-    if (ok) ok = issue_s(0);
-    if (ok && nblk > 1) ok = issue_s(1);
-    for (int j = 0; ok && j < nblk; ++j) {
-      const int s = j % kStages, b = j & 1;
-      ok = warp_wait(&sm.p_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 54) &&
-           warp_wait(&sm.v_full[s], uint32_t(j / kStages) & 1u, sm, a.status, 55) &&
-           warp_wait(&sm.pv_empty[b], uint32_t(j >> 1) & 1u, sm, a.status, 56);
-      if (!ok) break;
-      tc_fence_after();
+    } else if (warp == 1) {
+      // ---------------- MMA issuers: lane 0 the S stream, lane 1 the P.V stream ----------------
+      // S(j) goes into TMEM slot j % 4 once the correction warps are done with
+      // P.V(j - 4) there; P.V(j) goes into the same slot once P(j) is written
+      // (the softmax has finished reading S(j)).  Two independent threads, so
+      // that neither stream waits behind the other's inputs.  Both MMAs start
+      // from a zero accumulator.
       if (lane == 0) {
-        const uint64_t pd = smem_desc_k_sw128(sm.p[b]), vd = smem_desc_k_sw128(sm.v[s]);
+        bool ok = wait_sleep(&sm.q_full, 0, abort_flag, a.status, 51);
+        const uint64_t qd = smem_desc_k_sw128(sm.q);
+        for (int j = 0; ok && j < nblk; ++j) {
+          const int s = j % kStages, slot = j % kSlots;
+          ok = wait_sleep(&sm.k_full[s], uint32_t(j / kStages) & 1u, abort_flag, a.status, 52) &&
+               (j < kSlots || wait_sleep(&sm.slot_free[slot], uint32_t(j / kSlots - 1) & 1u, abort_flag, a.status, 53));
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t kd = smem_desc_k_sw128(sm.k[s]);
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 32; ++kk)
-          mma_i8(tmem + kColPV + 128u * b, pd + uint64_t(2 * kk), vd + uint64_t(2 * kk), kIdescPV, 1);
-        mma_commit(&sm.v_empty[s]);
-        mma_commit(&sm.pv_full[b]);
+          for (int kk = 0; kk < kDim / 32; ++kk)
+            mma_i8(tmem + 128u * slot, qd + uint64_t(2 * kk), kd + uint64_t(2 * kk), kIdescQK, kk);
+          mma_commit(&sm.k_empty[s]);
+          mma_commit(&sm.s_full[slot]);
+        }
+        // every MMA this thread issued completes before TMEM is released
+        mma_commit(&sm.drain);
+      } else if (lane == 1) {
+        bool ok = true;
+        for (int j = 0; ok && j < nblk; ++j) {
+          const int s = j % kStages, slot = j % kSlots;
+          ok = wait_sleep(&sm.p_full[slot], uint32_t(j / kSlots) & 1u, abort_flag, a.status, 54) &&
+               wait_sleep(&sm.v_full[s], uint32_t(j / kStages) & 1u, abort_flag, a.status, 55);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t pd = smem_desc_k_sw128(sm.p[slot]), vd = smem_desc_k_sw128(sm.v[s]);
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 32; ++kk)
+            mma_i8(tmem + 128u * slot, pd + uint64_t(2 * kk), vd + uint64_t(2 * kk), kIdescPV, kk);
+          mma_commit(&sm.v_empty[s]);
+          mma_commit(&sm.pv_full[slot]);
+        }
+        mma_commit(&sm.drain);
       }
+      if (lane < 2) mbar_wait_bounded(&sm.drain, 0, nullptr, a.status, 57, kTimeoutNs);
       __syncwarp();
-      if (j + 2 < nblk) ok = issue_s(j + 2);
-    }
-    // every MMA issued here completes before TMEM is released
-    if (lane == 0) {
-      mma_commit(&sm.drain);
-      mbar_wait_bounded(&sm.drain, 0, nullptr, a.status, 57, kTimeoutNs);
-    }
-    __syncwarp();
-  } else if (warp < 2 + kCorrWarps) {
+    }   // warps 2 and 3: idle
+  } else if (warp < kSoftWarp0) {
+    regs_set<kRegsCorr>();
     // ---------------- correction: O <- fmaf(float(P.V), tile_scale, O * o_scale) ----------------
     // Thread = (query row, half): TMEM lane r of quadrant warp % 4 and output
     // channels [64 h, 64 h + 64), O of them in registers.  Block j's P.V joins O
-    // here while the softmax works on block j + 1; o_scale and tile_scale come
-    // from the softmax warp of the row.  x * 1 == x for every value O takes (FTZ
+    // here while the softmax works on later blocks; o_scale and tile_scale come
+    // from the block's chain step.  x * 1 == x for every value O takes (FTZ
     // arithmetic makes no subnormals), so a warp rescales all of its rows when
     // any of them needs it.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - kCorrWarp0) >> 2;
     const int r = quarter * 32 + lane;
     const int row = bx * kRows + r;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint32_t col0 = uint32_t(64 * half);
-    const uint64_t nbias2 = pkf(-kBiasF, -kBiasF);
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      tmem_fill_32cols(tmem + kColPV + 128u * b + lane_off + col0, kBias);
-      tmem_fill_32cols(tmem + kColPV + 128u * b + lane_off + col0 + 32, kBias);
-    }
-    tmem_store_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&sm.pv_empty[0]);
-      mbar_arrive(&sm.pv_empty[1]);
-    }
     uint64_t o2[32];   // O of channels col0 + [0, 64), as FP32 pairs
 #pragma unroll
     for (int i = 0; i < 32; ++i) o2[i] = 0ull;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
-      const int b = j & 1, slot = j % kScSlots;
-      if (!warp_wait(&sm.sc_full[slot], uint32_t(j / kScSlots) & 1u, sm, a.status, 71)) {
+      const int slot = j % kSlots;
+      const uint32_t ph = uint32_t(j / kSlots) & 1u;
+      if (!warp_wait(&sm.sc_full[slot], ph, sm, a.status, 71)) {
         ok = false;
         break;
       }
       const float2 sc = sm.sc[slot][r];
-      if (!warp_wait(&sm.pv_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 72)) {
+      if (!warp_wait(&sm.pv_full[slot], ph, sm, a.status, 72)) {
         ok = false;
         break;
       }
@@ -482,23 +481,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) o2[i] = mul2(o2[i], os2);
       }
       const uint64_t ts2 = pkf(sc.y, sc.y);
-      const uint32_t t_pv = tmem + kColPV + 128u * b + lane_off + col0;
+      const uint32_t t_pv = tmem + 128u * slot + lane_off + col0;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint32_t pv[16];
-        tmem_load_16cols(t_pv + 16 * g, pv);
+      for (int g = 0; g < 2; ++g) {
+        uint32_t pv[32];
+        tmem_load_32cols(t_pv + 32 * g, pv);
         tmem_load_wait();
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o2[8 * g + i] = fma2(add2(pk(pv[2 * i], pv[2 * i + 1]), nbias2), ts2, o2[8 * g + i]);
+        for (int i = 0; i < 16; ++i)
+          o2[16 * g + i] = fma2(pkf(float(int(pv[2 * i])), float(int(pv[2 * i + 1]))), ts2, o2[16 * g + i]);
       }
-      // P.V buffer b is rebiased for block j + 2
-      tmem_fill_32cols(t_pv, kBias);
-      tmem_fill_32cols(t_pv + 32, kBias);
-      tmem_store_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.pv_empty[b]);
+      if (lane == 0) mbar_arrive(&sm.slot_free[slot]);
     }
     // O = (O / d) * v_scale in BF16
     if (ok && warp_wait(&sm.inv_full, 0, sm, a.status, 73) && row < a.q_len) {
@@ -522,122 +517,166 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax: thread = query row = TMEM lane ----------------
-    // The row's 128 scores are read from TMEM in two 64-column halves, twice:
-    // once for the class maxima, once for the probabilities.  The four class
-    // denominators are kept in key order, as the reference's four quad threads
-    // keep theirs.
+    regs_set<kRegsSoft>();
+    // ---------------- softmax ----------------
+    // Two warps per TMEM lane quadrant, thread = query row: warp `sub` takes the
+    // blocks j with j % 2 == sub.  A block's probabilities, P codes and
+    // denominators depend only on its own maximum, so the two warps compute
+    // them side by side; the running maximum and the class-denominator chain --
+    // the reference's sequential part -- pass from block to block, and so from
+    // warp to warp, in a short chain step through shared memory.  The four
+    // class denominators take the 16-key runs in key order, as the reference's
+    // four quad threads do.
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
+    const int sub = (warp - kSoftWarp0) >> 2;
+    const int r = quarter * 32 + lane;                  // row within the block (TMEM lane)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g) tmem_fill_32cols(tmem + kColS + 128u * b + lane_off + 32 * g, kBias);
-    }
-    tmem_store_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&sm.s_empty[0]);
-      mbar_arrive(&sm.s_empty[1]);
-    }
     const float q_scale = a.qs[int64_t(bh_q) * a.q_blocks * 32 + bx * 32 + (r >> 5) * 8 + (r & 7)];
     const float sm_base = a.sm_scale * kLog2e;
     const float* kscale = a.ks + int64_t(bh_k) * nblk * 4;
-    float kn[4];                              // the next block's K scales, loaded a block early
+    float kn[4];                              // the K scales of this warp's next block
 #pragma unroll
-    for (int t = 0; t < 4; ++t) kn[t] = __ldg(kscale + t);
-    const uint64_t nbias2 = pkf(-kBiasF, -kBiasF);
-    float m = -50000.0f;
-    float d[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-    bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j & 1;
+    for (int t = 0; t < 4; ++t) kn[t] = sub < nblk ? __ldg(kscale + sub * 4 + t) : 0.0f;
+    for (int j = sub; j < nblk; j += 2) {
       const bool last = j == nblk - 1;
-      const uint32_t t_s = tmem + kColS + 128u * b + lane_off;
-      // S buffer b ^ 1 (block j - 1's scores, read) is rebiased for block j + 1;
-      // the stores complete under the maxima below
-      if (j > 0) {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) tmem_fill_32cols(tmem + kColS + 128u * (b ^ 1) + lane_off + 32 * g, kBias);
-      }
-      if (!warp_wait(&sm.s_full[b], uint32_t(j >> 1) & 1u, sm, a.status, 61)) {
-        ok = false;
-        break;
-      }
+      const int slot = j % kSlots;
+      const uint32_t t_s = tmem + 128u * slot + lane_off;
+      if (!warp_wait(&sm.s_full[slot], uint32_t(j / kSlots) & 1u, sm, a.status, 61)) break;
       tc_fence_after();
       float scale[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) scale[t] = sm_base * (q_scale * kn[t]);
-      if (!last) {
+      if (j + 2 < nblk) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) kn[t] = __ldg(kscale + (j + 1) * 4 + t);
+        for (int t = 0; t < 4; ++t) kn[t] = __ldg(kscale + (j + 2) * 4 + t);
       }
       // per-class maxima: class t holds keys 2t, 2t+1, 2t+8, 2t+9 of every run
       // of 16 (integers; in the last block floats, with the keys past Sk at
       // -1e30 and the maximum starting at -50000)
       float mx[4];
-      uint32_t v[64];
+      uint32_t v[32];
       if (!last) {
-        // two chains per class (keys 2t, 2t+1 and keys 2t+8, 2t+9 of each run)
-        float mb[4][2];
+        int mb[4][2];   // two chains per class
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_load_64cols(t_s + 64 * hh, v);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          tmem_load_32cols(t_s + 32 * q4, v);
           tmem_load_wait();
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int o = 2 * t + 8 * e;
-              float x = hh == 0 ? max3(as_f(v[o]), as_f(v[o + 1]), as_f(v[16 + o]))
-                                : max3(mb[t][e], as_f(v[o]), as_f(v[o + 1]));
-              x = hh == 0 ? max3(x, as_f(v[17 + o]), as_f(v[32 + o])) : max3(x, as_f(v[16 + o]), as_f(v[17 + o]));
-              x = hh == 0 ? max3(x, as_f(v[33 + o]), as_f(v[48 + o])) : max3(x, as_f(v[32 + o]), as_f(v[33 + o]));
-              x = hh == 0 ? fmaxf(x, as_f(v[49 + o])) : max3(x, as_f(v[48 + o]), as_f(v[49 + o]));
-              mb[t][e] = x;
+              int x = max(max(int(v[o]), int(v[o + 1])), max(int(v[16 + o]), int(v[17 + o])));
+              mb[t][e] = q4 == 0 ? x : max(mb[t][e], x);
             }
           }
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) mx[t] = __fadd_rn(fmaxf(mb[t][0], mb[t][1]), -kBiasF);
+        for (int t = 0; t < 4; ++t) mx[t] = float(max(mb[t][0], mb[t][1]));
       } else {
 #pragma unroll
         for (int t = 0; t < 4; ++t) mx[t] = -50000.0f;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_load_64cols(t_s + 64 * hh, v);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          tmem_load_32cols(t_s + 32 * q4, v);
           tmem_load_wait();
-          const int key0 = j * kKeys + 64 * hh;
+          const int key0 = j * kKeys + 32 * q4;
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float sc = key0 + i < a.kv_len ? unbias(v[i]) : -1.0e30f;
+          for (int i = 0; i < 32; ++i) {
+            const float sc = key0 + i < a.kv_len ? float(int(v[i])) : -1.0e30f;
             mx[(i & 7) >> 1] = fmaxf(mx[(i & 7) >> 1], sc);
           }
         }
-      }
-      if (j > 0) {
-        tmem_store_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.s_empty[b ^ 1]);
       }
       float mt[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) mt[t] = fmaf(mx[t], scale[t], -kExpOffset);
       const float tile_m = fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3]));
-      const float m_prev = m;
-      m = fmaxf(m_prev, tile_m);
+      // probabilities -> u8 P (key order of V: the four keys of class t of each
+      // 16-key run in one word at byte 4t) and the runs' class denominators.
+      // P buffer j % 4 was last read by P.V(j - 4), complete since S(j) is.
+      const float neg_m = -tile_m;
+      const uint64_t negm2 = pkf(neg_m, neg_m);
+      uint64_t scale2[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) scale2[t] = pkf(scale[t], scale[t]);
+      uint8_t* const prow = sm.p[slot] + (r >> 3) * 1024 + (r & 7) * 128;
+      float den[8][4];
+      // (two copies of the loop, so that neither has a branch inside)
+      if (!last) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          tmem_load_32cols(t_s + 32 * q4, v);
+          tmem_load_wait();
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t words[4];
+            const int chunk = 2 * q4 + c2;        // 16-key run = 16-byte chunk of the P row
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i0 = 16 * c2 + 2 * t;
+              // x = fmaf(float(s), scale_t, -tile_m), two keys per instruction
+              uint32_t x0, x1, x2, x3;
+              upk(fma2(pkf(float(int(v[i0])), float(int(v[i0 + 1]))), scale2[t], negm2), x0, x1);
+              upk(fma2(pkf(float(int(v[i0 + 8])), float(int(v[i0 + 9]))), scale2[t], negm2), x2, x3);
+              words[t] = u8x4(ex2(as_f(x0)), ex2(as_f(x1)), ex2(as_f(x2)), ex2(as_f(x3)));
+              // the integer sum of the four codes, exact as a float
+              den[chunk][t] = float(int(__dp4a(words[t], 0x01010101u, 0u)));
+            }
+            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
+                                                                                   words[3]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          tmem_load_32cols(t_s + 32 * q4, v);
+          tmem_load_wait();
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t words[4];
+            const int chunk = 2 * q4 + c2;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i0 = 16 * c2 + 2 * t;
+              const int k0 = j * kKeys + 32 * q4 + i0;
+              const float s0 = k0 < a.kv_len ? float(int(v[i0])) : -1.0e30f;
+              const float s1 = k0 + 1 < a.kv_len ? float(int(v[i0 + 1])) : -1.0e30f;
+              const float s2 = k0 + 8 < a.kv_len ? float(int(v[i0 + 8])) : -1.0e30f;
+              const float s3 = k0 + 9 < a.kv_len ? float(int(v[i0 + 9])) : -1.0e30f;
+              const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
+              const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
+              words[t] = u8x4(p0, p1, p2, p3);
+              den[chunk][t] = (p0 + p1) + (p2 + p3);   // the last block sums the unrounded p
+            }
+            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
+                                                                                   words[3]);
+          }
+        }
+      }
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[slot]);
+      // chain step: the running maximum and the denominators, block after block
+      float m_prev = -50000.0f;
+      float d[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+      if (j > 0) {
+        if (!warp_wait(&sm.cbar[quarter], uint32_t(j - 1) & 1u, sm, a.status, 62)) break;
+        m_prev = sm.cm[r];
+        const float4 dd = sm.cd[r];
+        d[0] = dd.x;
+        d[1] = dd.y;
+        d[2] = dd.z;
+        d[3] = dd.w;
+      }
+      const float m = fmaxf(m_prev, tile_m);
       const float smaller = ex2(-fabsf(m_prev - tile_m));
       const float o_scale = m_prev < tile_m ? smaller : 1.0f;
       const float tile_scale = tile_m < m_prev ? smaller : 1.0f;
       // o_scale and tile_scale of this block to the row's correction threads.
-      // Slot j % 4 was last read for block j - 4, whose fold completed before
-      // P.V(j - 2) was issued, which came before S(j) (waited on above).
-      sm.sc[j % kScSlots][r] = make_float2(o_scale, tile_scale);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.sc_full[j % kScSlots]);
+      // Slot j % 4 was last read for block j - 4, before the correction released
+      // that block's TMEM slot for S(j) (waited on above).
+      sm.sc[slot][r] = make_float2(o_scale, tile_scale);
       // blocks before the last rescale d on their own (the reference applies
       // o_scale under a branch); the last block folds d * o_scale into its
       // first denominator update, as the reference's straight-line float path
@@ -646,78 +685,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t) d[t] *= o_scale;
       }
-      // pass 2: probabilities -> u8 P (key order of V: the four keys of class t
-      // of each 16-key run in one word at byte 4t), denominators in key order.
-      // P buffer b was last read by P.V(j - 2), complete since S(j) is.
-      const float neg_m = -tile_m;
-      const uint64_t negm2 = pkf(neg_m, neg_m);
-      uint64_t scale2[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) scale2[t] = pkf(scale[t], scale[t]);
-      uint8_t* prow = sm.p[b] + (r >> 3) * 1024 + (r & 7) * 128;
-      // (two copies of the loop, so that neither has a branch inside: the
-      // groups of four keys then interleave freely)
-      if (!last) {
+      for (int c = 0; c < 8; ++c) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_load_64cols(t_s + 64 * hh, v);
-          tmem_load_wait();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t words[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const int i0 = 16 * c + 2 * t;
-              // s = biased - 1.5 * 2^23 and x = fmaf(s, scale_t, -tile_m), two keys per instruction
-              uint32_t x0, x1, x2, x3;
-              upk(fma2(add2(pk(v[i0], v[i0 + 1]), nbias2), scale2[t], negm2), x0, x1);
-              upk(fma2(add2(pk(v[i0 + 8], v[i0 + 9]), nbias2), scale2[t], negm2), x2, x3);
-              words[t] = u8x4(ex2(as_f(x0)), ex2(as_f(x1)), ex2(as_f(x2)), ex2(as_f(x3)));
-              // the integer sum of the four codes (dp4a onto the bias: the float comes out exact)
-              d[t] = fmaf(unbias(__dp4a(words[t], 0x01010101u, kBias)), tile_scale, d[t]);
-            }
-            const int chunk = 4 * hh + c;        // 16-byte chunk of the P row
-            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
-                                                                                   words[3]);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_load_64cols(t_s + 64 * hh, v);
-          tmem_load_wait();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t words[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const int i0 = 16 * c + 2 * t;
-              const int k0 = j * kKeys + 64 * hh + i0;
-              const float s0 = k0 < a.kv_len ? unbias(v[i0]) : -1.0e30f;
-              const float s1 = k0 + 1 < a.kv_len ? unbias(v[i0 + 1]) : -1.0e30f;
-              const float s2 = k0 + 8 < a.kv_len ? unbias(v[i0 + 8]) : -1.0e30f;
-              const float s3 = k0 + 9 < a.kv_len ? unbias(v[i0 + 9]) : -1.0e30f;
-              const float p0 = ex2(fmaf(s0, scale[t], neg_m)), p1 = ex2(fmaf(s1, scale[t], neg_m));
-              const float p2 = ex2(fmaf(s2, scale[t], neg_m)), p3 = ex2(fmaf(s3, scale[t], neg_m));
-              words[t] = u8x4(p0, p1, p2, p3);
-              const float den = (p0 + p1) + (p2 + p3);   // the last block sums the unrounded p
-              d[t] = (hh == 0 && c == 0) ? fmaf(d[t], o_scale, __fmul_rn(den, tile_scale))
-                                         : fmaf(den, tile_scale, d[t]);
-            }
-            const int chunk = 4 * hh + c;
-            *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(words[0], words[1], words[2],
-                                                                                   words[3]);
-          }
-        }
+        for (int t = 0; t < 4; ++t)
+          d[t] = (last && c == 0) ? fmaf(d[t], o_scale, __fmul_rn(den[c][t], tile_scale))
+                                  : fmaf(den[c][t], tile_scale, d[t]);
       }
-      fence_async_shared();
+      if (!last) {
+        sm.cm[r] = m;
+        sm.cd[r] = make_float4(d[0], d[1], d[2], d[3]);
+      } else {
+        sm.xinv[r] = rcp((d[0] + d[1]) + (d[2] + d[3]));
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full[b]);
-    }
-    if (ok) {
-      sm.xinv[r] = rcp((d[0] + d[1]) + (d[2] + d[3]));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.inv_full);
+      if (lane == 0) {
+        mbar_arrive(&sm.sc_full[slot]);
+        mbar_arrive(last ? &sm.inv_full : &sm.cbar[quarter]);
+      }
     }
   }
   tc_fence_before();
@@ -853,6 +838,16 @@ H3SK_EXPORT int h3_dense_launch_window(const H3DenseArgs* a, uintptr_t stream_pt
   args.sm_scale = a->sm_scale;
   args.status = status;
   const int smem = int(sizeof(Smem)) + 1024;
+  // the warpgroups' setmaxnreg shares need the block's launch registers; refuse
+  // (never launch) a build whose launch register count would leave them short
+  static int launch_regs = -1;
+  if (launch_regs < 0) {
+    cudaFuncAttributes attr;
+    const cudaError_t fe = cudaFuncGetAttributes(&attr, attention_kernel);
+    if (fe != cudaSuccess) return fe;
+    launch_regs = attr.numRegs;
+  }
+  if (launch_regs < kRegsLaunch) return cudaErrorInvalidConfiguration;
   cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const dim3 grid(unsigned(q_blocks - start), a->qo_heads, a->batch);

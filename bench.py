@@ -70,6 +70,8 @@ def parse_args():
                          "operands (56 heads, one sequence of --attn-tokens tokens)")
     ap.add_argument("--attn-tokens", type=int, default=32768,
                     help="sequence length of the --op attention line (default 32768)")
+    ap.add_argument("--attn-heads", type=int, default=56,
+                    help="head count of the --op attention line (default 56, the H3 geometry)")
     return ap.parse_args()
 
 
@@ -817,13 +819,13 @@ def run_attention(args):
 
     from h3_speedkit import _lib
     from h3_speedkit.ops.dense import DenseLibrary, allocate_output
-    heads, m = 56, args.attn_tokens
+    heads, m = args.attn_heads, args.attn_tokens
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     packed = _attention_operands(m, heads, dev)
     ops = 4.0 * m * m * 128 * heads          # Q K^T and P V, 2 ops per multiply-add
     scores = float(m) * m * heads            # one ex2 per score
-    cfg = {"workload": f"INT8 attention, H3 geometry: 56 heads x 128, Sq = Sk = {m}, batch 1",
+    cfg = {"workload": f"INT8 attention, H3 geometry: {heads} heads x 128, Sq = Sk = {m}, batch 1",
            "tokens": m, "heads": heads, "head_dim": 128, "layout": "Q/K [1,H,S,128], V [H*128, S], O BSHD",
            "l2": "inputs larger than L2", "timing": f"median of {args.steps} launches"}
     base = {"metric": "INT8 attention TOPS (H3 geometry)", "unit": "TOPS", "n_gpus": 1, "steps": args.steps,

@@ -534,10 +534,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float q_scale = a.qs[int64_t(bh_q) * a.q_blocks * 32 + bx * 32 + (r >> 5) * 8 + (r & 7)];
     const float sm_base = a.sm_scale * kLog2e;
     const float* kscale = a.ks + int64_t(bh_k) * nblk * 4;
+    bool return_early = false;
     float kn[4];                              // the K scales of this warp's next block
 #pragma unroll
     for (int t = 0; t < 4; ++t) kn[t] = sub < nblk ? __ldg(kscale + sub * 4 + t) : 0.0f;
-    for (int j = sub; j < nblk; j += 2) {
+    // The odd-block warps start once P(0) is written: the two warps of a
+    // quadrant then run half a round apart, so that one's exp2 stream overlaps
+    // the other's maxima and chain step (the chain's order keeps the offset).
+    if (sub == 1 && nblk > 1 && !warp_wait(&sm.p_full[0], 0, sm, a.status, 60)) return_early = true;
+    for (int j = sub; !return_early && j < nblk; j += 2) {
       const bool last = j == nblk - 1;
       const int slot = j % kSlots;
       const uint32_t t_s = tmem + 128u * slot + lane_off;

@@ -83,11 +83,16 @@ class QKV:
             raise ValueError("QKV operand dtype/shape does not match the CUDA ABI: " +
                              str([(str(t.dtype), tuple(t.shape), str(dtype), shape)
                                   for t, dtype, shape in expected]))
-        out = self.run(q, w, xs, ws, rope, qw, kw, eps, heads=HEADS)
+        return self.pack(self.run(q, w, xs, ws, rope, qw, kw, eps, heads=HEADS), m, HEADS)
+
+    @staticmethod
+    def pack(out, m, heads):
+        """The attention operands of a ``run`` result, as the reference's QKV op
+        returns them (ops/qkv.py:80-83): codes and scales viewed [1, H, ...]."""
         parts = (m + 127) // 128
         return _result_type()(
-            q=out["qi"].view(1, HEADS, m, HEAD), k=out["ki"].view(1, HEADS, m, HEAD), v=out["vi"],
-            q_scale=out["qs"].view(1, HEADS, parts * 32), k_scale=out["ks"].view(1, HEADS, parts * 4),
+            q=out["qi"].view(1, heads, m, HEAD), k=out["ki"].view(1, heads, m, HEAD), v=out["vi"],
+            q_scale=out["qs"].view(1, heads, parts * 32), k_scale=out["ks"].view(1, heads, parts * 4),
             v_scale=out["vs"], original_head_dim=HEAD, input_dtype=torch.bfloat16,
             attention_scale=HEAD ** -0.5, cta_k=128, attn_mask=None)
 

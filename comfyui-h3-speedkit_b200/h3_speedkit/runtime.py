@@ -11,11 +11,13 @@ mutation; a launch failure aborts the request, never retried).  Differences:
   ``libh3sk_b200.so`` published under the reference's library names and checked
   against ``_native/build.json`` (same manifest schema);
 * the hidden width K is generic (the reference fixes 5376);
-* attention is not part of this path: ``Backend.block`` takes an ``attention``
-  callable on the BF16 Q/K/V slices of the QKV output (identity on V in the
-  benchmark configuration).  ``patch_model`` installs replacements only with an
-  attention provider; without one it raises ``Unsupported`` and the model stays
-  unpatched.
+* attention: ``Backend.block(..., attention="int8")`` runs the reference's own
+  attention half (runtime.py:129-146): the QKV op's pre-quantised operands, the
+  INT8 attention (BSHD, rows below the window zero), the register ConvRot
+  quantiser of its output, outproj.  ``attention=None`` is the identity on V of
+  the benchmark configuration, and a callable on the BF16 Q/K/V slices of a
+  plain QKV projection stays possible.  ``patch_model`` uses "int8" unless told
+  otherwise.
 
 ComfyUI and comfy-kitchen are imported lazily, only on the model-patching path.
 """
@@ -35,6 +37,7 @@ import torch
 
 from . import _lib
 from .ops.convrot import ConvRotRegister, quantize_int8_rowwise_convrot64
+from .ops.dense import DenseLibrary, allocate_output
 from .ops.gemm import int8_gate_residual, int8_linear
 from .ops.norm_quant import DEVICE_CAPABILITY, NormQuant
 
@@ -91,6 +94,9 @@ class Backend:
         self.lib = _lib.load(library)
         self.norm = NormQuant(library)
         self.convrot = ConvRotRegister(library)
+        from .ops.qkv import QKV
+        self.qkv = QKV(self.directory)
+        self.dense = DenseLibrary(library)
         # the reference's GEMM entry points by their own names (runtime.py:62-66)
         self.fc1, self.gate = self.lib.h3_int8, self.lib.h3_int8_gate
 
@@ -129,21 +135,48 @@ class Backend:
         int8_gate_residual(q[window], w, qs[window].reshape(-1), ws, x[window],
                            gate.to(dtype=torch.bfloat16).contiguous(), rows[window])
 
+    def int8_attention(self, block, qi, qs, w, ws, rope, skip):
+        """The reference's attention half up to outproj (runtime.py:129-146): the QKV
+        op's pre-quantised operands (per-head RMS, RoPE, K anchors, rotation, INT8),
+        the INT8 attention from query block skip // 128 on (rows below it zero),
+        its BSHD output as [M, heads * 128] BF16."""
+        m, dev = qi.shape[0], qi.device
+        if rope is None:
+            raise Unsupported("INT8 attention needs the block's RoPE table")
+        heads = w.shape[0] // (3 * 128)
+        qw = block.attn.q_norm.weight.to(device=dev, dtype=torch.bfloat16).contiguous()
+        kw = block.attn.k_norm.weight.to(device=dev, dtype=torch.bfloat16).contiguous()
+        rope = rope.to(device=dev, dtype=torch.bfloat16).contiguous()
+        packed = self.qkv.pack(self.qkv.run(qi, w, qs, ws, rope, qw, kw, float(block.attn.q_norm.eps),
+                                            heads=heads), m, heads)
+        output = allocate_output(packed, "bshd")
+        self.dense.bind(packed, output, start=skip // 128)()
+        return output.transpose(1, 2).reshape(m, heads * 128)
+
     def block(self, block, x, t_emb, segments, rope=None, *, rows, skip=0, counts=None, attention=None,
               mlp_act="gelu_tanh"):
         """One block of the linear path on BF16 tokens x [M, D], updated in place
-        (runtime.py:126-164).  attention(q, k, v) -> [M, D_attn] BF16; None is the
-        identity on V.  mlp_act: 'gelu_tanh' (FC1 epilogue, the benchmark
-        configuration) or 'swiglu' (the H3 geometry: FC1 rows are [gate | up])."""
+        (runtime.py:126-164).  attention: "int8" runs the reference's attention
+        half (QKV op, INT8 attention, register ConvRot of its output); a callable
+        attention(q, k, v) -> [M, D_attn] BF16 takes the slices of a plain QKV
+        projection; None is the identity on V (the benchmark configuration).
+        mlp_act: 'gelu_tanh' (FC1 epilogue, the benchmark configuration) or
+        'swiglu' (the H3 geometry: FC1 rows are [gate | up])."""
         counts = Counter() if counts is None else counts
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = block.adaln_proj(t_emb)
         qi, qs = self.normalize(block.norm1, x, shift_msa, scale_msa, rows)
         w, ws = self.plain_weight(block.attn.qkv_proj, x)
-        qkv = int8_linear(qi, w, qs, ws)
-        width = qkv.shape[1] // 3
-        q_, k_, v_ = qkv[:, :width], qkv[:, width:2 * width], qkv[:, 2 * width:]
-        attn = v_ if attention is None else attention(q_, k_, v_)
-        aq, asc = quantize_int8_rowwise_convrot64(attn)
+        if attention == "int8":
+            attn = self.int8_attention(block, qi, qs, w, ws, rope, skip)
+            aq = torch.empty(attn.shape, device=x.device, dtype=torch.int8)
+            asc = torch.empty((len(x), 1), device=x.device, dtype=torch.float32)
+            self.convrot.bind(attn, aq, asc, check_finite=False)()
+        else:
+            qkv = int8_linear(qi, w, qs, ws)
+            width = qkv.shape[1] // 3
+            q_, k_, v_ = qkv[:, :width], qkv[:, width:2 * width], qkv[:, 2 * width:]
+            attn = v_ if attention is None else attention(q_, k_, v_)
+            aq, asc = quantize_int8_rowwise_convrot64(attn)
         self.gate_projection(block.attn.out_proj, aq, asc, x, gate_msa, rows, skip)
         qi, qs = self.normalize(block.norm2, x, shift_mlp, scale_mlp, rows)
         w1, ws1 = self.plain_weight(block.mlp.fc1, x)
@@ -229,7 +262,7 @@ class BlockReplacement:
 class ModelPatch:
     """Request wrapper + block replacements (the roles of runtime.py:167-308)."""
 
-    def __init__(self, model, backend, verify_new_shapes=True, attention=None, blocks=BLOCKS):
+    def __init__(self, model, backend, verify_new_shapes=True, attention="int8", blocks=BLOCKS):
         self.model = model
         self.backend = backend
         self.attention = attention
@@ -319,13 +352,15 @@ class ModelPatch:
         return {"img": expected}
 
 
-def patch_model(model, directory=None, *, release_embeddings=True, verify_new_shapes=True, attention=None,
+def patch_model(model, directory=None, *, release_embeddings=True, verify_new_shapes=True, attention="int8",
                 backend=None):
     """Return a Comfy clone with explicit block replacements and a request
-    wrapper (runtime.py:311-338).  The original model is not modified."""
+    wrapper (runtime.py:311-338).  The original model is not modified.
+    attention: "int8" (the reference's QKV op and INT8 attention, the default) or
+    a callable provider on the BF16 Q/K/V slices; None (identity) is refused."""
     import comfy.patcher_extension as pe
     if attention is None:
-        raise Unsupported("The B200 linear path needs an attention provider (attention is outside this path)")
+        raise Unsupported("The B200 path needs an attention provider: 'int8' or a callable (None is identity)")
     clone = model.clone()
     options = clone.model_options.setdefault("transformer_options", {})
     existing = options.get("patches_replace", {}).get("dit", {})

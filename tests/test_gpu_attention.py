@@ -10,6 +10,8 @@ op (pinned to the reference's r84_kfourwarp.cu elsewhere) on seeded projections
 reference's key permutation -- and, for the corner cases, from seeded random
 codes and scales.
 """
+import ctypes as ct
+
 import pytest
 import torch
 
@@ -116,3 +118,89 @@ def test_attention_rejects_bad_layouts_before_launch(device):
     padded = torch.empty((1, 2, 400, 128), dtype=torch.bfloat16, device=device)[:, :, :300]
     with pytest.raises(ValueError, match="BHSD or BSHD"):
         lib.bind(packed, padded)
+
+
+def _h3_block_ns(bw, qw, kw):
+    from types import SimpleNamespace as NS
+
+    def linear(w, s):
+        return NS(weight=w, weight_int8=w, weight_scale=s)
+
+    return NS(adaln_proj=lambda t: (bw.shift_msa, bw.scale_msa, bw.gate_msa, bw.shift_mlp, bw.scale_mlp,
+                                    bw.gate_mlp),
+              norm1=NS(weight=bw.norm1, eps=1e-6), norm2=NS(weight=bw.norm2, eps=1e-6),
+              attn=NS(qkv_proj=linear(bw.qkv, bw.qkv_s), out_proj=linear(bw.out, bw.out_s),
+                      q_norm=NS(weight=qw, eps=1e-6), k_norm=NS(weight=kw, eps=1e-6)),
+              mlp=NS(fc1=linear(bw.fc1, bw.fc1_s), fc2=linear(bw.fc2, bw.fc2_s)))
+
+
+def _reference_block(x, bw, qw, kw, rope, rows, skip):
+    """runtime.py:126-164 of the reference as a chain of its own kernels (compiled
+    from its sources): the K=5376 prologue, the sample gather, the K anchor
+    detector, the fused QKV kernel r84_kfourwarp.cu, the INT8 attention
+    dense_ring.cu, the register ConvRot quantiser, gate.cu and fc1.cu, the
+    Kitchen SwiGLU quantiser.  Two steps have no C kernel in the reference and
+    come from this library, pinned elsewhere: the K-only sample projection and
+    the V quantiser (Triton in the reference)."""
+    from h3_speedkit import _lib
+    lib = _lib.load()
+    dev, m = x.device, x.shape[0]
+    st = torch.cuda.current_stream().cuda_stream
+    q, qs = ref_gpu.norm_quant(x, bw.norm1, bw.shift_msa, bw.scale_msa, rows, 1e-6)
+    sq, sx, sr = ref_gpu.sample_gather(q, qs, rope.view(m, 192))
+    sd = torch.empty((3, 56, 9, 128), dtype=torch.bfloat16, device=dev)
+    assert lib.h3_sample_konly_ex(sq.data_ptr(), bw.qkv.data_ptr(), sx.data_ptr(), bw.qkv_s.data_ptr(),
+                                  sd.data_ptr(), sr.data_ptr(), qw.data_ptr(), kw.data_ptr(),
+                                  ct.c_float(1e-6), 9, 56, 5376, None, st) == 1
+    sk = sd[1].contiguous()
+    anchors = ref_gpu.sample_anchor(sk)
+    t = ref_gpu.qkv_quant_kv(q, bw.qkv, qs, bw.qkv_s, rope, qw, kw, 1e-6, sk, anchors)
+    parts = (m + 127) // 128
+    vi = torch.empty((56 * 128, parts * 128), dtype=torch.int8, device=dev)
+    vs = torch.empty((56 * 128,), dtype=torch.float32, device=dev)
+    vinv = torch.empty_like(vs)
+    assert lib.h3_quant_v(t["vp"].data_ptr(), t["d"][2].data_ptr(), vi.data_ptr(), vs.data_ptr(),
+                          vinv.data_ptr(), m, 56, st) == 1
+    o = ref_gpu.dense(t["qi"].view(1, 56, m, 128), t["ki"].view(1, 56, m, 128), vi,
+                      t["qs"].view(1, 56, parts * 32), t["ks"].view(1, 56, parts * 4), vs, 128 ** -0.5,
+                      layout="bshd", start=skip // 128)
+    attn = o.transpose(1, 2).reshape(m, 7168)
+    aq, asc, _ = ref_gpu.convrot_register(attn, 0)
+    w = slice(skip, None)
+    ref_gpu.int8_gate(aq[w], bw.out, asc.view(-1)[w], bw.out_s, bw.gate_msa, rows[w], x[w], out=x[w])
+    q, qs = ref_gpu.norm_quant(x, bw.norm2, bw.shift_mlp, bw.scale_mlp, rows, 1e-6)
+    hidden = torch.zeros((m, bw.fc1.shape[0]), dtype=torch.bfloat16, device=dev)
+    hidden[w] = ref_gpu.int8(q[w].contiguous(), bw.fc1, qs.view(-1)[w].contiguous(), bw.fc1_s)
+    hq, hs = ref_gpu.kitchen_quant(hidden, 2)
+    ref_gpu.int8_gate(hq[w], bw.fc2, hs.view(-1)[w], bw.fc2_s, bw.gate_mlp, rows[w], x[w], out=x[w])
+    return x
+
+
+@pytest.mark.parametrize("skip", [0, 256])
+def test_runtime_block_with_int8_attention_equals_reference_chain(device, skip):
+    """Backend.block(attention="int8") -- the reference's whole block, attention
+    included -- at the H3 geometry (hidden 5376, 56 heads, SwiGLU MLP, two adaLN
+    table rows), with and without the last-block window: bit for bit the chain
+    of the reference's own kernels."""
+    from h3_speedkit import synthetic
+    from h3_speedkit.runtime import Backend
+    for name in ("ref_dense.so", "ref_qkv.so", "ref_gather.so", "ref_anchor.so", "ref_fc1.so", "ref_gate.so",
+                 "ref_kitchen.so", "ref_convrot.so", "ref_norm_k5376.so"):
+        if not ref_gpu.available(name):
+            pytest.fail(f"oracle/_ref/{name} is missing: build it with oracle/build.py")
+    m = 512
+    bw = synthetic.h3_block(0, tables=2, device=device)
+    g = torch.Generator(device=device).manual_seed(77)
+    ang = torch.rand((m, 48), generator=g, device=device) * 6.283
+    rope = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).reshape(1, m, 1, 48, 2, 2)
+    rope = rope.to(torch.bfloat16)
+    qw = (torch.rand((128,), generator=g, device=device) + 0.5).to(torch.bfloat16)
+    kw = (torch.rand((128,), generator=g, device=device) + 0.5).to(torch.bfloat16)
+    x0 = synthetic.cfg5_tokens(m, 5376, device=device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    ours = x0.clone()
+    Backend().block(_h3_block_ns(bw, qw, kw), ours, None, None, rope, rows=rows, skip=skip, attention="int8",
+                    mlp_act="swiglu")
+    ref = _reference_block(x0.clone(), bw, qw, kw, rope, rows, skip)
+    torch.cuda.synchronize()
+    assert torch.equal(ours, ref)

@@ -153,7 +153,8 @@ def test_patch_model_installs_on_a_clone_and_rejects_double_install():
     model = FakeModel()
     with patch.dict(sys.modules, _fake_comfy()):
         with pytest.raises(Unsupported, match="attention provider"):
-            runtime.patch_model(model)
+            runtime.patch_model(model, attention=None)
+        assert runtime.patch_model(model, backend=object())._h3_speedkit.attention == "int8"
         fast = runtime.patch_model(model, attention=lambda q, k, v: v, backend=object())
         assert model.model_options == {"transformer_options": {"keep": "original"}}
         options = fast.model_options["transformer_options"]

@@ -64,10 +64,11 @@ def parse_args():
                     help="block geometry of the stack: cfg5 (default) or the H3 model's own (SwiGLU)")
     ap.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=5,
                     help="5 (default): the 8-block stack; 1-4: the single-op BASELINE configs on one GPU")
-    ap.add_argument("--op", choices=("qkv", "attention"), default=None,
+    ap.add_argument("--op", choices=("qkv", "attention", "block"), default=None,
                     help="qkv: the QKV op (projection -> pre-quantised attention operands) at the H3 "
                          "geometry on one GPU, --tokens rows; attention: the INT8 attention on those "
-                         "operands (56 heads, one sequence of --attn-tokens tokens)")
+                         "operands (56 heads, one sequence of --attn-tokens tokens); block: one whole H3 "
+                         "block with its INT8 attention through runtime.Backend.block (--attn-tokens tokens)")
     ap.add_argument("--attn-tokens", type=int, default=32768,
                     help="sequence length of the --op attention line (default 32768)")
     ap.add_argument("--attn-heads", type=int, default=56,
@@ -894,6 +895,128 @@ def run_attention(args):
     return 0
 
 
+def _block_inputs(m: int, dev):
+    """One H3-geometry block (hidden 5376, 56 heads, SwiGLU, two adaLN table rows)
+    with seeded synthetic weights, RoPE table, Q/K norm weights and tokens."""
+    import torch
+    from h3_speedkit import synthetic
+    bw = synthetic.h3_block(0, tables=2, device=dev)
+    g = torch.Generator(device=dev).manual_seed(77)
+    ang = torch.rand((m, 48), generator=g, device=dev) * 6.283
+    rope = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).reshape(1, m, 1, 48, 2, 2)
+    qw = (torch.rand((128,), generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    kw = (torch.rand((128,), generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    x = synthetic.cfg5_tokens(m, 5376, device=dev)
+    rows = (torch.arange(m, device=dev) % 2).to(torch.int32)
+    return bw, rope.to(torch.bfloat16), qw, kw, x, rows
+
+
+def _block_ns(bw, qw, kw):
+    from types import SimpleNamespace as NS
+
+    def linear(w, s):
+        return NS(weight=w, weight_int8=w, weight_scale=s)
+    return NS(adaln_proj=lambda t: (bw.shift_msa, bw.scale_msa, bw.gate_msa, bw.shift_mlp, bw.scale_mlp,
+                                    bw.gate_mlp),
+              norm1=NS(weight=bw.norm1, eps=1e-6), norm2=NS(weight=bw.norm2, eps=1e-6),
+              attn=NS(qkv_proj=linear(bw.qkv, bw.qkv_s), out_proj=linear(bw.out, bw.out_s),
+                      q_norm=NS(weight=qw, eps=1e-6), k_norm=NS(weight=kw, eps=1e-6)),
+              mlp=NS(fc1=linear(bw.fc1, bw.fc1_s), fc2=linear(bw.fc2, bw.fc2_s)))
+
+
+def run_block(args):
+    """One whole H3 block (hidden 5376, 56 heads x 128 INT8 attention, SwiGLU MLP
+    of width 14336) on --attn-tokens tokens, through runtime.Backend.block with
+    attention="int8": prologue, QKV op, INT8 attention, ConvRot, outproj, prologue,
+    FC1, SwiGLU quantiser, FC2 -- the reference's runtime.py:126-164.  Median of
+    `--steps` blocks after `--warmup` (tokens updated in place, as in the model).
+    `--impl reference` times the same block as the chain of the reference's own
+    kernels compiled from its sources (its prologue, gather, anchor detector,
+    r84_kfourwarp.cu, dense_ring.cu, register ConvRot, gate.cu, fc1.cu and
+    Kitchen quantiser), with this library's K-only sample projection and V
+    quantiser for the two steps it has no C kernel for."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    import ctypes as ct
+    import torch
+    m = args.attn_tokens
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bw, rope, qw, kw, x, rows = _block_inputs(m, dev)
+    attn_ops = 4.0 * m * m * 128 * 56
+    lin_ops = 2.0 * m * 5376 * (3 * 7168 + 7168 + 2 * 14336 + 14336)
+    cfg = {"workload": f"one H3 block with INT8 attention: hidden 5376, 56 heads x 128, SwiGLU 14336, {m} tokens",
+           "tokens": m, "hidden": 5376, "heads": 56, "ffn": 14336, "l2": "inputs larger than L2",
+           "timing": f"median of {args.steps} blocks"}
+    base = {"metric": "H3 block tokens/s (INT8 attention included)", "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg}
+    if args.impl == "reference":
+        from oracle import ref_gpu
+        from h3_speedkit import _lib
+        lib = _lib.load()
+        st = torch.cuda.current_stream().cuda_stream
+        parts = (m + 127) // 128
+
+        def ref_block(_):
+            q, qs = ref_gpu.norm_quant(x, bw.norm1, bw.shift_msa, bw.scale_msa, rows, 1e-6)
+            sq, sx, sr = ref_gpu.sample_gather(q, qs, rope.view(m, 192))
+            sd = torch.empty((3, 56, 9, 128), dtype=torch.bfloat16, device=dev)
+            lib.h3_sample_konly_ex(sq.data_ptr(), bw.qkv.data_ptr(), sx.data_ptr(), bw.qkv_s.data_ptr(),
+                                   sd.data_ptr(), sr.data_ptr(), qw.data_ptr(), kw.data_ptr(), ct.c_float(1e-6),
+                                   9, 56, 5376, None, st)
+            sk = sd[1].contiguous()
+            t = ref_gpu.qkv_quant_kv(q, bw.qkv, qs, bw.qkv_s, rope, qw, kw, 1e-6, sk, ref_gpu.sample_anchor(sk))
+            vi = torch.empty((56 * 128, parts * 128), dtype=torch.int8, device=dev)
+            vs = torch.empty((56 * 128,), dtype=torch.float32, device=dev)
+            lib.h3_quant_v(t["vp"].data_ptr(), t["d"][2].data_ptr(), vi.data_ptr(), vs.data_ptr(),
+                           torch.empty_like(vs).data_ptr(), m, 56, st)
+            o = ref_gpu.dense(t["qi"].view(1, 56, m, 128), t["ki"].view(1, 56, m, 128), vi,
+                              t["qs"].view(1, 56, parts * 32), t["ks"].view(1, 56, parts * 4), vs, 128 ** -0.5)
+            aq, asc, _ = ref_gpu.convrot_register(o.transpose(1, 2).reshape(m, 7168), 0)
+            ref_gpu.int8_gate(aq, bw.out, asc.view(-1), bw.out_s, bw.gate_msa, rows, x, out=x)
+            q, qs = ref_gpu.norm_quant(x, bw.norm2, bw.shift_mlp, bw.scale_mlp, rows, 1e-6)
+            h = ref_gpu.int8(q, bw.fc1, qs.view(-1), bw.fc1_s)
+            hq, hs = ref_gpu.kitchen_quant(h, 2)
+            ref_gpu.int8_gate(hq, bw.fc2, hs.view(-1), bw.fc2_s, bw.gate_mlp, rows, x, out=x)
+        ms = _median_ms(ref_block, warmup=max(3, args.warmup), iters=max(3, args.steps))
+        value = m / (ms / 1e3)
+        line = dict(base, value=value, ms_per_step=ms, impl="reference",
+                    cpu_baseline={"value": value, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                                  "sample": "the reference's GPU kernels chained as its runtime.py block"},
+                    e2e={"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return 0
+    from h3_speedkit.runtime import Backend
+    backend = Backend()
+    block = _block_ns(bw, qw, kw)
+
+    def ours(_):
+        backend.block(block, x, None, None, rope, rows=rows, attention="int8", mlp_act="swiglu")
+    clocks = ClockSampler()
+    clocks.start()
+    ms = _median_ms(ours, warmup=max(3, args.warmup), iters=max(3, args.steps))
+    clock = clocks.stop()
+    # end to end: the tokens from pinned host memory and back, around the block
+    x_h = x.cpu().pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+
+    def e2e(_):
+        x.copy_(x_h, non_blocking=True)
+        backend.block(block, x, None, None, rope, rows=rows, attention="int8", mlp_act="swiglu")
+        out_h.copy_(x, non_blocking=True)
+    e2e_ms = _median_ms(e2e, warmup=1, iters=max(3, min(args.steps, 5)))
+    nbytes = x_h.numel() * x_h.element_size()
+    line = dict(base, value=m / (ms / 1e3), ms_per_step=ms, tops=(attn_ops + lin_ops) / (ms / 1e3) / 1e12,
+                ops_split={"attention_tops_per_block": attn_ops / 1e12, "linear_tops_per_block": lin_ops / 1e12},
+                e2e={"value": m / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+                     "d2h_bytes_per_step": nbytes},
+                cpu_baseline=None, cpu_baseline_note="no CPU attention: the arithmetic is the GPU's ex2.approx",
+                clocks=clock, gpu_launches=16)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     global D, ATTN, FFN, SWIGLU
     args = parse_args()
@@ -902,6 +1025,8 @@ def main():
         return run_qkv(args)
     if args.op == "attention":
         return run_attention(args)
+    if args.op == "block":
+        return run_block(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.config != 5:

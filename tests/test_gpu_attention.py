@@ -204,3 +204,25 @@ def test_runtime_block_with_int8_attention_equals_reference_chain(device, skip):
     ref = _reference_block(x0.clone(), bw, qw, kw, rope, rows, skip)
     torch.cuda.synchronize()
     assert torch.equal(ours, ref)
+
+
+@pytest.mark.parametrize("batch,sq,sk,heads,kv_heads", [(2, 300, 700, 4, 2), (3, 129, 129, 2, 2),
+                                                         (2, 640, 128, 2, 1)])
+def test_attention_batches_and_unequal_lengths_equal_reference(device, batch, sq, sk, heads, kv_heads):
+    """Batch > 1 and query length != key length (the ABI's separate qo_len /
+    kv_len and batch strides): the same bits as the reference kernel."""
+    _need()
+    g = torch.Generator().manual_seed(batch * 1000 + sq + sk)
+    pq, pk = (sq + 127) // 128, (sk + 127) // 128
+    q = torch.randint(-127, 128, (batch, heads, sq, 128), generator=g, dtype=torch.int8)
+    k = torch.randint(-127, 128, (batch, kv_heads, sk, 128), generator=g, dtype=torch.int8)
+    v = torch.randint(-127, 128, (batch * kv_heads * 128, pk * 128), generator=g, dtype=torch.int8)
+    qs = torch.rand((batch, heads, pq * 32), generator=g) * 0.02 + 0.001
+    ks = torch.rand((batch, kv_heads, pk * 4), generator=g) * 0.02 + 0.001
+    vs = torch.rand((batch * kv_heads * 128,), generator=g) * 0.01 + 0.0005
+    packed = PrequantizedInt8Attention(
+        q=q.to(device), k=k.to(device), v=v.to(device), q_scale=qs.to(device), k_scale=ks.to(device),
+        v_scale=vs.to(device), original_head_dim=128, input_dtype=torch.bfloat16, attention_scale=128 ** -0.5,
+        cta_k=128, attn_mask=None)
+    for layout in ("bshd", "bhsd"):
+        _compare(packed, layout)

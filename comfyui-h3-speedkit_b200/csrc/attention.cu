@@ -4,6 +4,7 @@
 // for SM120).  Same C ABI (H3DenseArgs, h3_dense_*), same arithmetic, written
 // for tcgen05: S = Q K^T and O_blk = P V run as kind::i8 MMAs with int32
 // accumulators in TMEM, and one thread owns one query row for the softmax.
+// Operand layouts are the reference's; the int32 -> float conversions are exact.
 //
 // Operands (one batch, any head count; qo_heads % kv_heads == 0):
 //   Q  INT8 [B, Hq, Sq, 128], one FP32 scale per 4 rows {32b + s + 8j} of a
@@ -15,7 +16,8 @@
 //   O  BF16, BHSD or BSHD strides.
 //
 // Arithmetic, per query row and 128-key block j (the reference's, exactly):
-//   s = int32 Q.K (exact; float(s) is exact, |s| < 2^22);
+//   s = int32 Q.K (exact; float(s) is exact, |s| < 2^22);  (all int32 accumulators
+//   start at zero: the first K=32 step of each MMA overwrites its slot)
 //   per key class t: scale_t = (sm_scale * log2e) * (q_scale * k_scale[j][t]);
 //   m_t = fmaf(max_t(s), scale_t, -7.9943534), tile_m = max_t m_t,
 //   m = max(m_prev, tile_m), r = ex2(-|m_prev - tile_m|),
@@ -36,14 +38,21 @@
 // every FP32 operation has the reference's operands in the reference's order.
 // The unit is compiled with --use_fast_math, like the reference's dense unit.
 //
-// Roles: warp 0 TMA producer (Q once, K and V tiles into a 4-stage ring), warp
-// 1 TMEM owner and MMA issuer, warps 2-5 the correction (one thread per query
-// row: each block's P.V joins O, then the normalised output), and 4 x kParts
-// softmax warps (kParts threads per query row, each with kKeys / kParts of the
-// keys).  S is double-buffered in TMEM and the block's P.V joins O one block
-// late, so the tensor core and the correction warps work under the softmax.
-// Every mbarrier wait is bounded (2 s) and reports a status code instead of
-// hanging.
+// Roles (20 warps, five warpgroups):
+//   * warpgroup 0: warp 0 the TMA producer (lane 0: Q once and the K ring, lane
+//     1: the V ring, both 4 stages), warp 1 the TMEM owner and the MMA issuers
+//     (lane 0: S(j) into TMEM slot j % 4; lane 1: P.V(j) into the same slot
+//     once P(j) is written), warps 2-3 idle;
+//   * warpgroups 1-2: 8 correction warps, thread = (query row, 64 output
+//     channels) with O in registers: each block's P.V joins O, then the
+//     normalised BF16 output;
+//   * warpgroups 3-4: 8 softmax warps, two per TMEM lane quadrant taking
+//     alternate blocks, thread = query row; a short chain step per block
+//     carries the running maximum and the four class denominators from block
+//     to block in the reference's order.
+// setmaxnreg moves registers from warpgroup 0 to the others.  The four TMEM
+// slots let S run up to four blocks ahead of the softmax.  Every mbarrier wait
+// is bounded (2 s) and reports a status code instead of hanging.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -538,9 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float kn[4];                              // the K scales of this warp's next block
 #pragma unroll
     for (int t = 0; t < 4; ++t) kn[t] = sub < nblk ? __ldg(kscale + sub * 4 + t) : 0.0f;
-    // The odd-block warps start once P(0) is written: the two warps of a
-    // quadrant then run half a round apart, so that one's exp2 stream overlaps
-    // the other's maxima and chain step (the chain's order keeps the offset).
+    // The odd-block warps start once P(0) is written, which staggers the two
+    // warps' first exp2 streams (measured a few per cent faster).
     if (sub == 1 && nblk > 1 && !warp_wait(&sm.p_full[0], 0, sm, a.status, 60)) return_early = true;
     for (int j = sub; !return_early && j < nblk; j += 2) {
       const bool last = j == nblk - 1;

@@ -496,13 +496,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pv[32];
         tmem_load_32cols(t_pv + 32 * g, pv);
         tmem_load_wait();
+        if (g == 1) {
+          // every P.V value of the slot is in registers: release it for S(j + 4)
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.slot_free[slot]);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           o2[16 * g + i] = fma2(pkf(float(int(pv[2 * i])), float(int(pv[2 * i + 1]))), ts2, o2[16 * g + i]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.slot_free[slot]);
     }
     // O = (O / d) * v_scale in BF16
     if (ok && warp_wait(&sm.inv_full, 0, sm, a.status, 73) && row < a.q_len) {

@@ -404,13 +404,13 @@ def run_ours(args):
     gemms = {k: v for k, v in per_kernel.items() if k in gemm_ops}
     dominant = max(gemms, key=lambda k: gemms[k]["total_ms"])
     achieved = gemm_ops[dominant] / (gemms[dominant]["avg_ms"] / 1e3) / 1e12
-    traffic = None
+    # DRAM bytes per launch from the committed ncu capture (per row, scaled by
+    # this launch's rows); captured at the cfg5 geometry only
+    traffic_rows = {}
     tfile = ROOT / "profiles" / "traffic.json"
-    if tfile.exists() and args.geometry == "cfg5":   # captured at the cfg5 geometry
-        tdata = json.loads(tfile.read_text())
-        entry = tdata.get(dominant)
-        if entry:
-            traffic = entry["bytes_per_row"] * m_local
+    if tfile.exists() and args.geometry == "cfg5":
+        traffic_rows = {k: v["bytes_per_row"] for k, v in json.loads(tfile.read_text())["kernels"].items()}
+    traffic = traffic_rows[dominant] * m_local if dominant in traffic_rows else None
     step_total = sum(v["total_ms"] for v in per_kernel.values())
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM))
     pro = per_kernel.get("prologue")
@@ -420,7 +420,8 @@ def run_ours(args):
         pro_gbs = pro_bytes / (pro["avg_ms"] / 1e3) / 1e9
         prologue_line = {"bound": "hbm", "kernel": "norm_quant_stream (staged tables)", "achieved": pro_gbs,
                          "peak": hbm_peak,
-                         "unit": "GB/s", "frac": pro_gbs / hbm_peak, "bytes_per_launch": pro_bytes}
+                         "unit": "GB/s", "frac": pro_gbs / hbm_peak, "bytes_per_launch": pro_bytes,
+                         "traffic": traffic_rows["prologue"] * m_local if "prologue" in traffic_rows else None}
     value = args.tokens * args.steps / elapsed
     total_ops = args.tokens * block_ops() * args.blocks
     line = {

@@ -263,6 +263,29 @@ cudaError_t launch(const void* x, int64_t xs, void* q, void* scale, void* rotate
   return cudaGetLastError();
 }
 
+// The quantiser's last step for rows whose ConvRot256 ran elsewhere (the FC1
+// epilogue of h3_int8_gelu_rot): the row scale from the row's max |rotated value|
+// and the codes of the rotated values, already rounded to BF16 (the code rounds
+// each value to BF16 first, so nothing is lost).  One CTA per row, 16 values per
+// thread and step: two 16-byte streaming loads, one 16-byte store.
+__global__ void __launch_bounds__(256) codes_from_rotated(const __nv_bfloat16* __restrict__ v, int64_t vs,
+                                                          const uint32_t* __restrict__ rowmax, int8_t* __restrict__ q,
+                                                          float* __restrict__ scale, int k) {
+  const int64_t row = blockIdx.x;
+  const float s = int8_row_scale(__uint_as_float(__ldg(rowmax + row)));
+  if (threadIdx.x == 0) scale[row] = s;
+  const float scale_bf = __bfloat162float(__float2bfloat16_rn(s));
+  const uint4* src = reinterpret_cast<const uint4*>(v + row * vs);
+  uint4* dst = reinterpret_cast<uint4*>(q + row * int64_t(k));
+  for (int j = threadIdx.x; j < k / 16; j += blockDim.x) {
+    const uint4 a = __ldcs(src + 2 * j), b = __ldcs(src + 2 * j + 1);
+    dst[j] = make_uint4(rq::codes4(rq::bf2_to_f2(a.x), rq::bf2_to_f2(a.y), scale_bf),
+                        rq::codes4(rq::bf2_to_f2(a.z), rq::bf2_to_f2(a.w), scale_bf),
+                        rq::codes4(rq::bf2_to_f2(b.x), rq::bf2_to_f2(b.y), scale_bf),
+                        rq::codes4(rq::bf2_to_f2(b.z), rq::bf2_to_f2(b.w), scale_bf));
+  }
+}
+
 }  // namespace
 
 // Shared with the GEMM translation unit (requantisation of a gate-residual output).
@@ -317,6 +340,18 @@ H3SK_EXPORT int h3_convrot_register_run(const void* x, void* q, void* scale, voi
   if (mode == 0) return launch<kActNone, kModeQuant>(x, k, q, scale, nullptr, rows, k, stream);
   if (mode == 1) return launch<kActNone, kModeDiag>(x, k, q, scale, rotated, rows, k, stream);
   return launch<kActNone, kModeRotate>(x, k, nullptr, nullptr, rotated, rows, k, stream);
+}
+
+H3SK_EXPORT int h3_convrot_codes(const void* v, int64_t vs, const void* rowmax, void* q, void* scale, int64_t rows,
+                                 int k, uintptr_t stream_ptr) {
+  using namespace h3sk;
+  if (!v || !rowmax || !q || !scale || rows < 1 || rows > INT32_MAX || !valid_k(k) || vs < k || (vs % 8) ||
+      (uintptr_t(v) & 15u) || (uintptr_t(q) & 15u) || (uintptr_t(rowmax) & 3u) || (uintptr_t(scale) & 3u))
+    return cudaErrorInvalidValue;
+  codes_from_rotated<<<unsigned(rows), 256, 0, reinterpret_cast<cudaStream_t>(stream_ptr)>>>(
+      static_cast<const __nv_bfloat16*>(v), vs, static_cast<const uint32_t*>(rowmax), static_cast<int8_t*>(q),
+      static_cast<float*>(scale), k);
+  return cudaGetLastError();
 }
 
 H3SK_EXPORT int h3_convrot_quant_act(const void* x, int64_t xs, void* q, void* scale, int64_t rows, int k,

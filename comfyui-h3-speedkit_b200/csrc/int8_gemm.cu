@@ -99,7 +99,7 @@ constexpr int64_t kBSliceBytes = int64_t(H3SK_BSLICE_MB) << 20;
 constexpr int64_t kDualBSliceBytes = int64_t(H3SK_DUAL_BSLICE_MB) << 20;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
-enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads = 4, kEpiKinds = 5 };
+enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads = 4, kEpiGeluRot = 5, kEpiKinds = 6 };
 
 // Tile geometry of the two kernel shapes.
 //   single CTA: a 128 x 256 tile per CTA, B tile 256 rows, 4 stages of 48 KB;
@@ -123,7 +123,6 @@ struct Shape {
   static constexpr int stages = kPair ? (kDual ? H3SK_DUAL_STAGES : H3SK_PAIR_STAGES) : 4;
   static constexpr int stage_bufs = (kPair && !kDual) ? H3SK_STAGE_BUFS : 1;   // output staging buffers per warp
   static constexpr uint32_t idesc = idesc_i8(kBM * pair, kBN);
-  static constexpr uint32_t tempty_count = kPair ? 2 * kEpilogueWarps : kEpilogueWarps;
 };
 
 template <bool kPair, bool kDual = false>
@@ -164,6 +163,7 @@ struct GemmParams {
   int group_n;                    // N units per weight-stationary group
   int head_major;                 // 1: D is [N/128, M, 128] (one plane per 128 columns)
   HeadsArgs hd;                   // kEpiHeads only
+  uint32_t* rowmax;               // kEpiGeluRot only: [M] bits of max |rotated value|, zeroed by the host
   int* status;
   uint64_t timeout_ns;
 };
@@ -247,7 +247,7 @@ __device__ __forceinline__ uint32_t gelu_bf2(uint32_t w) {
   return pack_bf2(g);
 }
 
-// Named barrier among the four epilogue warps only.
+// Named barrier among the eight epilogue warps only.
 __device__ __forceinline__ void epilogue_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
 }
@@ -255,6 +255,115 @@ __device__ __forceinline__ void epilogue_sync() {
 // Named barrier among the four epilogue warps of one column half (one head).
 __device__ __forceinline__ void half_sync(int half) {
   asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
+}
+// Named barrier between the two epilogue warps of one TMEM lane quarter (the two
+// column halves of the same 32 rows).
+__device__ __forceinline__ void quarter_sync(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(4 + quarter) : "memory");
+}
+
+// ---- ConvRot256 of a tile row (the FC2-input quantiser's rotation) -------------
+// The quantiser's arithmetic (kernels/convrot/vendor/convrot64_exact.cuh:202-234,
+// 664-677): four radix-4 stages over index bit pairs (0,1), (2,3), (4,5), (6,7);
+// every stage output is 0.5 * h4_d(x0, x1, x2, x3) with the additions left to
+// right, d=0: ((x0+x1)+x2)-x3, d=1: ((x0+x1)-x2)+x3, d=2: ((x0-x1)+x2)+x3,
+// d=3: ((-x0+x1)+x2)+x3, all flushing subnormals (the reference builds its
+// quantiser with --use_fast_math).  This unit is built without fast math, so
+// every operation is written with its .ftz form.  0.5*RN(t +- x3) is computed as
+// fma(t, 0.5, +-0.5*x3) (exact scaling by 0.5 commutes with the rounding) and
+// (-x0+x1)+x2 as x2-(x0-x1) (the same rounded value).
+__device__ __forceinline__ float z_add(float a, float b) {
+  float c;
+  asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(c) : "f"(a), "f"(b));
+  return c;
+}
+__device__ __forceinline__ float z_sub(float a, float b) {
+  float c;
+  asm("sub.rn.ftz.f32 %0, %1, %2;" : "=f"(c) : "f"(a), "f"(b));
+  return c;
+}
+__device__ __forceinline__ float z_mul(float a, float b) {
+  float c;
+  asm("mul.rn.ftz.f32 %0, %1, %2;" : "=f"(c) : "f"(a), "f"(b));
+  return c;
+}
+__device__ __forceinline__ float z_fma(float a, float b, float c) {
+  float d;
+  asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t z2_add(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t z2_sub(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t z2_mul(uint64_t a, uint64_t b) {
+  uint64_t c;
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  return c;
+}
+__device__ __forceinline__ uint64_t z2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// Stage over index bits 0,1 of 64 consecutive values held as 32 pairs (value 2i
+// in the low half of v[i]): quads of consecutive values.
+__device__ __forceinline__ void rot_stage01(uint64_t (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float x0 = p2_lo(v[2 * j]), x1 = p2_hi(v[2 * j]);
+    const float x2 = p2_lo(v[2 * j + 1]), x3 = p2_hi(v[2 * j + 1]);
+    const float a = z_add(x0, x1), b = z_sub(x0, x1);
+    const float h = z_mul(0.5f, x3);
+    const float t0 = z_add(a, x2), t1 = z_sub(a, x2), t2 = z_add(b, x2), t3 = z_sub(x2, b);
+    v[2 * j] = p2(z_fma(t0, 0.5f, -h), z_fma(t1, 0.5f, h));
+    v[2 * j + 1] = p2(z_fma(t2, 0.5f, h), z_fma(t3, 0.5f, h));
+  }
+}
+// Stage over the two index bits held at pair strides S and 2S: quads
+// {P, P+S, P+2S, P+3S} of pairs, for every P with those bits clear.
+template <int S>
+__device__ __forceinline__ void rot_stage_pairs(uint64_t (&v)[32]) {
+  const uint64_t half = p2(0.5f, 0.5f), nhalf = p2(-0.5f, -0.5f);
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    if ((q / S) & 3) continue;
+    const uint64_t x0 = v[q], x1 = v[q + S], x2 = v[q + 2 * S], x3 = v[q + 3 * S];
+    const uint64_t a = z2_add(x0, x1), b = z2_sub(x0, x1);
+    const uint64_t h = z2_mul(x3, half), nh = z2_mul(x3, nhalf);
+    const uint64_t t0 = z2_add(a, x2), t1 = z2_sub(a, x2), t2 = z2_add(b, x2), t3 = z2_sub(x2, b);
+    v[q] = z2_fma(t0, half, nh);
+    v[q + S] = z2_fma(t1, half, h);
+    v[q + 2 * S] = z2_fma(t2, half, h);
+    v[q + 3 * S] = z2_fma(t3, half, h);
+  }
+}
+__device__ __forceinline__ void tmem_store_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_load_16cols(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
 }
 __device__ __forceinline__ uint32_t warp_max_u32(uint32_t x) {
   uint32_t r;
@@ -403,7 +512,7 @@ __device__ __forceinline__ void store_chunk_acc(const GemmParams& p, const uint3
 // Column scales and bias come from shared memory as 16-byte broadcasts.  The
 // dequant and the gate FMA stay scalar: packed f32x2 forms of them were measured
 // to differ from the scalar IEEE operations on rare inputs.
-template <int kEpi>
+template <int kEpi, bool kAddBias = true>
 __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t (&r)[32], bool row_ok, int row,
                                              int col0, int c, float xs_row, const __nv_bfloat16* gate_row,
                                              const float* col_ws, const float* col_bias, uint32_t (&packed)[16]) {
@@ -415,8 +524,10 @@ __device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t
     const float w[4] = {w4.x, w4.y, w4.z, w4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
     float y[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h)
-      y[h] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(int(r[4 * q + h])), xs_row), w[h]), b[h]);
+    for (int h = 0; h < 4; ++h) {
+      const float prod = __fmul_rn(__fmul_rn(__int2float_rn(int(r[4 * q + h])), xs_row), w[h]);
+      y[h] = kAddBias ? __fadd_rn(prod, b[h]) : prod;
+    }
     packed[2 * q] = pack_bf2(y[0], y[1]);
     packed[2 * q + 1] = pack_bf2(y[2], y[3]);
   }
@@ -460,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
   using S = Shape<kPair, kDual>;
   using L = SmemLayout<kPair, kDual>;
+  constexpr uint32_t kTemptyCount = (kPair ? 2 : 1) * kEpilogueWarps;   // each epilogue warp of each CTA releases
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem + L::a;
@@ -489,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], S::tempty_count);
+      mbar_init(&tempty[a], kTemptyCount);
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -859,6 +971,105 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   codes4_rni(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15], inv));
           }
         }
+      } else if constexpr (kEpi == kEpiGeluRot) {
+        // ---- FC1 + GELU + the FC2-input quantiser's ConvRot256 ----
+        // The tile's 256 columns are one rotation group of each of its rows; the
+        // two warps of a lane quarter take the two column halves of its 32 rows.
+        // (Four warps per quarter, 18 per CTA, measured slower: 5.9 vs 5.5 ms.)
+        constexpr int kBlocks = 2;                  // 64-column blocks per warp in pass 1
+        constexpr int kRuns = 2;                    // 16-position runs per warp in pass 2
+        const int slice = half;
+        // Pass 1: this warp's 64-column blocks: the GELU values rounded to BF16
+        // (as the unfused FC1 stores them), widened, the stages over index bits
+        // (0,1), (2,3), (4,5), written back over the accumulator columns as FP32.
+#pragma unroll 1
+        for (int b = 0; b < kBlocks; ++b) {
+          const int blk = kBlocks * slice + b;
+          uint64_t v[32];
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * blk + cc;
+            uint32_t r[32];
+            __syncwarp();
+            tmem_load_32cols(t_row + uint32_t(c * 32), r);
+            tmem_load_wait();
+            // Without a bias the + 0 is left out: it only turns -0 into +0, and
+            // the sign of a zero reaches neither a code nor the row maximum.
+            uint32_t packed[16];
+            if (p.bias != nullptr)
+              chunk_values<kEpiGelu, true>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws, col_bias,
+                                           packed);
+            else
+              chunk_values<kEpiGelu, false>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws, col_bias,
+                                            packed);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[16 * cc + i] = p2_from_bf2(packed[i]);
+          }
+          rot_stage01(v);
+          rot_stage_pairs<2>(v);
+          rot_stage_pairs<8>(v);
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t w[32];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              w[2 * i] = uint32_t(v[16 * cc + i]);
+              w[2 * i + 1] = uint32_t(v[16 * cc + i] >> 32);
+            }
+            __syncwarp();
+            tmem_store_32cols(t_row + uint32_t((2 * blk + cc) * 32), w);
+          }
+        }
+        tmem_store_wait();
+        tc_fence_before();
+        quarter_sync(quarter);   // both column halves of these 32 rows are in TMEM
+        tc_fence_after();
+        // Pass 2: the stage over index bits (6,7) for this warp's positions c of
+        // each 64-column block: the four values c + 64 k.
+        // The outputs of positions [32 half, 32 half + 32) of block k are one
+        // 32-column chunk: the first run's words wait in registers for the second.
+        float mx = 0.0f;
+        uint32_t first[4][8];
+#pragma unroll
+        for (int cc = 0; cc < kRuns; ++cc) {
+          const int c0 = 16 * (kRuns * slice + cc);
+          uint64_t v[32];   // pair 8 k + i: positions c0 + 64 k + 2 i, + 1
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint32_t u[16];
+            __syncwarp();
+            tmem_load_16cols(t_row + uint32_t(c0 + 64 * k), u);
+            tmem_load_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * k + i] = p2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+          }
+          if (cc == kRuns - 1) release();   // every TMEM read of this accumulator is done
+          rot_stage_pairs<8>(v);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p2_lo(v[i])), fabsf(p2_hi(v[i]))),
+                                 fmaxf(fabsf(p2_lo(v[i + 1])), fabsf(p2_hi(v[i + 1])))));
+          if (cc == 0) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) first[k][i] = pack_bf2(v[8 * k + i]);
+          } else if (row_base < p.m) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                packed[i] = first[k][i];
+                packed[8 + i] = pack_bf2(v[8 * k + i]);
+              }
+              store_chunk(n0 + 32 * slice + 64 * k, packed);
+            }
+          }
+        }
+        // max |rotated value| of the row: non-negative and never NaN (fmaxf drops
+        // NaN), so its bits order as unsigned integers
+        if (row_ok) atomicMax(p.rowmax + row, __float_as_uint(mx));
       } else if constexpr (H3SK_TMEM_PREFETCH == 1 || (H3SK_TMEM_PREFETCH == 2 && kDual)) {
         // chunk c + 1's TMEM load is in flight while chunk c is computed
         uint32_t r[32];
@@ -1112,7 +1323,8 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 
 int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
              void* D, int64_t ldd, const void* gate, const int32_t* rows, const void* residual, int M, int N,
-             int K, cudaStream_t stream, bool heads = false, const HeadsArgs* hd = nullptr) {
+             int K, cudaStream_t stream, bool heads = false, const HeadsArgs* hd = nullptr,
+             uint32_t* rowmax = nullptr) {
   if (!A || !B || !D || M < 1 || N < 1 || K < 16 || K % 16 || N % 8 || ldd < N || ldd % 8)
     return fail(cudaErrorInvalidValue, "h3_int8: invalid shape or null operand");
   if (heads && ((epi != kEpiDequant && epi != kEpiHeads) || N % 128))
@@ -1120,6 +1332,8 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   if (epi == kEpiHeads && (!heads || !hd || hd->heads < 2 || hd->heads % 2 || N != 3 * hd->heads * 128 ||
                            !hd->freqs || !hd->qw || !hd->kw))
     return fail(cudaErrorInvalidValue, "h3_qkv: the fused head epilogue needs an even head count and N = 3*heads*128");
+  if (epi == kEpiGeluRot && (heads || !rowmax || (uintptr_t(rowmax) & 3u) || N % kBN))
+    return fail(cudaErrorInvalidValue, "h3_int8_gelu_rot: needs rowmax and N % 256 == 0");
   if ((uintptr_t(A) & 15u) || (uintptr_t(B) & 15u) || (uintptr_t(D) & 15u))
     return fail(cudaErrorInvalidValue, "h3_int8: A, B and D must be 16-byte aligned");
   if (epi != kEpiAcc && (!xs || !ws || (uintptr_t(xs) & 3u) || (uintptr_t(ws) & 3u)))
@@ -1155,6 +1369,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.k = K;
   p.head_major = heads ? 1 : 0;
   if (hd) p.hd = *hd;
+  p.rowmax = rowmax;
   p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
@@ -1165,7 +1380,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return fail(cudaErrorInvalidDevice, "h3_int8: no device");
   const int approx_pairs = device_info(device).sms / 2;
-  const bool dual = pair && epi != kEpiHeads && K >= kDualMinK && p.n_tiles % 2 == 0 &&
+  const bool dual = pair && epi != kEpiHeads && epi != kEpiGeluRot && K >= kDualMinK && p.n_tiles % 2 == 0 &&
                     int64_t(p.m_tiles) * (p.n_tiles / 2) >= int64_t(kDualMinWaves) * approx_pairs;
   const int dual_n = dual ? 2 : 1;
   p.n_units = p.n_tiles / dual_n;
@@ -1177,6 +1392,10 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   }
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
+  if (epi == kEpiGeluRot) {   // the row maxima accumulate from zero (after every check above)
+    e = cudaMemsetAsync(rowmax, 0, size_t(M) * sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return fail(e, "h3_int8_gelu_rot: row maxima reset failed");
+  }
   if (dual) {
     switch (epi) {
       case kEpiDequant: e = launch_gemm<kEpiDequant, true, true>(ma, mb, md, p, stream); break;
@@ -1190,6 +1409,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiGelu: e = launch_gemm<kEpiGelu, true>(ma, mb, md, p, stream); break;
       case kEpiGate: e = launch_gemm<kEpiGate, true>(ma, mb, md, p, stream); break;
       case kEpiHeads: e = launch_gemm<kEpiHeads, true>(ma, mb, md, p, stream); break;
+      case kEpiGeluRot: e = launch_gemm<kEpiGeluRot, true>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, true>(ma, mb, md, p, stream); break;
     }
   } else {
@@ -1198,6 +1418,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiGelu: e = launch_gemm<kEpiGelu, false>(ma, mb, md, p, stream); break;
       case kEpiGate: e = launch_gemm<kEpiGate, false>(ma, mb, md, p, stream); break;
       case kEpiHeads: e = launch_gemm<kEpiHeads, false>(ma, mb, md, p, stream); break;
+      case kEpiGeluRot: e = launch_gemm<kEpiGeluRot, false>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, false>(ma, mb, md, p, stream); break;
     }
   }
@@ -1255,6 +1476,13 @@ H3SK_EXPORT int h3_int8_ex(const int8_t* A, const int8_t* B, const float* xs, co
   if (epilogue == H3_EPI_ACC_INT32 && (ldd % 4)) return h3sk::fail(cudaErrorInvalidValue, "h3_int8_ex: ldd");
   return h3sk::run_gemm(epilogue, A, B, xs, ws, bias, D, ldd, nullptr, nullptr, nullptr, M, N, K,
                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+H3SK_EXPORT int h3_int8_gelu_rot(const int8_t* A, const int8_t* B, const float* xs, const float* ws,
+                                 const void* bias, void* V, void* rowmax, int M, int N, int K, int64_t ldv,
+                                 uintptr_t stream) {
+  return h3sk::run_gemm(h3sk::kEpiGeluRot, A, B, xs, ws, bias, V, ldv, nullptr, nullptr, nullptr, M, N, K,
+                        reinterpret_cast<cudaStream_t>(stream), false, nullptr, static_cast<uint32_t*>(rowmax));
 }
 
 H3SK_EXPORT int h3_int8_gate_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws,

@@ -40,10 +40,12 @@ EXPORTS = {
     "h3_convrot_register_query": ([_I, _P, _SZ], _I),
     "h3_convrot_register_run": ([_P] * 4 + [_I64, _I, _I, _SZ], _I),
     "h3_convrot_quant_act": ([_P, _I64, _P, _P, _I64, _I, _I, _SZ], _I),
+    "h3_convrot_codes": ([_P, _I64, _P, _P, _P, _I64, _I, _SZ], _I),
     "h3_int8": ([_P] * 5 + [_I] * 4 + [_SZ], _I),
     "h3_int8_gate": ([_P] * 8 + [_I] * 4 + [_SZ], _I),
     "h3_int8_ex": ([_P] * 6 + [_I] * 3 + [_I64, _I, _SZ], _I),
     "h3_int8_gate_ex": ([_P] * 11 + [_I] * 3 + [_SZ], _I),
+    "h3_int8_gelu_rot": ([_P] * 7 + [_I] * 3 + [_I64, _SZ], _I),
     "h3_int8_last_error": ([], _I),
     "h3_int8_error": ([], ct.c_char_p),
     "h3_qkv_quant_kv": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _SZ], _I),

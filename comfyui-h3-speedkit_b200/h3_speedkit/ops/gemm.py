@@ -61,6 +61,41 @@ def int8_linear(a, w, xs, ws, *, bias=None, gelu=False, out=None):
     return out
 
 
+def int8_linear_gelu_quant(a, w, xs, ws, *, bias=None, rotated=None, rowmax=None, out=None, out_scale=None):
+    """FC1 + GELU straight to the FC2 input: the ConvRot256 + per-token INT8 codes
+    of bf(gelu_tanh(bf(((A.W^T * xs) * ws) + bias))), equal bit for bit to
+    ``quantize_int8_rowwise_convrot64(int8_linear(..., gelu=True))``.  The
+    rotation runs in the GEMM's epilogue (``h3_int8_gelu_rot``), the codes in a
+    light pass over the rotated rows (``h3_convrot_codes``).  ``rotated`` (BF16
+    [M, N]) and ``rowmax`` (int32 [M]) are the scratch between the two.
+    Returns (q INT8 [M, N], scale FP32 [M, 1])."""
+    m, n, k = _check_operands(a, w, xs, ws)
+    if n % 256 or n > 16384:
+        raise ValueError(f'N must be a multiple of 256 up to 16384 (got {n})')
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+        raise ValueError('bias must be contiguous BF16 with N elements')
+    dev = a.device
+    rotated = torch.empty((m, n), dtype=torch.bfloat16, device=dev) if rotated is None else rotated
+    rowmax = torch.empty((m,), dtype=torch.int32, device=dev) if rowmax is None else rowmax
+    q = torch.empty((m, n), dtype=torch.int8, device=dev) if out is None else out
+    s = torch.empty((m, 1), dtype=torch.float32, device=dev) if out_scale is None else out_scale
+    for name, t, dt, shape in (('rotated', rotated, torch.bfloat16, (m, n)), ('rowmax', rowmax, torch.int32, (m,)),
+                               ('out', q, torch.int8, (m, n)), ('out_scale', s, torch.float32, (m, 1))):
+        if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.data_ptr() % 16 or t.device != dev:
+            raise ValueError(f'{name} must be a contiguous, 16-byte aligned {dt} {list(shape)} tensor on {dev}')
+    lib = _lib.load()
+    stream = _stream(a)
+    code = lib.h3_int8_gelu_rot(a.data_ptr(), w.data_ptr(), xs.data_ptr(), ws.data_ptr(),
+                                bias.data_ptr() if bias is not None else None, rotated.data_ptr(),
+                                rowmax.data_ptr(), m, n, k, n, stream)
+    _lib.check_int8(code)
+    code = lib.h3_convrot_codes(rotated.data_ptr(), n, rowmax.data_ptr(), q.data_ptr(), s.data_ptr(), m, n,
+                                stream)
+    if code:
+        raise RuntimeError(f'h3_convrot_codes: CUDA error {code}')
+    return q, s
+
+
 def int8_accumulators(a, w, out=None):
     """Raw int32 accumulators A.W^T (debug epilogue, bit-exact checks)."""
     m, n, k = _check_operands(a, w, None, None)

@@ -10,6 +10,8 @@ SpeedKit, with attention replaced by an identity passthrough of V):
     q, qs   = prologue(x; norm2, shift_mlp, scale_mlp)
     h       = bf(gelu_tanh(bf(dequant(q . Wfc1^T))))            FC1 + GELU epilogue
     hq, hs  = convrot_quant(h)                                  ACT none (GELU already applied)
+              (run as FC1 whose epilogue also rotates each 256-column group of h,
+              then a codes pass over the rotated rows: the same hq, hs bit for bit)
     x       = bf(fmaf(bf(dequant(hq . Wfc2^T)), gate_mlp, x))   FC2 gate-residual, in place
 
 Every op is row-local, so a contiguous token shard gives bit-identical rows on
@@ -213,6 +215,7 @@ class Workspace:
     h: torch.Tensor
     hq: torch.Tensor
     hs: torch.Tensor
+    hmax: torch.Tensor   # int32 [m]: FP32 bits of each row's max |rotated h| (fused FC1 rotation)
 
     @classmethod
     def allocate(cls, m: int, d: int, ffn: int, device, *, attn: int | None = None,
@@ -225,7 +228,8 @@ class Workspace:
                    aq=torch.empty((m, attn), dtype=torch.int8, **e),
                    as_=torch.empty((m, 1), dtype=torch.float32, **e),
                    h=torch.empty((m, fc1_n), dtype=torch.bfloat16, **e),
-                   hq=torch.empty((m, ffn), dtype=torch.int8, **e), hs=torch.empty((m, 1), dtype=torch.float32, **e))
+                   hq=torch.empty((m, ffn), dtype=torch.int8, **e), hs=torch.empty((m, 1), dtype=torch.float32, **e),
+                   hmax=torch.empty((m,), dtype=torch.int32, **e))
 
     @classmethod
     def for_block(cls, m: int, weights: BlockWeights, device) -> "Workspace":
@@ -257,10 +261,17 @@ class BlockPlan:
     With identity attention the V quantiser and the second prologue also start
     at ``skip``: their rows below it feed nothing.  Nothing is allocated when
     the plan runs.
+
+    ``fc1_rotation`` (GELU blocks): FC1's epilogue also runs the FC2-input
+    quantiser's ConvRot256 on each 256-column group and keeps each row's max
+    |rotated value| (``h3_int8_gelu_rot``); a light pass then writes the codes
+    and scales (``h3_convrot_codes``).  Same hq, hs bit for bit as FC1 followed
+    by the quantiser (False), and faster (the rotation runs in the GEMM's
+    epilogue warps while the tensor cores work).
     """
 
     def __init__(self, weights: BlockWeights, x: torch.Tensor, rows: torch.Tensor, ws: Workspace,
-                 eps: float = 1e-6, skip: int = 0):
+                 eps: float = 1e-6, skip: int = 0, fc1_rotation: bool = True):
         self.lib = _lib.load()
         m, d = x.shape
         g = geometry(weights)
@@ -304,10 +315,23 @@ class BlockPlan:
                  (P(x, s), P(w.norm2), P(w.shift_mlp), P(w.scale_mlp), P(rows, s), P(ws.q, s), P(ws.qs, s), None,
                   None, None, n, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0),
                   w.scale_mlp.stride(0), float(eps), tdt, 0)),
-                ("fc1", lib.h3_int8_ex,
-                 (P(ws.q, s), P(w.fc1), P(ws.qs, s), P(w.fc1_s), None, P(ws.h, s), n, n1, d, n1, fc1_epi)),
-                ("quant_h", lib.h3_convrot_quant_act,
-                 (P(ws.h, s), n1, P(ws.hq, s), P(ws.hs, s), n, ffn, mlp_act)),
+            ]
+            if fc1_rotation and not g["swiglu"]:
+                calls += [
+                    ("fc1", lib.h3_int8_gelu_rot,
+                     (P(ws.q, s), P(w.fc1), P(ws.qs, s), P(w.fc1_s), None, P(ws.h, s), P(ws.hmax, s), n, n1, d,
+                      n1)),
+                    ("quant_h", lib.h3_convrot_codes,
+                     (P(ws.h, s), n1, P(ws.hmax, s), P(ws.hq, s), P(ws.hs, s), n, ffn)),
+                ]
+            else:
+                calls += [
+                    ("fc1", lib.h3_int8_ex,
+                     (P(ws.q, s), P(w.fc1), P(ws.qs, s), P(w.fc1_s), None, P(ws.h, s), n, n1, d, n1, fc1_epi)),
+                    ("quant_h", lib.h3_convrot_quant_act,
+                     (P(ws.h, s), n1, P(ws.hq, s), P(ws.hs, s), n, ffn, mlp_act)),
+                ]
+            calls += [
                 ("fc2", lib.h3_int8_gate,
                  (P(ws.hq, s), P(w.fc2), P(ws.hs, s), P(w.fc2_s), P(x, s), P(w.gate_mlp), P(rows, s), P(x, s), n, d,
                   ffn, 13)),
@@ -348,15 +372,17 @@ class LocalStack:
     """All blocks over one contiguous shard of tokens, on the current device."""
 
     def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6,
-                 ws: Workspace | None = None, skip: int = 0):
+                 ws: Workspace | None = None, skip: int = 0, fc1_rotation: bool = True):
         """``skip``: the last block's row window (rows [0, skip) of this shard keep
-        the residual the previous blocks left; see BlockPlan)."""
+        the residual the previous blocks left; see BlockPlan).  ``fc1_rotation``:
+        see BlockPlan."""
         m, d = x.shape
         self.x, self.rows = x, rows
         if ws is not None and ws.q.shape[0] < m:
             raise ValueError("shared workspace too small for this shard")
         self.ws = ws if ws is not None else Workspace.for_block(m, blocks[0], x.device)
-        self.plans = [BlockPlan(b, x, rows, self.ws, eps, skip=skip if i == len(blocks) - 1 else 0)
+        self.plans = [BlockPlan(b, x, rows, self.ws, eps, skip=skip if i == len(blocks) - 1 else 0,
+                                fc1_rotation=fc1_rotation)
                       for i, b in enumerate(blocks)]
         self.graph = None
 

@@ -164,6 +164,22 @@ def test_last_block_row_window(device, skip):
     assert stack.launches_per_step == 8 * 3 - (6 if skip == m else 0)
 
 
+@pytest.mark.parametrize("skip", [0, 300])
+def test_fc1_rotation_plan_equals_unfused_plan(device, skip):
+    """FC1 with the FC2-input quantiser's rotation in its epilogue plus the codes
+    pass (the default plan) against FC1 then the quantiser: the same stack output
+    bit for bit, with and without a last-block row window."""
+    m = 1000
+    blocks = _blocks(2, device)
+    x0 = synthetic.cfg5_tokens(m, D).to(device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    fused, unfused = x0.clone(), x0.clone()
+    LocalStack(blocks, fused, rows, skip=skip).run()
+    LocalStack(blocks, unfused, rows, skip=skip, fc1_rotation=False).run()
+    torch.cuda.synchronize()
+    assert torch.equal(fused, unfused)
+
+
 def test_last_block_row_window_matches_cpu_restatement(device):
     m, skip = 384, 128
     blocks = _blocks(2, device)

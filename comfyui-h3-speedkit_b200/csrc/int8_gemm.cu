@@ -112,7 +112,7 @@ enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads
 //   stage holds the A tile and both B halves (48 KB, 4 stages), the leader
 //   issues the A stage against both and accumulates into both TMEM
 //   accumulators, so A is written into shared memory once per two tiles.
-template <bool kPair, bool kDual = false>
+template <bool kPair, bool kDual = false, bool kRot = false>
 struct Shape {
   static constexpr int pair = kPair ? 2 : 1;
   static constexpr int dual_n = kDual ? 2 : 1;             // N-tiles per work unit
@@ -120,14 +120,17 @@ struct Shape {
   static constexpr int b_rows = kPair ? kBN / 2 : kBN;    // B rows loaded per CTA
   static constexpr int b_tile_bytes = b_rows * kBK;
   static constexpr int stage_bytes = kATileBytes + dual_n * b_tile_bytes;
-  static constexpr int stages = kPair ? (kDual ? H3SK_DUAL_STAGES : H3SK_PAIR_STAGES) : 4;
-  static constexpr int stage_bufs = (kPair && !kDual) ? H3SK_STAGE_BUFS : 1;   // output staging buffers per warp
+  // The rotating FC1 epilogue stores four chunks back to back at the end of a
+  // tile: its CTA pairs trade an operand stage for a second staging buffer.
+  static constexpr int stages =
+      kPair ? (kDual ? H3SK_DUAL_STAGES : (kRot ? H3SK_PAIR_STAGES - 1 : H3SK_PAIR_STAGES)) : 4;
+  static constexpr int stage_bufs = (kPair && !kDual) ? (kRot ? 2 : H3SK_STAGE_BUFS) : 1;   // output staging buffers per warp
   static constexpr uint32_t idesc = idesc_i8(kBM * pair, kBN);
 };
 
-template <bool kPair, bool kDual = false>
+template <bool kPair, bool kDual = false, bool kRot = false>
 struct SmemLayout {
-  using S = Shape<kPair, kDual>;
+  using S = Shape<kPair, kDual, kRot>;
   // offsets from the 1024-aligned base
   static constexpr int a = 0;
   static constexpr int b = S::stages * kATileBytes;                 // stage s: dual_n B tiles
@@ -144,6 +147,7 @@ struct SmemLayout {
 static_assert(SmemLayout<true>::dynamic_bytes <= 227 * 1024, "pair layout exceeds shared memory");
 static_assert(SmemLayout<false>::dynamic_bytes <= 227 * 1024, "single layout exceeds shared memory");
 static_assert(SmemLayout<true, true>::dynamic_bytes <= 227 * 1024, "dual layout exceeds shared memory");
+static_assert(SmemLayout<true, false, true>::dynamic_bytes <= 227 * 1024, "rotating layout exceeds shared memory");
 
 struct GemmParams {
   const float* xs;
@@ -569,8 +573,8 @@ template <int kEpi, bool kPair, bool kDual = false>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
-  using S = Shape<kPair, kDual>;
-  using L = SmemLayout<kPair, kDual>;
+  using S = Shape<kPair, kDual, kEpi == kEpiGeluRot>;
+  using L = SmemLayout<kPair, kDual, kEpi == kEpiGeluRot>;
   constexpr uint32_t kTemptyCount = (kPair ? 2 : 1) * kEpilogueWarps;   // each epilogue warp of each CTA releases
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1276,7 +1280,7 @@ int* status_ptr() {
 template <int kEpi, bool kPair, bool kDual = false>
 cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, GemmParams p,
                         cudaStream_t stream) {
-  using L = SmemLayout<kPair, kDual>;
+  using L = SmemLayout<kPair, kDual, kEpi == kEpiGeluRot>;
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;

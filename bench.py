@@ -440,7 +440,10 @@ def run_ours(args):
                      "int8_mma_probe_tops": i8["probe_tops"], "frac_of_burst": achieved / i8["burst"],
                      "per_gemm": {k: {"tops": round(gemm_ops[k] / (v["avg_ms"] / 1e3) / 1e12, 1),
                                       "frac": round(gemm_ops[k] / (v["avg_ms"] / 1e3) / 1e12 / int8_peak, 4)}
-                                  for k, v in gemms.items()}},
+                                  for k, v in gemms.items()},
+                     "fc1_epilogue": ("GELU and the FC2-input quantiser's ConvRot256 (h3_int8_gelu_rot); the launch "
+                                      "also does that rotation, so its TOPS counts the GEMM's ops over the "
+                                      "combined time" if not SWIGLU else "dequant (SwiGLU in the FC2-input quantiser)")},
         "roofline_prologue": prologue_line,
         "kernels": {k: {"launches": v["launches"], "avg_ms": round(v["avg_ms"], 4),
                         "share": round(v["total_ms"] / step_total, 4)} for k, v in per_kernel.items()},

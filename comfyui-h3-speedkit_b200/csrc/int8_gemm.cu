@@ -11,7 +11,9 @@
 //               each smem stage and publishes each finished accumulator.
 //   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column half
 //               (w - 2) / 4, 32 columns per tcgen05.ld; dequantise, apply the
-//               fused epilogue (bias, GELU, gate-residual, raw int32) and store.
+//               fused epilogue (bias, GELU, gate-residual, raw int32, the QKV
+//               head epilogue, or GELU followed by the FC2-input quantiser's
+//               ConvRot256 of the tile's 256-column group) and store.
 //               The second accumulator lets the epilogue of tile t overlap the
 //               mainloop of tile t+1 (in the dual form a unit's two tiles use
 //               both accumulators and the epilogue does not overlap).

@@ -98,6 +98,30 @@ def test_convrot_act_rejects_before_launch():
     assert lib.h3_convrot_quant_act(8, 4096, 16, 16, 4, 4096, 0, 0) == INVALID         # 16-byte x
 
 
+def test_fc1_rotation_entry_points_reject_before_launch():
+    """h3_int8_gelu_rot and h3_convrot_codes check their operands before any CUDA
+    call (and before the row maxima are reset)."""
+    lib = _lib.load()
+    #                       A   B   xs  ws  bias  V  rowmax  M    N    K    ldv
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, None, 128, 256, 128, 256, 0) == 0    # no rowmax
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 18, 128, 256, 128, 256, 0) == 0      # rowmax % 4
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 16, 128, 264, 128, 264, 0) == 0      # N % 256
+    assert b"256" in lib.h3_int8_error()
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 16, 128, 256, 100, 256, 0) == 0      # K % 16
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 8, 16, 128, 256, 128, 256, 0) == 0       # 16-byte V
+    assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 16, 128, 256, 128, 200, 0) == 0      # ldv < N
+    #                       v   vs    rowmax q   scale rows k
+    assert lib.h3_convrot_codes(16, 4096, 16, 16, 16, 4, 4000, 0) == INVALID    # k % 256
+    assert lib.h3_convrot_codes(16, 4096, 16, 16, 16, 4, 32768, 0) == INVALID   # k > 16384
+    assert lib.h3_convrot_codes(16, 4000, 16, 16, 16, 4, 4096, 0) == INVALID    # vs < k
+    assert lib.h3_convrot_codes(16, 4100, 16, 16, 16, 4, 4096, 0) == INVALID    # vs % 8
+    assert lib.h3_convrot_codes(8, 4096, 16, 16, 16, 4, 4096, 0) == INVALID     # 16-byte v
+    assert lib.h3_convrot_codes(16, 4096, 16, 8, 16, 4, 4096, 0) == INVALID     # 16-byte q
+    assert lib.h3_convrot_codes(16, 4096, 18, 16, 16, 4, 4096, 0) == INVALID    # rowmax % 4
+    assert lib.h3_convrot_codes(16, 4096, None, 16, 16, 4, 4096, 0) == INVALID  # no rowmax
+    assert lib.h3_convrot_codes(16, 4096, 16, 16, 16, 0, 4096, 0) == INVALID    # rows < 1
+
+
 def test_gemm_returns_zero_with_a_reason():
     lib = _lib.load()
     # K % 16 != 0

@@ -101,7 +101,18 @@ constexpr int64_t kBSliceBytes = int64_t(H3SK_BSLICE_MB) << 20;
 constexpr int64_t kDualBSliceBytes = int64_t(H3SK_DUAL_BSLICE_MB) << 20;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s per wait
 
-enum : int { kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads = 4, kEpiGeluRot = 5, kEpiKinds = 6 };
+enum : int {
+  kEpiDequant = 0, kEpiGelu = 1, kEpiGate = 2, kEpiAcc = 3, kEpiHeads = 4,
+  kEpiGeluRot = 5,      // GELU, then the next quantiser's ConvRot256 of every tile
+  kEpiDequantRot = 6,   // dequant, and ConvRot256 of the tiles from column rot_n0 on
+  kEpiKinds = 7
+};
+// Epilogues that rotate 256-column tiles for the next quantiser, and the plain
+// epilogue they apply first.
+__host__ __device__ constexpr bool is_rot(int epi) { return epi == kEpiGeluRot || epi == kEpiDequantRot; }
+__host__ __device__ constexpr int base_epi(int epi) {
+  return epi == kEpiGeluRot ? kEpiGelu : (epi == kEpiDequantRot ? kEpiDequant : epi);
+}
 
 // Tile geometry of the two kernel shapes.
 //   single CTA: a 128 x 256 tile per CTA, B tile 256 rows, 4 stages of 48 KB;
@@ -169,7 +180,8 @@ struct GemmParams {
   int group_n;                    // N units per weight-stationary group
   int head_major;                 // 1: D is [N/128, M, 128] (one plane per 128 columns)
   HeadsArgs hd;                   // kEpiHeads only
-  uint32_t* rowmax;               // kEpiGeluRot only: [M] bits of max |rotated value|, zeroed by the host
+  uint32_t* rowmax;               // rotating kinds: [M] bits of max |rotated value|, zeroed by the host
+  int rot_n0;                     // rotating kinds: first rotated column (tiles from here on rotate)
   int* status;
   uint64_t timeout_ns;
 };
@@ -575,8 +587,8 @@ template <int kEpi, bool kPair, bool kDual = false>
 __global__ void __launch_bounds__(kThreads, 1)
     int8_gemm_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const __grid_constant__ CUtensorMap map_d, const GemmParams p) {
-  using S = Shape<kPair, kDual, kEpi == kEpiGeluRot>;
-  using L = SmemLayout<kPair, kDual, kEpi == kEpiGeluRot>;
+  using S = Shape<kPair, kDual, is_rot(kEpi)>;
+  using L = SmemLayout<kPair, kDual, is_rot(kEpi)>;
   constexpr uint32_t kTemptyCount = (kPair ? 2 : 1) * kEpilogueWarps;   // each epilogue warp of each CTA releases
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -854,7 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row_ok && col0 < p.n) store_chunk_acc(p, r, row, col0);
         } else if (col0 < p.n && row_base < p.m) {
           uint32_t packed[16];
-          chunk_values<kEpi>(p, r, row_ok, row, col0, c, xs_row, gate_row, col_ws, col_bias, packed);
+          chunk_values<base_epi(kEpi)>(p, r, row_ok, row, col0, c, xs_row, gate_row, col_ws, col_bias, packed);
           store_chunk(col0, packed);
         }
       };
@@ -977,105 +989,120 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   codes4_rni(v[16 * q + 12], v[16 * q + 13], v[16 * q + 14], v[16 * q + 15], inv));
           }
         }
-      } else if constexpr (kEpi == kEpiGeluRot) {
-        // ---- FC1 + GELU + the FC2-input quantiser's ConvRot256 ----
-        // The tile's 256 columns are one rotation group of each of its rows; the
-        // two warps of a lane quarter take the two column halves of its 32 rows.
-        // (Four warps per quarter, 18 per CTA, measured slower: 5.9 vs 5.5 ms.)
-        constexpr int kBlocks = 2;                  // 64-column blocks per warp in pass 1
-        constexpr int kRuns = 2;                    // 16-position runs per warp in pass 2
-        const int slice = half;
-        // Pass 1: this warp's 64-column blocks: the GELU values rounded to BF16
-        // (as the unfused FC1 stores them), widened, the stages over index bits
-        // (0,1), (2,3), (4,5), written back over the accumulator columns as FP32.
+      } else if constexpr (is_rot(kEpi)) {
+        if (n0 < p.rot_n0) {
+          // a tile before the rotated columns: the plain epilogue
 #pragma unroll 1
-        for (int b = 0; b < kBlocks; ++b) {
-          const int blk = kBlocks * slice + b;
-          uint64_t v[32];
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int c = 2 * blk + cc;
+          for (int c = c_first; c <= c_last; ++c) {
             uint32_t r[32];
             __syncwarp();
             tmem_load_32cols(t_row + uint32_t(c * 32), r);
             tmem_load_wait();
-            // Without a bias the + 0 is left out: it only turns -0 into +0, and
-            // the sign of a zero reaches neither a code nor the row maximum.
-            uint32_t packed[16];
-            if (p.bias != nullptr)
-              chunk_values<kEpiGelu, true>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws, col_bias,
-                                           packed);
-            else
-              chunk_values<kEpiGelu, false>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws, col_bias,
-                                            packed);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[16 * cc + i] = p2_from_bf2(packed[i]);
+            if (c == c_last) release();
+            emit(c, r);
           }
-          rot_stage01(v);
-          rot_stage_pairs<2>(v);
-          rot_stage_pairs<8>(v);
+        } else {
+          // ---- the epilogue (GELU for FC1, dequant for the QKV V tiles) + the next
+          // quantiser's ConvRot256 ----
+          // The tile's 256 columns are one rotation group of each of its rows; the
+          // two warps of a lane quarter take the two column halves of its 32 rows.
+          // (Four warps per quarter, 18 per CTA, measured slower: 5.9 vs 5.5 ms.)
+          constexpr int kBlocks = 2;                  // 64-column blocks per warp in pass 1
+          constexpr int kRuns = 2;                    // 16-position runs per warp in pass 2
+          const int slice = half;
+          // Pass 1: this warp's 64-column blocks: the epilogue's values rounded to
+          // BF16 (as the unfused GEMM stores them), widened, the stages over index
+          // bits (0,1), (2,3), (4,5), written back over the accumulator columns as
+          // FP32.
+#pragma unroll 1
+          for (int b = 0; b < kBlocks; ++b) {
+            const int blk = kBlocks * slice + b;
+            uint64_t v[32];
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            uint32_t w[32];
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = 2 * blk + cc;
+              uint32_t r[32];
+              __syncwarp();
+              tmem_load_32cols(t_row + uint32_t(c * 32), r);
+              tmem_load_wait();
+              // Without a bias the + 0 is left out: it only turns -0 into +0, and
+              // the sign of a zero reaches neither a code nor the row maximum.
+              uint32_t packed[16];
+              if (p.bias != nullptr)
+                chunk_values<base_epi(kEpi), true>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws,
+                                                   col_bias, packed);
+              else
+                chunk_values<base_epi(kEpi), false>(p, r, row_ok, row, n0 + c * 32, c, xs_row, nullptr, col_ws,
+                                                    col_bias, packed);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w[2 * i] = uint32_t(v[16 * cc + i]);
-              w[2 * i + 1] = uint32_t(v[16 * cc + i] >> 32);
+              for (int i = 0; i < 16; ++i) v[16 * cc + i] = p2_from_bf2(packed[i]);
             }
-            __syncwarp();
-            tmem_store_32cols(t_row + uint32_t((2 * blk + cc) * 32), w);
+            rot_stage01(v);
+            rot_stage_pairs<2>(v);
+            rot_stage_pairs<8>(v);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              uint32_t w[32];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                w[2 * i] = uint32_t(v[16 * cc + i]);
+                w[2 * i + 1] = uint32_t(v[16 * cc + i] >> 32);
+              }
+              __syncwarp();
+              tmem_store_32cols(t_row + uint32_t((2 * blk + cc) * 32), w);
+            }
           }
-        }
-        tmem_store_wait();
-        tc_fence_before();
-        quarter_sync(quarter);   // both column halves of these 32 rows are in TMEM
-        tc_fence_after();
-        // Pass 2: the stage over index bits (6,7) for this warp's positions c of
-        // each 64-column block: the four values c + 64 k.
-        // The outputs of positions [32 half, 32 half + 32) of block k are one
-        // 32-column chunk: the first run's words wait in registers for the second.
-        float mx = 0.0f;
-        uint32_t first[4][8];
+          tmem_store_wait();
+          tc_fence_before();
+          quarter_sync(quarter);   // both column halves of these 32 rows are in TMEM
+          tc_fence_after();
+          // Pass 2: the stage over index bits (6,7) for this warp's positions c of
+          // each 64-column block: the four values c + 64 k.
+          // The outputs of positions [32 half, 32 half + 32) of block k are one
+          // 32-column chunk: the first run's words wait in registers for the second.
+          float mx = 0.0f;
+          uint32_t first[4][8];
 #pragma unroll
-        for (int cc = 0; cc < kRuns; ++cc) {
-          const int c0 = 16 * (kRuns * slice + cc);
-          uint64_t v[32];   // pair 8 k + i: positions c0 + 64 k + 2 i, + 1
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint32_t u[16];
-            __syncwarp();
-            tmem_load_16cols(t_row + uint32_t(c0 + 64 * k), u);
-            tmem_load_wait();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[8 * k + i] = p2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
-          }
-          if (cc == kRuns - 1) release();   // every TMEM read of this accumulator is done
-          rot_stage_pairs<8>(v);
-#pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p2_lo(v[i])), fabsf(p2_hi(v[i]))),
-                                 fmaxf(fabsf(p2_lo(v[i + 1])), fabsf(p2_hi(v[i + 1])))));
-          if (cc == 0) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) first[k][i] = pack_bf2(v[8 * k + i]);
-          } else if (row_base < p.m) {
+          for (int cc = 0; cc < kRuns; ++cc) {
+            const int c0 = 16 * (kRuns * slice + cc);
+            uint64_t v[32];   // pair 8 k + i: positions c0 + 64 k + 2 i, + 1
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              uint32_t packed[16];
+              uint32_t u[16];
+              __syncwarp();
+              tmem_load_16cols(t_row + uint32_t(c0 + 64 * k), u);
+              tmem_load_wait();
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                packed[i] = first[k][i];
-                packed[8 + i] = pack_bf2(v[8 * k + i]);
+              for (int i = 0; i < 8; ++i) v[8 * k + i] = p2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+            }
+            if (cc == kRuns - 1) release();   // every TMEM read of this accumulator is done
+            rot_stage_pairs<8>(v);
+#pragma unroll
+            for (int i = 0; i < 32; i += 2)
+              mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p2_lo(v[i])), fabsf(p2_hi(v[i]))),
+                                   fmaxf(fabsf(p2_lo(v[i + 1])), fabsf(p2_hi(v[i + 1])))));
+            if (cc == 0) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) first[k][i] = pack_bf2(v[8 * k + i]);
+            } else if (row_base < p.m) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  packed[i] = first[k][i];
+                  packed[8 + i] = pack_bf2(v[8 * k + i]);
+                }
+                store_chunk(n0 + 32 * slice + 64 * k, packed);
               }
-              store_chunk(n0 + 32 * slice + 64 * k, packed);
             }
           }
+          // max |rotated value| of the row: non-negative and never NaN (fmaxf drops
+          // NaN), so its bits order as unsigned integers
+          if (row_ok) atomicMax(p.rowmax + row, __float_as_uint(mx));
         }
-        // max |rotated value| of the row: non-negative and never NaN (fmaxf drops
-        // NaN), so its bits order as unsigned integers
-        if (row_ok) atomicMax(p.rowmax + row, __float_as_uint(mx));
       } else if constexpr (H3SK_TMEM_PREFETCH == 1 || (H3SK_TMEM_PREFETCH == 2 && kDual)) {
         // chunk c + 1's TMEM load is in flight while chunk c is computed
         uint32_t r[32];
@@ -1282,7 +1309,7 @@ int* status_ptr() {
 template <int kEpi, bool kPair, bool kDual = false>
 cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, GemmParams p,
                         cudaStream_t stream) {
-  using L = SmemLayout<kPair, kDual, kEpi == kEpiGeluRot>;
+  using L = SmemLayout<kPair, kDual, is_rot(kEpi)>;
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
@@ -1330,7 +1357,7 @@ cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
              void* D, int64_t ldd, const void* gate, const int32_t* rows, const void* residual, int M, int N,
              int K, cudaStream_t stream, bool heads = false, const HeadsArgs* hd = nullptr,
-             uint32_t* rowmax = nullptr) {
+             uint32_t* rowmax = nullptr, int rot_n0 = 0) {
   if (!A || !B || !D || M < 1 || N < 1 || K < 16 || K % 16 || N % 8 || ldd < N || ldd % 8)
     return fail(cudaErrorInvalidValue, "h3_int8: invalid shape or null operand");
   if (heads && ((epi != kEpiDequant && epi != kEpiHeads) || N % 128))
@@ -1338,8 +1365,9 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   if (epi == kEpiHeads && (!heads || !hd || hd->heads < 2 || hd->heads % 2 || N != 3 * hd->heads * 128 ||
                            !hd->freqs || !hd->qw || !hd->kw))
     return fail(cudaErrorInvalidValue, "h3_qkv: the fused head epilogue needs an even head count and N = 3*heads*128");
-  if (epi == kEpiGeluRot && (heads || !rowmax || (uintptr_t(rowmax) & 3u) || N % kBN))
-    return fail(cudaErrorInvalidValue, "h3_int8_gelu_rot: needs rowmax and N % 256 == 0");
+  if (is_rot(epi) && (heads || !rowmax || (uintptr_t(rowmax) & 3u) || N % kBN || rot_n0 < 0 || rot_n0 >= N ||
+                      rot_n0 % kBN))
+    return fail(cudaErrorInvalidValue, "h3_int8_rot: needs rowmax, N % 256 == 0 and rot_n0 % 256 == 0 below N");
   if ((uintptr_t(A) & 15u) || (uintptr_t(B) & 15u) || (uintptr_t(D) & 15u))
     return fail(cudaErrorInvalidValue, "h3_int8: A, B and D must be 16-byte aligned");
   if (epi != kEpiAcc && (!xs || !ws || (uintptr_t(xs) & 3u) || (uintptr_t(ws) & 3u)))
@@ -1376,6 +1404,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   p.head_major = heads ? 1 : 0;
   if (hd) p.hd = *hd;
   p.rowmax = rowmax;
+  p.rot_n0 = rot_n0;
   p.m_tiles = (M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM);
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
@@ -1386,7 +1415,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return fail(cudaErrorInvalidDevice, "h3_int8: no device");
   const int approx_pairs = device_info(device).sms / 2;
-  const bool dual = pair && epi != kEpiHeads && epi != kEpiGeluRot && K >= kDualMinK && p.n_tiles % 2 == 0 &&
+  const bool dual = pair && epi != kEpiHeads && !is_rot(epi) && K >= kDualMinK && p.n_tiles % 2 == 0 &&
                     int64_t(p.m_tiles) * (p.n_tiles / 2) >= int64_t(kDualMinWaves) * approx_pairs;
   const int dual_n = dual ? 2 : 1;
   p.n_units = p.n_tiles / dual_n;
@@ -1398,7 +1427,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
   }
   p.timeout_ns = kWaitTimeoutNs;
   cudaError_t e;
-  if (epi == kEpiGeluRot) {   // the row maxima accumulate from zero (after every check above)
+  if (is_rot(epi)) {   // the row maxima accumulate from zero (after every check above)
     e = cudaMemsetAsync(rowmax, 0, size_t(M) * sizeof(uint32_t), stream);
     if (e != cudaSuccess) return fail(e, "h3_int8_gelu_rot: row maxima reset failed");
   }
@@ -1416,6 +1445,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiGate: e = launch_gemm<kEpiGate, true>(ma, mb, md, p, stream); break;
       case kEpiHeads: e = launch_gemm<kEpiHeads, true>(ma, mb, md, p, stream); break;
       case kEpiGeluRot: e = launch_gemm<kEpiGeluRot, true>(ma, mb, md, p, stream); break;
+      case kEpiDequantRot: e = launch_gemm<kEpiDequantRot, true>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, true>(ma, mb, md, p, stream); break;
     }
   } else {
@@ -1425,6 +1455,7 @@ int run_gemm(int epi, const int8_t* A, const int8_t* B, const float* xs, const f
       case kEpiGate: e = launch_gemm<kEpiGate, false>(ma, mb, md, p, stream); break;
       case kEpiHeads: e = launch_gemm<kEpiHeads, false>(ma, mb, md, p, stream); break;
       case kEpiGeluRot: e = launch_gemm<kEpiGeluRot, false>(ma, mb, md, p, stream); break;
+      case kEpiDequantRot: e = launch_gemm<kEpiDequantRot, false>(ma, mb, md, p, stream); break;
       default: e = launch_gemm<kEpiAcc, false>(ma, mb, md, p, stream); break;
     }
   }
@@ -1489,6 +1520,15 @@ H3SK_EXPORT int h3_int8_gelu_rot(const int8_t* A, const int8_t* B, const float* 
                                  uintptr_t stream) {
   return h3sk::run_gemm(h3sk::kEpiGeluRot, A, B, xs, ws, bias, V, ldv, nullptr, nullptr, nullptr, M, N, K,
                         reinterpret_cast<cudaStream_t>(stream), false, nullptr, static_cast<uint32_t*>(rowmax));
+}
+
+H3SK_EXPORT int h3_int8_rot(const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
+                            void* D, void* rowmax, int M, int N, int K, int64_t ldd, int gelu, int rot_n0,
+                            uintptr_t stream) {
+  if (gelu != 0 && gelu != 1) return h3sk::fail(cudaErrorInvalidValue, "h3_int8_rot: gelu is 0 or 1");
+  return h3sk::run_gemm(gelu ? h3sk::kEpiGeluRot : h3sk::kEpiDequantRot, A, B, xs, ws, bias, D, ldd, nullptr,
+                        nullptr, nullptr, M, N, K, reinterpret_cast<cudaStream_t>(stream), false, nullptr,
+                        static_cast<uint32_t*>(rowmax), rot_n0);
 }
 
 H3SK_EXPORT int h3_int8_gate_ex(const int8_t* A, const int8_t* B, const float* xs, const float* ws,

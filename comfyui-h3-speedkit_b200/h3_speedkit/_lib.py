@@ -46,6 +46,7 @@ EXPORTS = {
     "h3_int8_ex": ([_P] * 6 + [_I] * 3 + [_I64, _I, _SZ], _I),
     "h3_int8_gate_ex": ([_P] * 11 + [_I] * 3 + [_SZ], _I),
     "h3_int8_gelu_rot": ([_P] * 7 + [_I] * 3 + [_I64, _SZ], _I),
+    "h3_int8_rot": ([_P] * 7 + [_I] * 3 + [_I64, _I, _I, _SZ], _I),
     "h3_int8_last_error": ([], _I),
     "h3_int8_error": ([], ct.c_char_p),
     "h3_qkv_quant_kv": ([_P] * 8 + [_F] + [_P] * 7 + [_I, _SZ], _I),

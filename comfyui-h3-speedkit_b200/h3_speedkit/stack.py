@@ -10,8 +10,11 @@ SpeedKit, with attention replaced by an identity passthrough of V):
     q, qs   = prologue(x; norm2, shift_mlp, scale_mlp)
     h       = bf(gelu_tanh(bf(dequant(q . Wfc1^T))))            FC1 + GELU epilogue
     hq, hs  = convrot_quant(h)                                  ACT none (GELU already applied)
-              (run as FC1 whose epilogue also rotates each 256-column group of h,
-              then a codes pass over the rotated rows: the same hq, hs bit for bit)
+
+Both quantisers after a GEMM run split: the GEMM's epilogue also rotates each
+256-column group it feeds to the quantiser (all of h; the V third of qkv) and
+keeps each row's max |rotated value|, then a codes pass over the rotated rows
+writes the same codes and scales bit for bit.
     x       = bf(fmaf(bf(dequant(hq . Wfc2^T)), gate_mlp, x))   FC2 gate-residual, in place
 
 Every op is row-local, so a contiguous token shard gives bit-identical rows on
@@ -215,7 +218,8 @@ class Workspace:
     h: torch.Tensor
     hq: torch.Tensor
     hs: torch.Tensor
-    hmax: torch.Tensor   # int32 [m]: FP32 bits of each row's max |rotated h| (fused FC1 rotation)
+    hmax: torch.Tensor   # int32 [m]: FP32 bits of each row's max |rotated h| (rotation in FC1's epilogue)
+    vmax: torch.Tensor   # int32 [m]: the same for the rotated V third of qkv (rotation in the QKV epilogue)
 
     @classmethod
     def allocate(cls, m: int, d: int, ffn: int, device, *, attn: int | None = None,
@@ -229,7 +233,7 @@ class Workspace:
                    as_=torch.empty((m, 1), dtype=torch.float32, **e),
                    h=torch.empty((m, fc1_n), dtype=torch.bfloat16, **e),
                    hq=torch.empty((m, ffn), dtype=torch.int8, **e), hs=torch.empty((m, 1), dtype=torch.float32, **e),
-                   hmax=torch.empty((m,), dtype=torch.int32, **e))
+                   hmax=torch.empty((m,), dtype=torch.int32, **e), vmax=torch.empty((m,), dtype=torch.int32, **e))
 
     @classmethod
     def for_block(cls, m: int, weights: BlockWeights, device) -> "Workspace":
@@ -262,16 +266,17 @@ class BlockPlan:
     at ``skip``: their rows below it feed nothing.  Nothing is allocated when
     the plan runs.
 
-    ``fc1_rotation`` (GELU blocks): FC1's epilogue also runs the FC2-input
-    quantiser's ConvRot256 on each 256-column group and keeps each row's max
-    |rotated value| (``h3_int8_gelu_rot``); a light pass then writes the codes
-    and scales (``h3_convrot_codes``).  Same hq, hs bit for bit as FC1 followed
-    by the quantiser (False), and faster (the rotation runs in the GEMM's
-    epilogue warps while the tensor cores work).
+    ``epilogue_rotation``: the QKV GEMM's epilogue runs the V quantiser's
+    ConvRot256 on the V third and, in GELU blocks, FC1's epilogue runs the
+    FC2-input quantiser's on all of h, each keeping the rows' max |rotated value|
+    (``h3_int8_rot``); a light pass then writes the codes and scales
+    (``h3_convrot_codes``).  Same aq, as, hq, hs bit for bit as the GEMMs
+    followed by the full quantisers (False), and faster: the rotations run in
+    the GEMMs' epilogue warps while the tensor cores work.
     """
 
     def __init__(self, weights: BlockWeights, x: torch.Tensor, rows: torch.Tensor, ws: Workspace,
-                 eps: float = 1e-6, skip: int = 0, fc1_rotation: bool = True):
+                 eps: float = 1e-6, skip: int = 0, epilogue_rotation: bool = True):
         self.lib = _lib.load()
         m, d = x.shape
         g = geometry(weights)
@@ -301,13 +306,23 @@ class BlockPlan:
              (P(x), P(w.norm1), P(w.shift_msa), P(w.scale_msa), P(rows), P(ws.q), P(ws.qs), None, None, None,
               m, d, w.shift_msa.shape[0], x.stride(0), w.shift_msa.stride(0), w.scale_msa.stride(0), float(eps),
               tdt, 0)),
-            ("qkv", lib.h3_int8_ex,
-             (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * attn, d, 3 * attn, EPI_DEQUANT)),
         ]
+        # qkv's V third (columns [2 attn, 3 attn)), the identity attention's output
+        if epilogue_rotation:
+            calls.append(("qkv", lib.h3_int8_rot,
+                          (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), P(ws.vmax), m, 3 * attn, d,
+                           3 * attn, 0, 2 * attn)))
+            quant_v = ("quant_v", lib.h3_convrot_codes,
+                       (P(ws.qkv, s) + 2 * attn * 2, 3 * attn, P(ws.vmax, s), P(ws.aq, s), P(ws.as_, s), n, attn))
+        else:
+            calls.append(("qkv", lib.h3_int8_ex,
+                          (P(ws.q), P(w.qkv), P(ws.qs), P(w.qkv_s), None, P(ws.qkv), m, 3 * attn, d, 3 * attn,
+                           EPI_DEQUANT)))
+            quant_v = ("quant_v", lib.h3_convrot_quant_act,
+                       (P(ws.qkv, s) + 2 * attn * 2, 3 * attn, P(ws.aq, s), P(ws.as_, s), n, attn, ACT_NONE))
         if n:
             calls += [
-                ("quant_v", lib.h3_convrot_quant_act,
-                 (P(ws.qkv, s) + 2 * attn * 2, 3 * attn, P(ws.aq, s), P(ws.as_, s), n, attn, ACT_NONE)),
+                quant_v,
                 ("outproj", lib.h3_int8_gate,
                  (P(ws.aq, s), P(w.out), P(ws.as_, s), P(w.out_s), P(x, s), P(w.gate_msa), P(rows, s), P(x, s), n, d,
                   attn, 13)),
@@ -316,7 +331,7 @@ class BlockPlan:
                   None, None, n, d, w.shift_mlp.shape[0], x.stride(0), w.shift_mlp.stride(0),
                   w.scale_mlp.stride(0), float(eps), tdt, 0)),
             ]
-            if fc1_rotation and not g["swiglu"]:
+            if epilogue_rotation and not g["swiglu"]:
                 calls += [
                     ("fc1", lib.h3_int8_gelu_rot,
                      (P(ws.q, s), P(w.fc1), P(ws.qs, s), P(w.fc1_s), None, P(ws.h, s), P(ws.hmax, s), n, n1, d,
@@ -372,9 +387,9 @@ class LocalStack:
     """All blocks over one contiguous shard of tokens, on the current device."""
 
     def __init__(self, blocks: list[BlockWeights], x: torch.Tensor, rows: torch.Tensor, eps: float = 1e-6,
-                 ws: Workspace | None = None, skip: int = 0, fc1_rotation: bool = True):
+                 ws: Workspace | None = None, skip: int = 0, epilogue_rotation: bool = True):
         """``skip``: the last block's row window (rows [0, skip) of this shard keep
-        the residual the previous blocks left; see BlockPlan).  ``fc1_rotation``:
+        the residual the previous blocks left; see BlockPlan).  ``epilogue_rotation``:
         see BlockPlan."""
         m, d = x.shape
         self.x, self.rows = x, rows
@@ -382,7 +397,7 @@ class LocalStack:
             raise ValueError("shared workspace too small for this shard")
         self.ws = ws if ws is not None else Workspace.for_block(m, blocks[0], x.device)
         self.plans = [BlockPlan(b, x, rows, self.ws, eps, skip=skip if i == len(blocks) - 1 else 0,
-                                fc1_rotation=fc1_rotation)
+                                epilogue_rotation=epilogue_rotation)
                       for i, b in enumerate(blocks)]
         self.graph = None
 

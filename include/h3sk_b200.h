@@ -251,6 +251,19 @@ int h3_int8_gate_ex(const int8_t* A, const int8_t* B, const float* xs, const flo
 int h3_int8_gelu_rot(const int8_t* A, const int8_t* B, const float* xs, const float* ws,
                      const void* bias, void* V, void* rowmax, int M, int N, int K, int64_t ldv,
                      uintptr_t stream);
+/*
+ * The same with the plain dequant epilogue when gelu == 0, and the rotation
+ * limited to the columns [rot_n0, N) (rot_n0 % 256 == 0): D holds the plain
+ * epilogue's BF16 values below rot_n0 and the rotated values from it on, and
+ * rowmax the rows' max |rotated value| over those columns.  With gelu == 0 and
+ * rot_n0 = 2N/3 this is the QKV projection whose V third feeds the next
+ * quantiser: h3_convrot_codes(D + rot_n0, ldd, rowmax, q, scale, M, N - rot_n0)
+ * then equals h3_convrot_quant_act(D_plain + rot_n0, ldd, ...) bit for bit.
+ * gelu == 1, rot_n0 == 0 is h3_int8_gelu_rot.  Returns 1 / 0.
+ */
+int h3_int8_rot(const int8_t* A, const int8_t* B, const float* xs, const float* ws, const void* bias,
+                void* D, void* rowmax, int M, int N, int K, int64_t ldd, int gelu, int rot_n0,
+                uintptr_t stream);
 /* cudaError_t-style code of the last failed h3_int8* call on this host thread
  * (0 if the last call succeeded; cudaErrorInvalidValue for a rejected argument). */
 int h3_int8_last_error(void);

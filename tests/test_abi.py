@@ -98,7 +98,7 @@ def test_convrot_act_rejects_before_launch():
     assert lib.h3_convrot_quant_act(8, 4096, 16, 16, 4, 4096, 0, 0) == INVALID         # 16-byte x
 
 
-def test_fc1_rotation_entry_points_reject_before_launch():
+def test_rotating_gemm_and_codes_entry_points_reject_before_launch():
     """h3_int8_gelu_rot and h3_convrot_codes check their operands before any CUDA
     call (and before the row maxima are reset)."""
     lib = _lib.load()
@@ -110,6 +110,11 @@ def test_fc1_rotation_entry_points_reject_before_launch():
     assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 16, 128, 256, 100, 256, 0) == 0      # K % 16
     assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 8, 16, 128, 256, 128, 256, 0) == 0       # 16-byte V
     assert lib.h3_int8_gelu_rot(16, 16, 16, 16, None, 16, 16, 128, 256, 128, 200, 0) == 0      # ldv < N
+    #                  A   B   xs  ws  bias D  rowmax M    N    K    ldd  gelu rot_n0
+    assert lib.h3_int8_rot(16, 16, 16, 16, None, 16, 16, 128, 768, 128, 768, 0, 100, 0) == 0   # rot_n0 % 256
+    assert lib.h3_int8_rot(16, 16, 16, 16, None, 16, 16, 128, 768, 128, 768, 0, 768, 0) == 0   # rot_n0 >= N
+    assert lib.h3_int8_rot(16, 16, 16, 16, None, 16, 16, 128, 768, 128, 768, 2, 512, 0) == 0   # gelu 0 / 1
+    assert lib.h3_int8_rot(16, 16, 16, 16, None, 16, None, 128, 768, 128, 768, 0, 512, 0) == 0  # no rowmax
     #                       v   vs    rowmax q   scale rows k
     assert lib.h3_convrot_codes(16, 4096, 16, 16, 16, 4, 4000, 0) == INVALID    # k % 256
     assert lib.h3_convrot_codes(16, 4096, 16, 16, 16, 4, 32768, 0) == INVALID   # k > 16384

@@ -50,6 +50,32 @@ def test_fused_rotation_equals_fc1_then_quantiser(device, m, n, k, use_bias):
     assert _lib.pipeline_status() == 0
 
 
+@pytest.mark.parametrize("m,attn,k", [(300, 1024, 512), (4096, 4096, 4096), (77, 256, 256), (1000, 7168, 1024)])
+def test_qkv_v_rotation_equals_plain_qkv_then_quantiser(device, m, attn, k):
+    """h3_int8_rot with the dequant epilogue and rot_n0 = 2 attn (the QKV
+    projection whose V third feeds the next quantiser): the Q and K columns equal
+    the plain dequant GEMM bit for bit, and the codes pass over the rotated V
+    third gives the quantiser's codes and scales of the plain V third."""
+    n = 3 * attn
+    a, w, xs, ws, _ = _operands(m, n, k, m + attn + k, device)
+    plain = gemm.int8_linear(a, w, xs, ws)
+    q_ref, s_ref = quantize_int8_rowwise_convrot64(plain[:, 2 * attn:])
+    d = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+    vmax = torch.empty((m,), dtype=torch.int32, device=device)
+    q = torch.empty((m, attn), dtype=torch.int8, device=device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=device)
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check_int8(lib.h3_int8_rot(a.data_ptr(), w.data_ptr(), xs.data_ptr(), ws.data_ptr(), None, d.data_ptr(),
+                                    vmax.data_ptr(), m, n, k, n, 0, 2 * attn, st))
+    assert lib.h3_convrot_codes(d[:, 2 * attn:].data_ptr(), n, vmax.data_ptr(), q.data_ptr(), s.data_ptr(), m, attn,
+                                st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(d[:, :2 * attn].view(torch.int16), plain[:, :2 * attn].view(torch.int16))
+    assert torch.equal(s.view(torch.int32), s_ref.view(torch.int32))
+    assert torch.equal(q, q_ref)
+
+
 def test_fused_rotation_overflowing_rows(device):
     """Large activation scales drive some GELU outputs past the BF16 range (inf),
     whose rotations give inf and NaN; scales clamp at BF16_MAX / 127 and the

@@ -165,17 +165,33 @@ def test_last_block_row_window(device, skip):
 
 
 @pytest.mark.parametrize("skip", [0, 300])
-def test_fc1_rotation_plan_equals_unfused_plan(device, skip):
-    """FC1 with the FC2-input quantiser's rotation in its epilogue plus the codes
-    pass (the default plan) against FC1 then the quantiser: the same stack output
-    bit for bit, with and without a last-block row window."""
+def test_epilogue_rotation_plan_equals_unfused_plan(device, skip):
+    """The quantisers' rotations in the GEMM epilogues (the V third in QKV's, all
+    of h in FC1's) plus the codes passes -- the default plan -- against the GEMMs
+    followed by the full quantisers: the same stack output bit for bit, with and
+    without a last-block row window."""
     m = 1000
     blocks = _blocks(2, device)
     x0 = synthetic.cfg5_tokens(m, D).to(device)
     rows = (torch.arange(m, device=device) % 2).to(torch.int32)
     fused, unfused = x0.clone(), x0.clone()
     LocalStack(blocks, fused, rows, skip=skip).run()
-    LocalStack(blocks, unfused, rows, skip=skip, fc1_rotation=False).run()
+    LocalStack(blocks, unfused, rows, skip=skip, epilogue_rotation=False).run()
+    torch.cuda.synchronize()
+    assert torch.equal(fused, unfused)
+
+
+def test_epilogue_rotation_plan_h3_geometry(device):
+    """The H3 geometry (SwiGLU: only the QKV epilogue rotates; the FC2-input
+    quantiser keeps its SwiGLU input activation) gives the same stack output
+    with and without the epilogue rotation."""
+    m = 640
+    blocks = [synthetic.h3_block(i, device=device, tables=2) for i in range(2)]
+    x0 = synthetic.cfg5_tokens(m, blocks[0].norm1.shape[0]).to(device)
+    rows = (torch.arange(m, device=device) % 2).to(torch.int32)
+    fused, unfused = x0.clone(), x0.clone()
+    LocalStack(blocks, fused, rows).run()
+    LocalStack(blocks, unfused, rows, epilogue_rotation=False).run()
     torch.cuda.synchronize()
     assert torch.equal(fused, unfused)
 

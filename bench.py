@@ -443,7 +443,8 @@ def run_ours(args):
                                   for k, v in gemms.items()},
                      "fc1_epilogue": ("GELU and the FC2-input quantiser's ConvRot256 (h3_int8_gelu_rot); the launch "
                                       "also does that rotation, so its TOPS counts the GEMM's ops over the "
-                                      "combined time" if not SWIGLU else "dequant (SwiGLU in the FC2-input quantiser)")},
+                                      "combined time" if not SWIGLU else "dequant (SwiGLU in the FC2-input quantiser)"),
+                     "qkv_epilogue": "dequant, and the V quantiser's ConvRot256 on the V third (h3_int8_rot)"},
         "roofline_prologue": prologue_line,
         "kernels": {k: {"launches": v["launches"], "avg_ms": round(v["avg_ms"], 4),
                         "share": round(v["total_ms"] / step_total, 4)} for k, v in per_kernel.items()},

@@ -12,8 +12,8 @@
 //   warps 2-9   epilogue: warp w reads TMEM lane quarter w % 4 and column half
 //               (w - 2) / 4, 32 columns per tcgen05.ld; dequantise, apply the
 //               fused epilogue (bias, GELU, gate-residual, raw int32, the QKV
-//               head epilogue, or GELU followed by the FC2-input quantiser's
-//               ConvRot256 of the tile's 256-column group) and store.
+//               head epilogue, or the dequant / GELU values followed by the next
+//               quantiser's ConvRot256 of the tile's 256-column group) and store.
 //               The second accumulator lets the epilogue of tile t overlap the
 //               mainloop of tile t+1 (in the dual form a unit's two tiles use
 //               both accumulators and the epilogue does not overlap).
@@ -133,8 +133,8 @@ struct Shape {
   static constexpr int b_rows = kPair ? kBN / 2 : kBN;    // B rows loaded per CTA
   static constexpr int b_tile_bytes = b_rows * kBK;
   static constexpr int stage_bytes = kATileBytes + dual_n * b_tile_bytes;
-  // The rotating FC1 epilogue stores four chunks back to back at the end of a
-  // tile: its CTA pairs trade an operand stage for a second staging buffer.
+  // The rotating epilogues store four chunks back to back at the end of a tile:
+  // their CTA pairs trade an operand stage for a second staging buffer.
   static constexpr int stages =
       kPair ? (kDual ? H3SK_DUAL_STAGES : (kRot ? H3SK_PAIR_STAGES - 1 : H3SK_PAIR_STAGES)) : 4;
   static constexpr int stage_bufs = (kPair && !kDual) ? (kRot ? 2 : H3SK_STAGE_BUFS) : 1;   // output staging buffers per warp

@@ -234,6 +234,44 @@ def test_block_geometry_from_weight_shapes():
         geometry(b)
 
 
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_block_plan_launch_lists(swiglu):
+    """The block plan's launches, bound on CPU tensors (nothing is launched):
+    with epilogue rotation the QKV GEMM rotates its V third (rot_n0 = 2 attn)
+    for the V codes pass, and in GELU blocks FC1 rotates all of h for the FC2
+    codes pass; SwiGLU blocks keep FC1 + the SwiGLU quantiser.  Without it, the
+    GEMMs are followed by the full quantisers."""
+    from h3_speedkit import _lib, synthetic
+    from h3_speedkit.stack import BlockPlan, Workspace
+    d, ffn, attn, m, skip = 512, 512, 768, 384, 128
+    b = synthetic.cfg5_block(0, d, ffn, attn=attn, swiglu=swiglu)
+    x = torch.zeros((m, d), dtype=torch.bfloat16)
+    rows = torch.zeros((m,), dtype=torch.int32)
+    ws = Workspace.for_block(m, b, "cpu")
+    lib = _lib.load()
+    fused = BlockPlan(b, x, rows, ws, skip=skip)
+    names = [(name, fn.__name__) for name, fn, _ in fused.calls]
+    assert names == [("prologue", "h3_norm_quant_run_t"), ("qkv", "h3_int8_rot"),
+                     ("quant_v", "h3_convrot_codes"), ("outproj", "h3_int8_gate"),
+                     ("prologue", "h3_norm_quant_run_t"),
+                     ("fc1", "h3_int8_ex" if swiglu else "h3_int8_gelu_rot"),
+                     ("quant_h", "h3_convrot_quant_act" if swiglu else "h3_convrot_codes"),
+                     ("fc2", "h3_int8_gate")]
+    qkv_args = fused.calls[1][2]
+    assert qkv_args[-2:] == (0, 2 * attn)                 # plain dequant, V third rotated
+    assert qkv_args[6] == ws.vmax.data_ptr()              # row maxima of all m rows
+    quant_v_args = fused.calls[2][2]
+    assert quant_v_args[2] == ws.vmax.data_ptr() + 4 * skip   # the window's rows only
+    assert quant_v_args[5:] == (m - skip, attn)
+    plain = BlockPlan(b, x, rows, ws, skip=skip, epilogue_rotation=False)
+    names = [(name, fn.__name__) for name, fn, _ in plain.calls]
+    assert [n for n, _ in names] == [c[0] for c in fused.calls]
+    assert dict(names)["qkv"] == "h3_int8_ex"
+    assert names[2] == ("quant_v", "h3_convrot_quant_act")
+    assert names[6] == ("quant_h", "h3_convrot_quant_act")
+    assert lib is _lib.load()
+
+
 def test_residual_validate_rejects_before_gpu_work():
     """ops.residual_quant.validate: the reference's metadata checks (residual_quant.py:57-112) on CPU."""
     from h3_speedkit.ops import residual_quant as rq
